@@ -1,0 +1,514 @@
+#!/usr/bin/env python
+"""KV-cache block save/load throughput on B200 (one process per GPU).
+
+Workload (default): Llama-3.1-8B-shaped paged KV, 32 layers
+of KV-first [2, 8192, 16, 8, 128] bf16 ~N(0,1) per GPU; one 10,240-token
+prefix = 640 blocks saved (all layers) to the pinned pool and restored into
+640 other block ids. Seeded synthetic data; block ids seeded-shuffled (or
+sorted with --order sorted). Each rank runs its own copy on its own GPU into
+its own pool (weak scaling; no collective on the data path).
+
+One step = save of the 640 blocks x 32 layers + load of them back.
+  value : payload GB/s (save + load bytes / time) of the transfer executor,
+          device-timed with CUDA events on the calling stream, max over ranks.
+  e2e   : the same through the engine API (PegaEngine.batch_save_kv_blocks +
+          batch_load_kv_blocks + LoadState completion), host wall clock.
+Also reported: save/load split, p50 load ms, host-link peak and fraction, the
+pack/unpack kernel HBM roofline, the reference's own copy strategy timed on the
+same GPU, and a CPU gather/scatter baseline.
+
+--impl reference: the reference's CPU implementation of the path (the oracle
+port of its copies, multi-threaded) on this host's cores; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "KV save/load GB/s per GPU at 1/2/4/8 B200 vs host-link roofline; p50 load ms"
+
+WORKLOADS = {
+    # BASELINE config 1
+    "llama8b": dict(layers=32, num_blocks=8192, heads=8, head_dim=128, block_size=16, blocks=640,
+                    desc="Llama-3.1-8B layer-wise offload: 32 layers, KV-first [2,8192,16,8,128] bf16, 640 blocks"),
+    # BASELINE config 3 at TP=t (t = world size): each rank holds 8/t heads
+    "llama70b_tp": dict(layers=80, num_blocks=4096, heads=8, head_dim=128, block_size=16, blocks=2048, tp=True,
+                        desc="Llama-3-70B TP sharding: 80 layers, [2,4096,16,8/t,128] bf16, 2048 blocks per rank"),
+    # BASELINE config 0 (separate K and V tensors, segments=1)
+    "gpt2": dict(layers=24, num_blocks=256, heads=12, head_dim=64, block_size=16, blocks=64, separate=True,
+                 desc="GPT-2-small: 12 layers x separate K,V [256,16,12,64] fp16, 64 blocks"),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- helpers
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def link_peaks(torch, device: int) -> dict:
+    """Pinned host<->device copy-engine bandwidth with 1 GiB buffers (best of 3)."""
+    n = 1 << 30
+    host = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    dev = torch.empty(n, dtype=torch.uint8, device=device)
+    out = {}
+    s = torch.cuda.Stream(device)
+    for name, fn in (("h2d", lambda: dev.copy_(host, non_blocking=True)),
+                     ("d2h", lambda: host.copy_(dev, non_blocking=True))):
+        best = 0.0
+        with torch.cuda.stream(s):
+            fn()
+            for _ in range(3):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(s)
+                fn()
+                b.record(s)
+                b.synchronize()
+                best = max(best, n / (a.elapsed_time(b) / 1e3) / 1e9)
+        out[name] = round(best, 2)
+    del host, dev
+    return out
+
+
+def make_workload(torch, wl: dict, device: int, rank: int, world: int, order: str):
+    """KV tensors on the GPU plus seeded src/dst block lists."""
+    heads = wl["heads"] // world if wl.get("tp") else wl["heads"]
+    nb, bs, hd = wl["num_blocks"], wl["block_size"], wl["head_dim"]
+    gen = torch.Generator(device=f"cuda:{device}").manual_seed(1000 + rank)
+    tensors = []
+    for _ in range(wl["layers"]):
+        shape = (nb, bs, heads, hd) if wl.get("separate") else (2, nb, bs, heads, hd)
+        dt = torch.float16 if wl.get("separate") else torch.bfloat16
+        tensors.append(torch.randn(shape, generator=gen, device=f"cuda:{device}", dtype=torch.float32).to(dt))
+    cpu_gen = torch.Generator().manual_seed(3 + rank)
+    n = wl["blocks"]
+    if order == "sorted":
+        src = np.arange(n)
+        dst = (np.arange(n) + n) % nb
+    else:
+        src = torch.randperm(nb, generator=cpu_gen)[:n].numpy()
+        dst = torch.randperm(nb, generator=torch.Generator().manual_seed(4 + rank))[:n].numpy()
+    return tensors, src, dst
+
+
+def executor_specs(tensors, src, dst, pool_ptr):
+    from pegaflow_b200 import Layout, LoadSpec, SaveSpec
+
+    saves, loads = [], []
+    off = 0
+    n = len(src)
+    for t in tensors:
+        lay = Layout.from_tensor(t)
+        if lay.split:
+            k, v = pool_ptr + off, pool_ptr + off + n * lay.bytes_per_block
+            unit = lay.bytes_per_block
+            off += 2 * n * unit
+            ks = np.arange(n, dtype=np.uint64) * unit + k
+            saves.append(SaveSpec(lay, src, k, v))
+            loads.append(LoadSpec(lay, dst, ks, ks + (v - k)))
+        else:
+            unit = lay.block_size_bytes
+            k = pool_ptr + off
+            off += n * unit
+            ks = np.arange(n, dtype=np.uint64) * unit + k
+            saves.append(SaveSpec(lay, src, k, None))
+            loads.append(LoadSpec(lay, dst, ks, None))
+        off = (off + 4095) // 4096 * 4096
+    return saves, loads, off
+
+
+def payload_bytes(tensors, n) -> int:
+    from pegaflow_b200 import Layout
+
+    total = 0
+    for t in tensors:
+        lay = Layout.from_tensor(t)
+        total += n * (2 * lay.bytes_per_block if lay.split else lay.block_size_bytes)
+    return total
+
+
+# ----------------------------------------------------------------------------- CPU arms
+
+
+class CpuWorkload:
+    """Oracle port of the reference's copies (multi-threaded memcpy gather and
+    scatter) on host-resident buffers with the workload's layout: a bounded
+    sample of `max_layers` layers with the workload's block lists."""
+
+    def __init__(self, wl: dict, threads: int, max_layers: int = 8):
+        from oracle import oracle
+
+        self.oracle = oracle
+        oracle.build()
+        self.threads = threads
+        L = min(wl["layers"], max_layers)
+        nb, bs, hd, heads = wl["num_blocks"], wl["block_size"], wl["head_dim"], wl["heads"]
+        seg = bs * heads * hd * 2
+        n = wl["blocks"]
+        src = np.random.default_rng(3).permutation(nb)[:n]
+        dst = np.random.default_rng(4).permutation(nb)[:n]
+        self.saves, self.loads = [], []
+        for i in range(L):
+            lay = oracle.Layout(nb * seg, nb, seg, 0, 1) if wl.get("separate") else \
+                oracle.Layout(2 * nb * seg, nb, seg, nb * seg, 2)
+            cache = np.empty(lay.size_bytes, np.uint8)
+            cache[::4096] = i  # fault every page in before timing
+            kp = np.zeros(n * seg, np.uint8)
+            vp = np.zeros(n * seg, np.uint8) if lay.split else None
+            self.saves.append((lay, cache, src, kp, vp))
+            self.loads.append((lay, cache, dst, kp, vp))
+        self.sample = f"{L} of {wl['layers']} layers x {n} blocks (save + load), host-resident buffers"
+
+    def step(self) -> int:
+        moved = self.oracle.mt_transfer(self.saves, True, self.threads)
+        moved += self.oracle.mt_transfer(self.loads, False, self.threads)
+        return moved
+
+    def rate(self, seconds: float) -> dict:
+        self.step()
+        moved, reps = 0, 0
+        t0 = time.perf_counter()
+        while True:
+            moved += self.step()
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        return {"value": round(moved / el / 1e9, 3), "unit": "GB/s", "cores": self.threads, "kind": "port",
+                "sample": f"{self.sample}, {reps} reps in {el:.1f} s"}
+
+
+def run_reference_arm(args, wl) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cw = CpuWorkload(wl, threads)
+    for _ in range(args.warmup):
+        cw.step()
+    times, vals = [], []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        moved = cw.step()
+        el = time.perf_counter() - t0
+        times.append(el * 1e3)
+        vals.append(moved / el / 1e9)
+    value = round(statistics.median(vals), 3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(times), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (host-resident, seeded block lists)", "config": config_block(args, wl),
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": cw.sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference path is Rust over cudarc copies with no CPU implementation and cannot be built "
+                "here (no Rust toolchain); this arm times the oracle port of its copy algorithm on host cores",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(args, wl) -> dict:
+    return {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
+            "blocks_moved": wl["blocks"], "block_ids": args.order, "kv_dtype": "fp16" if wl.get("separate") else "bf16",
+            "save_mode": args.save_mode, "load_mode": args.load_mode,
+            "l2": "inputs larger than L2 (payload >= 36 MiB per layer set; KV cache >> 126 MB)",
+            "parallelism": f"dp{args.gpus} (independent ranks, weak scaling)"}
+
+
+# ----------------------------------------------------------------------------- main arm
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama8b")
+    ap.add_argument("--order", choices=["shuffled", "sorted"], default="shuffled")
+    ap.add_argument("--save-mode", default="auto", choices=["auto", "staged", "direct"])
+    ap.add_argument("--load-mode", default="auto", choices=["auto", "staged", "direct"])
+    ap.add_argument("--chunk-mib", type=int, default=0)
+    ap.add_argument("--slots", type=int, default=0)
+    ap.add_argument("--copy-streams", type=int, default=0)
+    ap.add_argument("--ctas-per-sm", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=0, help="engine-API steps (default: --steps)")
+    ap.add_argument("--no-refcopy", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    args.warmup = max(args.warmup, 0)
+
+    if args.impl == "reference":
+        run_reference_arm(args, wl)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device(f"cuda:{local}"))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def min_over_ranks(x: float) -> float:
+        return -max_over_ranks(-x)
+
+    from pegaflow_b200 import Executor, PegaEngine, PinnedBuffer, PyLoadState, refcopy_load, refcopy_save
+
+    peaks = measured_peaks()
+    link = link_peaks(torch, local)
+    tensors, src, dst = make_workload(torch, wl, local, rank, world, args.order)
+    n = len(src)
+    payload = payload_bytes(tensors, n)
+    torch.cuda.synchronize()
+
+    ex = Executor(local, save_mode=args.save_mode, load_mode=args.load_mode,
+                  staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
+                  copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm)
+    pool = PinnedBuffer(payload + wl["layers"] * 8192 + (1 << 20), write_combined=True)
+    saves, loads, _ = executor_specs(tensors, src, dst, pool.ptr)
+    stream = torch.cuda.Stream(local)
+    sp = stream.cuda_stream
+
+    def step(evs=None):
+        if evs:
+            evs[0].record(stream)
+        ex.save(saves, stream=sp)
+        if evs:
+            evs[1].record(stream)
+        ex.load(loads, stream=sp)
+        if evs:
+            evs[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+
+    ex.reset_stats()
+    ex.set_timing(True)
+    sampler = ClockSampler(local)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    per = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for k in range(args.steps):
+        step(per[k])
+    t_end.record(stream)
+    t_end.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ex.set_timing(False)
+    st = ex.stats()
+    ms = t_start.elapsed_time(t_end)
+    save_ms = [e[0].elapsed_time(e[1]) for e in per]
+    load_ms = [e[1].elapsed_time(e[2]) for e in per]
+    ms_max = max_over_ranks(ms)
+    steps = args.steps
+    value = world * 2 * payload * steps / (ms_max / 1e3) / 1e9
+    save_gbps = min_over_ranks(payload / (statistics.median(save_ms) / 1e3) / 1e9)
+    load_gbps = min_over_ranks(payload / (statistics.median(load_ms) / 1e3) / 1e9)
+    p50_load = max_over_ranks(statistics.median(load_ms))
+    kernel_gbps = st["kernel_bytes"] / (st["kernel_ms"] / 1e3) / 1e9 if st["kernel_ms"] > 0 else None
+
+    # ---- e2e through the engine API (host wall clock) ------------------------
+    e2e_steps = args.e2e_steps or args.steps
+    eng = PegaEngine(2 * payload + (256 << 20), enable_lfu_admission=False,
+                     executor=dict(save_mode=args.save_mode, load_mode=args.load_mode,
+                                   staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
+                                   copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm))
+    names = [f"model.layers.{i}.self_attn" for i in range(len(tensors))]
+    from pegaflow_b200 import Layout
+
+    for nm, t in zip(names, tensors):
+        lay = Layout.from_tensor(t)
+        eng.register_context_layer(f"bench{rank}", "bench", local, nm, lay.data_ptr, lay.size_bytes, lay.num_blocks,
+                                   lay.bytes_per_block, lay.kv_stride_bytes, lay.segments, 0, 1, len(tensors))
+    src_l, dst_l = src.tolist(), dst.tolist()
+
+    def e2e_step(k):
+        hashes = [f"r{rank}-s{k}-b{i}".encode() for i in range(n)]
+        t0 = time.perf_counter()
+        eng.batch_save_kv_blocks(f"bench{rank}", 0, local, [(nm, src_l, hashes) for nm in names])
+        t1 = time.perf_counter()
+        s = PyLoadState()
+        eng.batch_load_kv_blocks(f"bench{rank}", 0, local, s.shm_name(), names, dst_l, hashes)
+        deadline = time.perf_counter() + 120.0
+        while not s.is_ready():
+            if time.perf_counter() > deadline:
+                raise TimeoutError("engine load did not complete within 120 s")
+        t2 = time.perf_counter()
+        assert s.get_state() == 1, "engine load failed"
+        s.close()
+        return t1 - t0, t2 - t1
+
+    for k in range(args.warmup):
+        e2e_step(-1 - k)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_times = [e2e_step(k) for k in range(e2e_steps)]
+    e2e_wall = time.perf_counter() - t0
+    barrier()
+    e2e_wall = max_over_ranks(e2e_wall)
+    e2e_value = world * 2 * payload * e2e_steps / e2e_wall / 1e9
+    e2e_load_p50 = max_over_ranks(statistics.median([b for _, b in e2e_times]) * 1e3)
+    eng_metrics = eng.metrics()
+    eng.close()
+
+    # ---- the reference's copy strategy on the same GPU ------------------------
+    ref = None
+    if not args.no_refcopy:
+        t0 = time.perf_counter()
+        refcopy_save(local, saves)
+        t1 = time.perf_counter()
+        runs = refcopy_load(local, loads)
+        t2 = time.perf_counter()
+        ref = {"save_GBps": round(payload / (t1 - t0) / 1e9, 3), "load_GBps": round(payload / (t2 - t1) / 1e9, 3),
+               "value": round(2 * payload / (t2 - t0) / 1e9, 3), "load_ms": round((t2 - t1) * 1e3, 3),
+               "h2d_runs": runs, "d2h_copies": sum(len(s.block_idx) * (2 if s.layout.split else 1) for s in saves),
+               "how": "per-segment synchronous D2H (gpu_worker.rs:343-360) + merged-run async H2D "
+                      "(transfer.rs:116-198), restated in C++, same GPU and pool"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = CpuWorkload(wl, os.cpu_count() or 1).rate(args.cpu_seconds)
+
+    if rank == 0:
+        link_dir = min(link["h2d"], link["d2h"])
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded ~N(0,1) bf16 KV)",
+            "config": config_block(args, wl),
+            "per_gpu_GBps": round(value / world, 3),
+            "save_GBps": round(save_gbps, 3), "load_GBps": round(load_gbps, 3), "p50_load_ms": round(p50_load, 3),
+            "payload_bytes_per_direction": payload,
+            "host_link": {"peak_h2d_GBps": link["h2d"], "peak_d2h_GBps": link["d2h"],
+                          "save_frac": round(save_gbps / link["d2h"], 3),
+                          "load_frac": round(load_gbps / link["h2d"], 3),
+                          "how": "pinned 1 GiB cudaMemcpyAsync, best of 3, this GPU"},
+            "roofline": {"bound": "hbm", "achieved": round(kernel_gbps, 1) if kernel_gbps else None,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(kernel_gbps / peaks["hbm_gbs"], 3) if kernel_gbps else None,
+                         "traffic": None, "peak_source": peaks["source"],
+                         "kernel": "kv_copy_kernel (pack+unpack)",
+                         "bytes_per_launch": round(st["kernel_bytes"] / max(1, st["timed_launches"])),
+                         "avg_launch_us": round(st["kernel_ms"] * 1e3 / max(1, st["timed_launches"]), 2)},
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": payload,
+                    "d2h_bytes_per_step": payload, "p50_load_ms": round(e2e_load_p50, 3), "steps": e2e_steps,
+                    "api": "PegaEngine.batch_save_kv_blocks + batch_load_kv_blocks + PyLoadState"},
+            "gpu_launches": st["kernel_launches"],
+            "copy_calls": st["copy_calls"],
+            "reference_copy_path": ref,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "engine_metrics": {k: eng_metrics[k] for k in ("save_bytes", "load_bytes", "load_failures",
+                                                           "cache_block_evictions")},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

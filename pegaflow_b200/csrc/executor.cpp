@@ -1,0 +1,726 @@
+// Transfer executor: plan building, validation, staging-ring pipeline.
+//
+// Save (staged):  pack kernel -> HBM slot  ==event==>  D2H DMA -> pinned pool
+// Load (staged):  H2D DMA -> HBM slot  ==event==>  unpack kernel -> paged KV
+// Slots form a ring; a slot is refilled only after the consumer of its last
+// contents has finished (ev_drained). Several copy streams keep more than one
+// DMA in flight on the host link. Direct mode skips the ring: the kernel
+// reads/writes mapped pinned host memory itself.
+#include "executor.h"
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+#include "common.h"
+#include "pinned.h"
+
+namespace pf {
+
+// ---------------------------------------------------------------------------
+// Layout helpers (reference semantics)
+// ---------------------------------------------------------------------------
+
+bool is_split_layout(const pf_layer_desc& l) {
+  // lib.rs:636, gpu_worker.rs:218,326
+  return l.segments == 2 && l.kv_stride_bytes > l.bytes_per_block;
+}
+
+bool is_contiguous_layout(const pf_layer_desc& l) {
+  // transfer.rs:50-52
+  return l.segments <= 1 || l.kv_stride_bytes == l.bytes_per_block;
+}
+
+UnitGeometry save_geometry(const pf_layer_desc& l) {
+  if (is_split_layout(l)) return {2u, l.bytes_per_block, l.kv_stride_bytes};
+  // copy_block_gpu_to_cpu (transfer.rs:200-239)
+  if (is_contiguous_layout(l)) return {1u, l.bytes_per_block * l.segments, 0};
+  return {static_cast<uint32_t>(l.segments), l.bytes_per_block, l.kv_stride_bytes};
+}
+
+UnitGeometry load_geometry(const pf_layer_desc& l) {
+  if (is_split_layout(l)) return {2u, l.bytes_per_block, l.kv_stride_bytes};
+  // gpu_worker.rs:260-282: one block_size_bytes copy at segment 0's offset.
+  return {1u, l.bytes_per_block * l.segments, 0};
+}
+
+void validate_layout(const pf_layer_desc& l, const char* layer_name) {
+  // register_context_layer (lib.rs:389-449), same order and messages.
+  const std::string name = layer_name ? layer_name : "";
+  if (l.bytes_per_block == 0 || l.num_blocks == 0 || l.segments == 0) {
+    throw invalid_argument("invalid KV cache layout for layer " + name);
+  }
+  if (l.segments > 1 && l.kv_stride_bytes == 0) {
+    throw invalid_argument("kv_stride_bytes must be > 0 when segments > 1 for layer " + name);
+  }
+  uint64_t block_size = 0;
+  if (mul_ovf(l.bytes_per_block, l.segments, &block_size)) {
+    throw invalid_argument("block size overflow: bytes_per_block=" + std::to_string(l.bytes_per_block) +
+                           " segments=" + std::to_string(l.segments) + " for layer " + name);
+  }
+  uint64_t max_block_offset = 0;
+  if (mul_ovf(l.num_blocks - 1, l.bytes_per_block, &max_block_offset)) {
+    throw invalid_argument("num_blocks " + std::to_string(l.num_blocks) + " too large for layer " + name);
+  }
+  uint64_t max_segment_offset = 0;
+  if (mul_ovf(l.segments - 1, l.kv_stride_bytes, &max_segment_offset)) {
+    throw invalid_argument("segments/stride overflow for layer " + name + " (segments=" +
+                           std::to_string(l.segments) + ", stride=" + std::to_string(l.kv_stride_bytes) + ")");
+  }
+  uint64_t max_offset = 0;
+  if (add_ovf(max_block_offset, max_segment_offset, &max_offset)) {
+    throw invalid_argument("layout offset overflow for layer " + name);
+  }
+  uint64_t end = 0;
+  if (add_ovf(max_offset, l.bytes_per_block, &end)) {
+    throw invalid_argument("layout end overflow for layer " + name);
+  }
+  if (end > l.size_bytes) {
+    throw invalid_argument("registered memory too small for layer " + name + ": need at least " +
+                           std::to_string(end) + " bytes, got " + std::to_string(l.size_bytes));
+  }
+}
+
+uint64_t segment_offset(const pf_layer_desc& l, uint64_t block_idx, uint64_t segment_idx) {
+  // transfer.rs:18-47
+  if (segment_idx >= l.segments) throw storage_error("Segment index out of range");
+  uint64_t base = 0, seg = 0, off = 0, end = 0;
+  if (mul_ovf(block_idx, l.bytes_per_block, &base)) throw storage_error("Block offset overflow");
+  if (mul_ovf(segment_idx, l.kv_stride_bytes, &seg)) throw storage_error("Segment offset overflow");
+  if (add_ovf(base, seg, &off)) throw storage_error("Combined offset overflow");
+  if (add_ovf(off, l.bytes_per_block, &end) || end > l.size_bytes) {
+    throw storage_error("Block " + std::to_string(block_idx) + " segment " + std::to_string(segment_idx) +
+                        " exceeds registered memory (offset " + std::to_string(off) + ", size " +
+                        std::to_string(l.bytes_per_block) + ", limit " + std::to_string(l.size_bytes) + ")");
+  }
+  return off;
+}
+
+namespace {
+
+constexpr uint64_t kDenseAlign = 256;
+constexpr uint64_t kMaxUnitBytes = 1ull << 31;
+
+uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+bool aligned16(uint64_t v) { return (v & 15u) == 0; }
+
+// The copy of unit (b, u) must stay inside the registration. This is stricter
+// than segment_offset for non-split loads, where the reference copies
+// block_size_bytes after checking only bytes_per_block (transfer.rs:39-44 vs
+// gpu_worker.rs:266-272); a copy past size_bytes is refused here instead of
+// writing outside the registered tensor.
+void check_unit_range(const pf_layer_desc& l, uint64_t b, uint32_t u, const UnitGeometry& g) {
+  uint64_t off = 0, t = 0, end = 0;
+  if (mul_ovf(b, l.bytes_per_block, &off) || mul_ovf(u, g.unit_stride, &t) || add_ovf(off, t, &off) ||
+      add_ovf(off, g.unit_bytes, &end) || end > l.size_bytes) {
+    throw storage_error("Block " + std::to_string(b) + " unit " + std::to_string(u) + " (" +
+                        std::to_string(g.unit_bytes) + " bytes) exceeds registered memory (limit " +
+                        std::to_string(l.size_bytes) + ")");
+  }
+}
+
+// The KV tensor must be device memory of this executor's device.
+void check_device_range(int device, const pf_layer_desc& l) {
+  for (uint64_t addr : {l.data_ptr, l.data_ptr + l.size_bytes - 1}) {
+    cudaPointerAttributes attr{};
+    cudaError_t err = cudaPointerGetAttributes(&attr, reinterpret_cast<const void*>(addr));
+    if (err != cudaSuccess) {
+      cudaGetLastError();
+      throw invalid_argument("KV tensor address is not CUDA memory");
+    }
+    if ((attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) || attr.device != device) {
+      throw invalid_argument("KV tensor is not device memory of device " + std::to_string(device));
+    }
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Executor lifecycle
+// ---------------------------------------------------------------------------
+
+Executor::Executor(int device, const pf_executor_config& cfg) : device_(device), cfg_(cfg) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    throw cuda_init("no CUDA device available");
+  }
+  if (device < 0 || device >= count) {
+    throw cuda_init("device " + std::to_string(device) + " out of range (" + std::to_string(count) + " devices)");
+  }
+  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  cuda_check(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
+  if (cfg_.staging_chunk_bytes == 0) cfg_.staging_chunk_bytes = 16ull << 20;
+  if (cfg_.staging_slots == 0) cfg_.staging_slots = 4;
+  if (cfg_.ctas_per_sm == 0) cfg_.ctas_per_sm = 4;
+  if (cfg_.copy_streams == 0) cfg_.copy_streams = 2;
+  if (cfg_.save_mode == PF_MODE_AUTO) cfg_.save_mode = PF_MODE_STAGED;
+  if (cfg_.load_mode == PF_MODE_AUTO) cfg_.load_mode = PF_MODE_STAGED;
+  // A slot must hold one tile plus the alignment slack of a chunk start.
+  slot_bytes_ = align_up(std::max<uint64_t>(cfg_.staging_chunk_bytes, 2 * kTileBytes), kDenseAlign);
+  slots_ = std::max<uint32_t>(cfg_.staging_slots, 1);
+
+  cuda_check(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda_check(cudaStreamCreateWithFlags(&kstream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  cstreams_.resize(cfg_.copy_streams);
+  ev_copy_done_.resize(cfg_.copy_streams);
+  for (uint32_t i = 0; i < cfg_.copy_streams; ++i) {
+    cuda_check(cudaStreamCreateWithFlags(&cstreams_[i], cudaStreamNonBlocking), "cudaStreamCreate");
+    cuda_check(cudaEventCreateWithFlags(&ev_copy_done_[i], cudaEventDisableTiming), "cudaEventCreate");
+  }
+  ev_filled_.resize(slots_);
+  ev_drained_.resize(slots_);
+  for (uint32_t i = 0; i < slots_; ++i) {
+    cuda_check(cudaEventCreateWithFlags(&ev_filled_[i], cudaEventDisableTiming), "cudaEventCreate");
+    cuda_check(cudaEventCreateWithFlags(&ev_drained_[i], cudaEventDisableTiming), "cudaEventCreate");
+  }
+  cuda_check(cudaEventCreateWithFlags(&ev_start_, cudaEventDisableTiming), "cudaEventCreate");
+  cuda_check(cudaEventCreateWithFlags(&ev_plan_, cudaEventDisableTiming), "cudaEventCreate");
+  cuda_check(cudaEventCreateWithFlags(&ev_done_, cudaEventDisableTiming), "cudaEventCreate");
+  cuda_check(cudaMalloc(reinterpret_cast<void**>(&staging_), slot_bytes_ * slots_), "cudaMalloc(staging)");
+  // Nothing is in flight yet: record the "previous call finished" events once.
+  cuda_check(cudaEventRecord(ev_done_, kstream_), "cudaEventRecord");
+  for (uint32_t i = 0; i < cfg_.copy_streams; ++i) {
+    cuda_check(cudaEventRecord(ev_copy_done_[i], cstreams_[i]), "cudaEventRecord");
+  }
+}
+
+Executor::~Executor() {
+  cudaSetDevice(device_);
+  cudaDeviceSynchronize();
+  for (auto& p : timed_) {
+    cudaEventDestroy(p.first);
+    cudaEventDestroy(p.second);
+  }
+  for (auto e : event_pool_) cudaEventDestroy(e);
+  for (auto e : ev_filled_) cudaEventDestroy(e);
+  for (auto e : ev_drained_) cudaEventDestroy(e);
+  for (auto e : ev_copy_done_) cudaEventDestroy(e);
+  cudaEventDestroy(ev_start_);
+  cudaEventDestroy(ev_plan_);
+  cudaEventDestroy(ev_done_);
+  for (auto s : cstreams_) cudaStreamDestroy(s);
+  cudaStreamDestroy(kstream_);
+  cudaStreamDestroy(own_stream_);
+  cudaFree(staging_);
+  cudaFree(d_plan_);
+  if (h_plan_) cudaFreeHost(h_plan_);
+  cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Plan building
+// ---------------------------------------------------------------------------
+
+void Executor::build_save(const pf_save_layer* layers, uint64_t n_layers, bool staged, Built* b) {
+  uint64_t dense = 0;
+  uint32_t unit_base = 0;
+  for (uint64_t li = 0; li < n_layers; ++li) {
+    const pf_save_layer& s = layers[li];
+    const pf_layer_desc& l = s.layer;
+    const std::string lname = "#" + std::to_string(li);
+    validate_layout(l, lname.c_str());
+    if (s.n == 0) continue;
+    if (s.block_idx == nullptr || s.k_dst == nullptr) throw invalid_argument("null block list or destination");
+    if (l.num_blocks > 0xffffffffull || s.n > 0xffffffffull) throw invalid_argument("too many blocks for one layer");
+    check_device_range(device_, l);
+    const UnitGeometry g = save_geometry(l);
+    if (g.unit_bytes > kMaxUnitBytes) throw invalid_argument("block larger than 2 GiB");
+    const uint64_t block_size = l.bytes_per_block * l.segments;
+
+    for (uint64_t i = 0; i < s.n; ++i) {
+      const int64_t bi = s.block_idx[i];
+      if (bi < 0 || static_cast<uint64_t>(bi) >= l.num_blocks) {
+        // lib.rs:597-603
+        throw invalid_argument("block " + std::to_string(bi) + " out of range for layer " + lname + " (" +
+                               std::to_string(l.num_blocks) + " blocks registered)");
+      }
+      const uint64_t blk = static_cast<uint64_t>(bi);
+      if (is_split_layout(l)) {
+        segment_offset(l, blk, 0);
+        segment_offset(l, blk, 1);
+      } else if (is_contiguous_layout(l)) {
+        segment_offset(l, blk, 0);
+      } else {
+        for (uint64_t sg = 0; sg < l.segments; ++sg) segment_offset(l, blk, sg);
+      }
+      for (uint32_t u = 0; u < g.units; ++u) check_unit_range(l, blk, u, g);
+    }
+
+    // Host destinations (SaveBlock pointers, lib.rs:671-679 and 739-747).
+    std::vector<uint64_t> host_base(g.units);
+    uint64_t host_pitch;
+    const uint64_t k = reinterpret_cast<uint64_t>(s.k_dst);
+    if (is_split_layout(l)) {
+      if (s.v_dst) {
+        host_base[0] = k;
+        host_base[1] = reinterpret_cast<uint64_t>(s.v_dst);
+        host_pitch = l.bytes_per_block;
+      } else {  // SaveBlock with v_dst_ptr None: V follows K (gpu_worker.rs:354-356)
+        host_base[0] = k;
+        host_base[1] = k + l.bytes_per_block;
+        host_pitch = 2 * l.bytes_per_block;
+      }
+    } else if (is_contiguous_layout(l)) {
+      host_base[0] = k;
+      host_pitch = block_size;
+    } else {  // strided: segment s at dst + s*bytes_per_block (transfer.rs:228-230)
+      for (uint32_t u = 0; u < g.units; ++u) host_base[u] = k + u * l.bytes_per_block;
+      host_pitch = block_size;
+    }
+
+    PlanLayer p{};
+    p.cache_base = l.data_ptr;
+    p.block_pitch = l.bytes_per_block;
+    p.unit_stride = g.unit_stride;
+    p.unit_bytes = static_cast<uint32_t>(g.unit_bytes);
+    p.units = g.units;
+    p.n = static_cast<uint32_t>(s.n);
+    p.tiles_per_unit = static_cast<uint32_t>((g.unit_bytes + kTileBytes - 1) / kTileBytes);
+    p.tile_start = b->total_tiles;
+    p.tile_count = static_cast<uint64_t>(g.units) * s.n * p.tiles_per_unit;
+    if (p.tile_count > 0xffffffffull) throw invalid_argument("layer transfer too large for one plan");
+    p.ids_off = static_cast<uint32_t>(b->ids.size());
+    p.side_off = static_cast<uint32_t>(b->side_base.size());
+    p.unit_off = unit_base;
+    p.done_index = static_cast<uint32_t>(li);
+    bool vec = aligned16(l.data_ptr) && aligned16(l.bytes_per_block) && aligned16(g.unit_stride) &&
+               aligned16(g.unit_bytes);
+    dense = align_up(dense, kDenseAlign);
+    const uint64_t dense_layer = dense;
+    if (staged) {
+      p.side_pitch = g.unit_bytes;
+      for (uint32_t u = 0; u < g.units; ++u) b->side_base.push_back(dense_layer + u * s.n * g.unit_bytes);
+    } else {
+      p.side_pitch = host_pitch;
+      vec = vec && aligned16(host_pitch);
+      for (uint32_t u = 0; u < g.units; ++u) {
+        vec = vec && aligned16(host_base[u]);
+        b->side_base.push_back(host_base[u]);
+      }
+    }
+    p.flags = vec ? kFlagVector : 0u;
+    for (uint64_t i = 0; i < s.n; ++i) b->ids.push_back(static_cast<uint32_t>(s.block_idx[i]));
+
+    // Host extents in unit order, merged where both sides are contiguous.
+    for (uint32_t u = 0; u < g.units; ++u) {
+      for (uint64_t i = 0; i < s.n; ++i) {
+        const uint64_t d = dense_layer + (u * s.n + i) * g.unit_bytes;
+        const uint64_t h = host_base[u] + i * host_pitch;
+        if (!b->runs.empty()) {
+          Run& r = b->runs.back();
+          if (r.dense + r.bytes == d && r.host + r.bytes == h) {
+            r.bytes += g.unit_bytes;
+            continue;
+          }
+        }
+        b->runs.push_back({d, h, g.unit_bytes});
+      }
+    }
+    dense = dense_layer + static_cast<uint64_t>(g.units) * s.n * g.unit_bytes;
+    b->total_tiles += p.tile_count;
+    b->total_bytes += static_cast<uint64_t>(g.units) * s.n * g.unit_bytes;
+    unit_base += g.units * static_cast<uint32_t>(s.n);
+    b->layers.push_back(p);
+  }
+}
+
+void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool staged, Built* b) {
+  uint64_t dense = 0;
+  uint32_t unit_base = 0;
+  for (uint64_t li = 0; li < n_layers; ++li) {
+    const pf_load_layer& s = layers[li];
+    const pf_layer_desc& l = s.layer;
+    const std::string lname = "#" + std::to_string(li);
+    validate_layout(l, lname.c_str());
+    if (s.n == 0) continue;
+    if (s.block_idx == nullptr || s.k_src == nullptr) throw invalid_argument("null block list or source");
+    if (l.num_blocks > 0xffffffffull || s.n > 0xffffffffull) throw invalid_argument("too many blocks for one layer");
+    check_device_range(device_, l);
+    const UnitGeometry g = load_geometry(l);
+    if (g.unit_bytes > kMaxUnitBytes) throw invalid_argument("block larger than 2 GiB");
+    const bool split = is_split_layout(l);
+
+    for (uint64_t i = 0; i < s.n; ++i) {
+      const int64_t bi = s.block_idx[i];
+      if (bi < 0) throw invalid_argument("negative block index " + std::to_string(bi));
+      const uint64_t blk = static_cast<uint64_t>(bi);
+      // process_load_task's checks (gpu_worker.rs:227-230, 266-267) ...
+      segment_offset(l, blk, 0);
+      if (split) segment_offset(l, blk, 1);
+      // ... plus the copy's own end (see check_unit_range).
+      for (uint32_t u = 0; u < g.units; ++u) check_unit_range(l, blk, u, g);
+      if (s.k_src[i] == nullptr) throw invalid_argument("null source pointer for block " + std::to_string(bi));
+    }
+
+    PlanLayer p{};
+    p.cache_base = l.data_ptr;
+    p.block_pitch = l.bytes_per_block;
+    p.unit_stride = g.unit_stride;
+    p.unit_bytes = static_cast<uint32_t>(g.unit_bytes);
+    p.units = g.units;
+    p.n = static_cast<uint32_t>(s.n);
+    p.tiles_per_unit = static_cast<uint32_t>((g.unit_bytes + kTileBytes - 1) / kTileBytes);
+    p.tile_start = b->total_tiles;
+    p.tile_count = static_cast<uint64_t>(g.units) * s.n * p.tiles_per_unit;
+    if (p.tile_count > 0xffffffffull) throw invalid_argument("layer transfer too large for one plan");
+    p.ids_off = static_cast<uint32_t>(b->ids.size());
+    p.side_off = static_cast<uint32_t>(b->side_base.size());
+    p.unit_off = unit_base;
+    p.done_index = static_cast<uint32_t>(li);
+    bool vec = aligned16(l.data_ptr) && aligned16(l.bytes_per_block) && aligned16(g.unit_stride) &&
+               aligned16(g.unit_bytes);
+    dense = align_up(dense, kDenseAlign);
+    const uint64_t dense_layer = dense;
+    p.side_pitch = g.unit_bytes;
+    for (uint32_t u = 0; u < g.units; ++u) b->side_base.push_back(dense_layer + u * s.n * g.unit_bytes);
+    for (uint64_t i = 0; i < s.n; ++i) b->ids.push_back(static_cast<uint32_t>(s.block_idx[i]));
+
+    for (uint32_t u = 0; u < g.units; ++u) {
+      for (uint64_t i = 0; i < s.n; ++i) {
+        uint64_t h;
+        if (u == 0) {
+          h = reinterpret_cast<uint64_t>(s.k_src[i]);
+        } else {  // V: LayerBlock::v_ptr or K + bytes_per_block (gpu_worker.rs:233-236)
+          const void* v = s.v_src ? s.v_src[i] : nullptr;
+          h = v ? reinterpret_cast<uint64_t>(v) : reinterpret_cast<uint64_t>(s.k_src[i]) + l.bytes_per_block;
+        }
+        if (!staged) {
+          b->side_ptrs.push_back(h);
+          vec = vec && aligned16(h);
+        }
+        const uint64_t d = dense_layer + (u * s.n + i) * g.unit_bytes;
+        if (!b->runs.empty()) {
+          Run& r = b->runs.back();
+          if (r.dense + r.bytes == d && r.host + r.bytes == h) {
+            r.bytes += g.unit_bytes;
+            continue;
+          }
+        }
+        b->runs.push_back({d, h, g.unit_bytes});
+      }
+    }
+    p.flags = vec ? kFlagVector : 0u;
+    dense = dense_layer + static_cast<uint64_t>(g.units) * s.n * g.unit_bytes;
+    b->total_tiles += p.tile_count;
+    b->total_bytes += static_cast<uint64_t>(g.units) * s.n * g.unit_bytes;
+    unit_base += g.units * static_cast<uint32_t>(s.n);
+    b->layers.push_back(p);
+  }
+}
+
+void Executor::make_chunks(const Built& b, std::vector<Chunk>* chunks) {
+  chunks->clear();
+  if (b.total_tiles == 0) return;
+  // Walk units in order; a chunk is a tile range whose dense span fits a slot.
+  // A chunk's dense start is rounded down to kDenseAlign so the slot shift
+  // (slot - dense_begin) keeps every 16-byte-aligned dense address aligned,
+  // even when the chunk starts inside a layer of unaligned units.
+  uint64_t cur_tb = 0, cur_db = 0, last_end = 0;
+  bool first = true;
+  uint64_t dense = 0;
+  for (const PlanLayer& p : b.layers) {
+    dense = align_up(dense, kDenseAlign);
+    const uint64_t nunits = static_cast<uint64_t>(p.units) * p.n;
+    for (uint64_t ul = 0; ul < nunits; ++ul) {
+      const uint64_t ud = dense + ul * p.unit_bytes;
+      const uint64_t ue = ud + p.unit_bytes;
+      const uint64_t ut = p.tile_start + ul * p.tiles_per_unit;
+      if (first) {
+        cur_tb = ut;
+        cur_db = ud / kDenseAlign * kDenseAlign;
+        first = false;
+      }
+      if (ue - cur_db <= slot_bytes_) {  // whole unit joins the current chunk
+        last_end = ue;
+        continue;
+      }
+      for (uint32_t t = 0; t < p.tiles_per_unit; ++t) {
+        const uint64_t d0 = ud + static_cast<uint64_t>(t) * kTileBytes;
+        const uint64_t d1 = std::min<uint64_t>(d0 + kTileBytes, ue);
+        if (d1 - cur_db > slot_bytes_) {
+          chunks->push_back({cur_tb, ut + t, cur_db, last_end});
+          cur_tb = ut + t;
+          cur_db = d0 / kDenseAlign * kDenseAlign;
+        }
+        last_end = d1;
+      }
+    }
+    dense += nunits * p.unit_bytes;
+  }
+  chunks->push_back({cur_tb, b.total_tiles, cur_db, last_end});
+}
+
+CopyArgs Executor::upload(const Built& b, bool with_counters, cudaStream_t s) {
+  auto a16 = [](size_t v) { return (v + 15) & ~size_t(15); };
+  const size_t sz_layers = a16(b.layers.size() * sizeof(PlanLayer));
+  const size_t sz_ids = a16(b.ids.size() * sizeof(uint32_t));
+  const size_t sz_base = a16(b.side_base.size() * sizeof(uint64_t));
+  const size_t sz_ptrs = a16(b.side_ptrs.size() * sizeof(uint64_t));
+  const size_t sz_cnt = with_counters ? a16(b.layers.size() * sizeof(unsigned long long)) : 0;
+  const size_t total = sz_layers + sz_ids + sz_base + sz_ptrs + sz_cnt;
+
+  // The pinned staging of the previous plan may still be in flight.
+  if (plan_pending_) cuda_check(cudaEventSynchronize(ev_plan_), "cudaEventSynchronize(plan)");
+  if (total > h_plan_cap_) {
+    if (h_plan_) cudaFreeHost(h_plan_);
+    h_plan_ = nullptr;
+    h_plan_cap_ = 0;
+    const size_t cap = std::max<size_t>(total * 2, 1 << 16);
+    cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&h_plan_), cap, cudaHostAllocDefault), "cudaHostAlloc(plan)");
+    h_plan_cap_ = cap;
+  }
+  if (total > d_plan_cap_) {
+    cuda_check(cudaStreamSynchronize(kstream_), "cudaStreamSynchronize");
+    if (d_plan_) cudaFree(d_plan_);
+    d_plan_ = nullptr;
+    d_plan_cap_ = 0;
+    const size_t cap = std::max<size_t>(total * 2, 1 << 16);
+    cuda_check(cudaMalloc(reinterpret_cast<void**>(&d_plan_), cap), "cudaMalloc(plan)");
+    d_plan_cap_ = cap;
+  }
+  uint8_t* h = h_plan_;
+  size_t off = 0;
+  std::memcpy(h + off, b.layers.data(), b.layers.size() * sizeof(PlanLayer));
+  off += sz_layers;
+  std::memcpy(h + off, b.ids.data(), b.ids.size() * sizeof(uint32_t));
+  off += sz_ids;
+  std::memcpy(h + off, b.side_base.data(), b.side_base.size() * sizeof(uint64_t));
+  off += sz_base;
+  if (!b.side_ptrs.empty()) std::memcpy(h + off, b.side_ptrs.data(), b.side_ptrs.size() * sizeof(uint64_t));
+  off += sz_ptrs;
+  if (sz_cnt) std::memset(h + off, 0, sz_cnt);
+  cuda_check(cudaMemcpyAsync(d_plan_, h_plan_, total, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync(plan)");
+  cuda_check(cudaEventRecord(ev_plan_, s), "cudaEventRecord(plan)");
+  plan_pending_ = true;
+
+  CopyArgs a{};
+  off = 0;
+  a.layers = reinterpret_cast<const PlanLayer*>(d_plan_ + off);
+  off += sz_layers;
+  a.ids = reinterpret_cast<const uint32_t*>(d_plan_ + off);
+  off += sz_ids;
+  a.side_base = reinterpret_cast<const uint64_t*>(d_plan_ + off);
+  off += sz_base;
+  a.side_ptrs = reinterpret_cast<const uint64_t*>(d_plan_ + off);
+  off += sz_ptrs;
+  a.layer_tiles_done = sz_cnt ? reinterpret_cast<unsigned long long*>(d_plan_ + off) : nullptr;
+  a.n_layers = static_cast<uint32_t>(b.layers.size());
+  return a;
+}
+
+int Executor::grid_for(uint64_t tiles) const {
+  const uint64_t max_grid = static_cast<uint64_t>(num_sms_) * cfg_.ctas_per_sm;
+  const uint64_t need = (tiles + 7) / 8;
+  return static_cast<int>(std::max<uint64_t>(1, std::min(need, max_grid)));
+}
+
+void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_begin, uint64_t tile_end,
+                      int64_t shift, cudaStream_t s) {
+  CopyArgs a = args0;
+  a.tile_begin = tile_begin;
+  a.tile_end = tile_end;
+  a.side_shift = shift;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (timing_) {
+    auto take = [this]() {
+      if (!event_pool_.empty()) {
+        cudaEvent_t e = event_pool_.back();
+        event_pool_.pop_back();
+        return e;
+      }
+      cudaEvent_t e;
+      cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+      return e;
+    };
+    e0 = take();
+    e1 = take();
+    cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
+  }
+  cuda_check(launch_copy(dir, table, a, grid_for(tile_end - tile_begin), s), "kernel launch");
+  if (timing_) {
+    cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
+    timed_.emplace_back(e0, e1);
+  }
+  stats_.kernel_launches += 1;
+}
+
+void Executor::copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h, cudaStream_t s) {
+  // First run ending after the chunk start.
+  auto it = std::upper_bound(b.runs.begin(), b.runs.end(), c.dense_begin,
+                             [](uint64_t v, const Run& r) { return v < r.dense + r.bytes; });
+  for (; it != b.runs.end() && it->dense < c.dense_end; ++it) {
+    const uint64_t lo = std::max(it->dense, c.dense_begin);
+    const uint64_t hi = std::min(it->dense + it->bytes, c.dense_end);
+    if (hi <= lo) continue;
+    void* host = reinterpret_cast<void*>(it->host + (lo - it->dense));
+    uint8_t* dev = slot + (lo - c.dense_begin);
+    if (d2h) {
+      cuda_check(cudaMemcpyAsync(host, dev, hi - lo, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync D2H");
+    } else {
+      cuda_check(cudaMemcpyAsync(dev, host, hi - lo, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync H2D");
+    }
+    stats_.copy_calls += 1;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Save / load
+// ---------------------------------------------------------------------------
+
+void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t caller) {
+  std::lock_guard<std::mutex> g(mu_);
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  const bool staged = cfg_.save_mode != PF_MODE_DIRECT;
+  Built b;
+  build_save(layers, n_layers, staged, &b);
+  if (b.total_tiles == 0) return;
+  if (!staged) {
+    for (const Run& r : b.runs) {
+      if (!pinned_contains(reinterpret_cast<void*>(r.host), r.bytes)) {
+        throw invalid_argument("direct mode needs destinations in pinned memory allocated by this library");
+      }
+    }
+  }
+  // Order after the caller's work and after this executor's previous call.
+  cuda_check(cudaEventRecord(ev_start_, caller), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(kstream_, ev_start_, 0), "cudaStreamWaitEvent");
+  for (auto e : ev_copy_done_) cuda_check(cudaStreamWaitEvent(kstream_, e, 0), "cudaStreamWaitEvent");
+  for (auto cs : cstreams_) {
+    cuda_check(cudaStreamWaitEvent(cs, ev_start_, 0), "cudaStreamWaitEvent");
+    cuda_check(cudaStreamWaitEvent(cs, ev_done_, 0), "cudaStreamWaitEvent");
+  }
+  const CopyArgs args = upload(b, false, kstream_);
+  if (!staged) {
+    launch(kPack, false, args, 0, b.total_tiles, 0, kstream_);
+    stats_.kernel_bytes += b.total_bytes;
+  } else {
+    std::vector<Chunk> chunks;
+    make_chunks(b, &chunks);
+    for (size_t k = 0; k < chunks.size(); ++k) {
+      const uint32_t si = static_cast<uint32_t>(k % slots_);
+      uint8_t* slot = staging_ + static_cast<uint64_t>(si) * slot_bytes_;
+      if (k >= slots_) cuda_check(cudaStreamWaitEvent(kstream_, ev_drained_[si], 0), "cudaStreamWaitEvent");
+      const int64_t shift = static_cast<int64_t>(reinterpret_cast<uint64_t>(slot)) -
+                            static_cast<int64_t>(chunks[k].dense_begin);
+      launch(kPack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, kstream_);
+      cuda_check(cudaEventRecord(ev_filled_[si], kstream_), "cudaEventRecord");
+      cudaStream_t cs = cstreams_[k % cstreams_.size()];
+      cuda_check(cudaStreamWaitEvent(cs, ev_filled_[si], 0), "cudaStreamWaitEvent");
+      copy_runs(b, chunks[k], slot, true, cs);
+      cuda_check(cudaEventRecord(ev_drained_[si], cs), "cudaEventRecord");
+    }
+    stats_.kernel_bytes += 2 * b.total_bytes;
+  }
+  cuda_check(cudaEventRecord(ev_done_, kstream_), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(caller, ev_done_, 0), "cudaStreamWaitEvent");
+  for (size_t j = 0; j < cstreams_.size(); ++j) {
+    cuda_check(cudaEventRecord(ev_copy_done_[j], cstreams_[j]), "cudaEventRecord");
+    cuda_check(cudaStreamWaitEvent(caller, ev_copy_done_[j], 0), "cudaStreamWaitEvent");
+  }
+  stats_.bytes_saved += b.total_bytes;
+}
+
+void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t caller, int64_t* layer_done) {
+  std::lock_guard<std::mutex> g(mu_);
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  const bool staged = cfg_.load_mode != PF_MODE_DIRECT;
+  Built b;
+  build_load(layers, n_layers, staged, &b);
+  if (layer_done) {
+    if (!pinned_contains(layer_done, n_layers * sizeof(int64_t))) {
+      throw invalid_argument("layer_done must be pinned memory allocated by this library");
+    }
+    // Layers without blocks are complete at once.
+    std::vector<bool> has(n_layers, false);
+    for (const PlanLayer& p : b.layers) has[p.done_index] = true;
+    for (uint64_t l = 0; l < n_layers; ++l) {
+      if (!has[l]) reinterpret_cast<volatile int64_t*>(layer_done)[l] = 1;
+    }
+  }
+  if (b.total_tiles == 0) return;
+  if (!staged) {
+    for (const Run& r : b.runs) {
+      if (!pinned_contains(reinterpret_cast<void*>(r.host), r.bytes)) {
+        throw invalid_argument("direct mode needs sources in pinned memory allocated by this library");
+      }
+    }
+  }
+  cuda_check(cudaEventRecord(ev_start_, caller), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(kstream_, ev_start_, 0), "cudaStreamWaitEvent");
+  for (auto e : ev_copy_done_) cuda_check(cudaStreamWaitEvent(kstream_, e, 0), "cudaStreamWaitEvent");
+  for (auto cs : cstreams_) {
+    cuda_check(cudaStreamWaitEvent(cs, ev_start_, 0), "cudaStreamWaitEvent");
+    cuda_check(cudaStreamWaitEvent(cs, ev_done_, 0), "cudaStreamWaitEvent");
+  }
+  CopyArgs args = upload(b, layer_done != nullptr, kstream_);
+  args.layer_done = layer_done;
+  if (!staged) {
+    launch(kUnpack, true, args, 0, b.total_tiles, 0, kstream_);
+    stats_.kernel_bytes += b.total_bytes;
+  } else {
+    std::vector<Chunk> chunks;
+    make_chunks(b, &chunks);
+    for (size_t k = 0; k < chunks.size(); ++k) {
+      const uint32_t si = static_cast<uint32_t>(k % slots_);
+      uint8_t* slot = staging_ + static_cast<uint64_t>(si) * slot_bytes_;
+      cudaStream_t cs = cstreams_[k % cstreams_.size()];
+      if (k >= slots_) cuda_check(cudaStreamWaitEvent(cs, ev_drained_[si], 0), "cudaStreamWaitEvent");
+      copy_runs(b, chunks[k], slot, false, cs);
+      cuda_check(cudaEventRecord(ev_filled_[si], cs), "cudaEventRecord");
+      cuda_check(cudaStreamWaitEvent(kstream_, ev_filled_[si], 0), "cudaStreamWaitEvent");
+      const int64_t shift = static_cast<int64_t>(reinterpret_cast<uint64_t>(slot)) -
+                            static_cast<int64_t>(chunks[k].dense_begin);
+      launch(kUnpack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, kstream_);
+      cuda_check(cudaEventRecord(ev_drained_[si], kstream_), "cudaEventRecord");
+    }
+    stats_.kernel_bytes += 2 * b.total_bytes;
+  }
+  cuda_check(cudaEventRecord(ev_done_, kstream_), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(caller, ev_done_, 0), "cudaStreamWaitEvent");
+  for (size_t j = 0; j < cstreams_.size(); ++j) {
+    cuda_check(cudaEventRecord(ev_copy_done_[j], cstreams_[j]), "cudaEventRecord");
+  }
+  stats_.bytes_loaded += b.total_bytes;
+}
+
+void Executor::save_sync(const pf_save_layer* layers, uint64_t n_layers) {
+  save(layers, n_layers, own_stream_);
+  cuda_check(cudaStreamSynchronize(own_stream_), "cudaStreamSynchronize(save)");
+}
+
+void Executor::load_sync(const pf_load_layer* layers, uint64_t n_layers) {
+  load(layers, n_layers, own_stream_, nullptr);
+  cuda_check(cudaStreamSynchronize(own_stream_), "cudaStreamSynchronize(load)");
+}
+
+void Executor::stats(pf_executor_stats* out) {
+  std::lock_guard<std::mutex> g(mu_);
+  for (auto& p : timed_) {
+    cuda_check(cudaEventSynchronize(p.second), "cudaEventSynchronize");
+    float ms = 0.f;
+    cuda_check(cudaEventElapsedTime(&ms, p.first, p.second), "cudaEventElapsedTime");
+    stats_.kernel_ms += ms;
+    stats_.timed_launches += 1;
+    event_pool_.push_back(p.first);
+    event_pool_.push_back(p.second);
+  }
+  timed_.clear();
+  *out = stats_;
+}
+
+void Executor::reset_stats() {
+  pf_executor_stats tmp;
+  stats(&tmp);
+  std::lock_guard<std::mutex> g(mu_);
+  stats_ = pf_executor_stats{};
+}
+
+void Executor::set_timing(bool on) {
+  std::lock_guard<std::mutex> g(mu_);
+  timing_ = on;
+}
+
+}  // namespace pf

@@ -1,0 +1,110 @@
+// Per-device transfer executor: the B200 replacement for GpuWorkerPool's copy
+// loops (pegaflow-core/src/gpu_worker.rs:205-390).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <utility>
+#include <vector>
+
+#include "pegaflow.h"
+#include "plan.h"
+
+namespace pf {
+
+// Geometry of one layer of a transfer, derived from its registration the
+// way the reference chooses its copy loop (gpu_worker.rs:218,326; transfer.rs:50-52).
+struct UnitGeometry {
+  uint32_t units;        // units per block
+  uint64_t unit_bytes;   // bytes per unit
+  uint64_t unit_stride;  // HBM distance between units of a block
+};
+UnitGeometry save_geometry(const pf_layer_desc& l);
+UnitGeometry load_geometry(const pf_layer_desc& l);
+bool is_split_layout(const pf_layer_desc& l);       // lib.rs:636
+bool is_contiguous_layout(const pf_layer_desc& l);  // transfer.rs:50-52
+
+// Layout checks of register_context_layer (lib.rs:389-449).
+void validate_layout(const pf_layer_desc& l, const char* layer_name);
+// transfer::segment_offset (transfer.rs:18-47).
+uint64_t segment_offset(const pf_layer_desc& l, uint64_t block_idx, uint64_t segment_idx);
+
+class Executor {
+ public:
+  Executor(int device, const pf_executor_config& cfg);
+  ~Executor();
+  Executor(const Executor&) = delete;
+  Executor& operator=(const Executor&) = delete;
+
+  int device() const { return device_; }
+
+  // Enqueue a save/load ordered after `caller`; `caller` waits for completion.
+  void save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t caller);
+  void load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t caller,
+            int64_t* layer_done);
+  // Blocking wrappers on the executor's own stream.
+  void save_sync(const pf_save_layer* layers, uint64_t n_layers);
+  void load_sync(const pf_load_layer* layers, uint64_t n_layers);
+
+  void stats(pf_executor_stats* out);
+  void reset_stats();
+  void set_timing(bool on);
+
+ private:
+  struct Run {  // one contiguous (dense offset, host address, bytes) extent
+    uint64_t dense;
+    uint64_t host;
+    uint64_t bytes;
+  };
+  struct Chunk {
+    uint64_t tile_begin, tile_end;
+    uint64_t dense_begin, dense_end;
+  };
+  struct Built {
+    std::vector<PlanLayer> layers;
+    std::vector<uint32_t> ids;
+    std::vector<uint64_t> side_base;
+    std::vector<uint64_t> side_ptrs;
+    std::vector<Run> runs;  // staged mode only
+    uint64_t total_tiles = 0;
+    uint64_t total_bytes = 0;
+  };
+
+  void build_save(const pf_save_layer* layers, uint64_t n, bool staged, Built* b);
+  void build_load(const pf_load_layer* layers, uint64_t n, bool staged, Built* b);
+  void make_chunks(const Built& b, std::vector<Chunk>* chunks);
+  CopyArgs upload(const Built& b, bool with_counters, cudaStream_t s);
+  void launch(Dir dir, bool table, const CopyArgs& args, uint64_t tile_begin,
+              uint64_t tile_end, int64_t shift, cudaStream_t s);
+  int grid_for(uint64_t tiles) const;
+  void copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h,
+                 cudaStream_t s);
+
+  int device_;
+  pf_executor_config cfg_;
+  int num_sms_ = 148;
+  cudaStream_t own_stream_ = nullptr;   // for the blocking wrappers
+  cudaStream_t kstream_ = nullptr;      // pack/unpack kernels
+  std::vector<cudaStream_t> cstreams_;  // copy-engine DMA
+  uint8_t* staging_ = nullptr;
+  uint64_t slot_bytes_ = 0;
+  uint32_t slots_ = 0;
+  std::vector<cudaEvent_t> ev_filled_, ev_drained_;
+  cudaEvent_t ev_start_ = nullptr, ev_plan_ = nullptr, ev_done_ = nullptr;
+  std::vector<cudaEvent_t> ev_copy_done_;
+  uint8_t* d_plan_ = nullptr;
+  size_t d_plan_cap_ = 0;
+  uint8_t* h_plan_ = nullptr;
+  size_t h_plan_cap_ = 0;
+  bool plan_pending_ = false;
+
+  std::mutex mu_;
+  bool timing_ = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed_;  // pending kernel spans
+  std::vector<cudaEvent_t> event_pool_;
+  pf_executor_stats stats_{};
+};
+
+}  // namespace pf

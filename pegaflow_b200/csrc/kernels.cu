@@ -1,0 +1,172 @@
+// sm_100a pack/unpack kernels for paged-KV block transfers.
+//
+// One kernel, two directions:
+//   kPack   : cache (paged KV in HBM) -> dense side   (save, replaces the
+//             per-segment cuMemcpyDtoH loop of gpu_worker.rs:343-360)
+//   kUnpack : dense side -> cache                      (load, replaces the
+//             per-run cuMemcpyHtoDAsync loop of transfer.rs:116-198)
+// The dense side is either the HBM staging ring (the copy engine moves it
+// across the host link) or mapped pinned host memory (zero-copy).
+//
+// Work is split into 4 KiB tiles (plan.h). Each CTA owns a contiguous range
+// of tiles and its 8 warps walk it interleaved, so neighbouring warps touch
+// neighbouring bytes. Per tile, one warp decodes (layer, unit, block) with
+// integer math, reads the block index once (a broadcast load), and moves the
+// tile with 8 x 16-byte loads per lane in flight before the 8 stores.
+// Sorted and shuffled block lists cost the same: the block index only picks
+// the tile's base address.
+//
+// Bounds: the host validates every (block, unit) range against the layer's
+// registered size before launch; the kernel does no unchecked indexing beyond
+// the plan it is given.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "plan.h"
+
+namespace pf {
+namespace {
+
+constexpr int kWarpsPerCta = 8;
+constexpr int kThreads = kWarpsPerCta * 32;
+constexpr int kVecPerLane = kTileBytes / (32 * 16);  // 8
+static_assert(kVecPerLane == 8, "tile = 32 lanes x 8 x 16 B");
+
+// Streaming 16-byte load: the source is read exactly once, so keep it out of L1.
+__device__ __forceinline__ uint4 ld_v4(const char* p) {
+  uint4 v;
+  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_v4(char* p, const uint4& v) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void copy_tile(char* dst, const char* src,
+                                          uint32_t bytes, bool vec, int lane) {
+  if (vec) {
+    if (bytes == kTileBytes) {
+      uint4 r[kVecPerLane];
+#pragma unroll
+      for (int k = 0; k < kVecPerLane; ++k) r[k] = ld_v4(src + (k * 32 + lane) * 16);
+#pragma unroll
+      for (int k = 0; k < kVecPerLane; ++k) st_v4(dst + (k * 32 + lane) * 16, r[k]);
+    } else {
+      // Tail of a unit: bytes is a multiple of 16 below one tile.
+      for (uint32_t off = lane * 16u; off < bytes; off += 512u) st_v4(dst + off, ld_v4(src + off));
+    }
+  } else {
+    // Unaligned layouts (e.g. 4-byte per-block scales): byte granularity.
+    for (uint32_t off = lane; off < bytes; off += 32u) dst[off] = src[off];
+  }
+}
+
+// Count `done` finished tiles of layer l; the warp that completes the layer
+// raises its flag in host memory after a system-scope fence, so a host poller
+// that sees the flag also sees every byte of the layer.
+__device__ __forceinline__ void flush_layer(const CopyArgs& a, uint32_t l,
+                                            uint64_t layer_tiles, uint32_t done,
+                                            int lane) {
+  if (a.layer_tiles_done == nullptr || done == 0) return;
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) {
+    const unsigned long long prev = atomicAdd(&a.layer_tiles_done[l], (unsigned long long)done);
+    if (prev + done == layer_tiles) {
+      __threadfence_system();
+      *reinterpret_cast<volatile int64_t*>(a.layer_done + a.layers[l].done_index) = 1;
+      __threadfence_system();
+    }
+  }
+  __syncwarp();
+}
+
+template <int DIR, bool TABLE>
+__global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+
+  const uint64_t total = a.tile_end - a.tile_begin;
+  const uint64_t per_cta = (total + gridDim.x - 1) / gridDim.x;
+  const uint64_t cta_begin = a.tile_begin + (uint64_t)blockIdx.x * per_cta;
+  uint64_t cta_end = cta_begin + per_cta;
+  if (cta_end > a.tile_end) cta_end = a.tile_end;
+
+  uint64_t tile = cta_begin + (uint64_t)warp;
+  if (tile >= cta_end) return;
+
+  // Layer of the first tile: last l with tile_start <= tile.
+  uint32_t lo = 0, hi = a.n_layers;
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (a.layers[mid].tile_start <= tile) lo = mid; else hi = mid;
+  }
+  uint32_t l = lo;
+  PlanLayer L = a.layers[l];
+  uint32_t done_in_layer = 0;
+
+  for (; tile < cta_end; tile += kWarpsPerCta) {
+    while (tile >= L.tile_start + L.tile_count) {
+      flush_layer(a, l, L.tile_count, done_in_layer, lane);
+      done_in_layer = 0;
+      ++l;
+      L = a.layers[l];
+    }
+    const uint32_t local = (uint32_t)(tile - L.tile_start);
+    const uint32_t unit_local = local / L.tiles_per_unit;
+    const uint32_t t = local - unit_local * L.tiles_per_unit;
+    const uint32_t u = unit_local / L.n;
+    const uint32_t i = unit_local - u * L.n;
+    const uint64_t b = a.ids[L.ids_off + i];
+    const uint32_t in_unit = t * kTileBytes;
+    const uint32_t rest = L.unit_bytes - in_unit;
+    const uint32_t bytes = rest < kTileBytes ? rest : kTileBytes;
+
+    char* cache = reinterpret_cast<char*>(L.cache_base + b * L.block_pitch +
+                                          (uint64_t)u * L.unit_stride + in_unit);
+    char* side;
+    if (TABLE) {
+      side = reinterpret_cast<char*>(a.side_ptrs[L.unit_off + unit_local] + in_unit);
+    } else {
+      side = reinterpret_cast<char*>(a.side_base[L.side_off + u] + (uint64_t)i * L.side_pitch +
+                                     in_unit + a.side_shift);
+    }
+    if (DIR == kPack) {
+      copy_tile(side, cache, bytes, (L.flags & kFlagVector) != 0, lane);
+    } else {
+      copy_tile(cache, side, bytes, (L.flags & kFlagVector) != 0, lane);
+    }
+    ++done_in_layer;
+  }
+  flush_layer(a, l, L.tile_count, done_in_layer, lane);
+}
+
+}  // namespace
+
+cudaError_t launch_copy(Dir dir, bool table, const CopyArgs& args, int grid,
+                        cudaStream_t stream) {
+  if (args.tile_end <= args.tile_begin) return cudaSuccess;
+  if (grid < 1) grid = 1;
+  if (dir == kPack) {
+    if (table) {
+      kv_copy_kernel<kPack, true><<<grid, kThreads, 0, stream>>>(args);
+    } else {
+      kv_copy_kernel<kPack, false><<<grid, kThreads, 0, stream>>>(args);
+    }
+  } else {
+    if (table) {
+      kv_copy_kernel<kUnpack, true><<<grid, kThreads, 0, stream>>>(args);
+    } else {
+      kv_copy_kernel<kUnpack, false><<<grid, kThreads, 0, stream>>>(args);
+    }
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace pf

@@ -1,0 +1,127 @@
+#include "pinned.h"
+
+#include <cuda_runtime.h>
+#include <sys/mman.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <fstream>
+#include <map>
+#include <mutex>
+#include <sstream>
+#include <string>
+
+#include "common.h"
+
+namespace pf {
+
+namespace {
+std::mutex g_reg_mu;
+std::map<uintptr_t, size_t>& registry() {
+  static std::map<uintptr_t, size_t> r;
+  return r;
+}
+}  // namespace
+
+void pinned_register(const void* p, size_t bytes) {
+  std::lock_guard<std::mutex> g(g_reg_mu);
+  registry()[reinterpret_cast<uintptr_t>(p)] = bytes;
+}
+
+void pinned_unregister(const void* p) {
+  std::lock_guard<std::mutex> g(g_reg_mu);
+  registry().erase(reinterpret_cast<uintptr_t>(p));
+}
+
+bool pinned_contains(const void* p, size_t bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  std::lock_guard<std::mutex> g(g_reg_mu);
+  auto& r = registry();
+  auto it = r.upper_bound(a);
+  if (it == r.begin()) return false;
+  --it;
+  return a >= it->first && a + bytes <= it->first + it->second && a + bytes >= a;
+}
+
+size_t huge_page_size() {
+  std::ifstream f("/proc/meminfo");
+  std::string line;
+  while (std::getline(f, line)) {
+    if (line.rfind("Hugepagesize:", 0) == 0) {
+      std::istringstream is(line);
+      std::string key, unit;
+      size_t kb = 0;
+      is >> key >> kb >> unit;
+      if (unit == "kB") return kb * 1024;
+    }
+  }
+  return 0;
+}
+
+PinnedMemory::PinnedMemory(size_t size, PinKind kind, bool write_combined) : kind_(kind) {
+  if (size == 0) throw Error(PF_ERR_INVALID_ARGUMENT, "size must be greater than zero");
+  switch (kind) {
+    case PinKind::kCudaHostAlloc: {
+      unsigned flags = cudaHostAllocPortable | cudaHostAllocMapped;
+      if (write_combined) flags |= cudaHostAllocWriteCombined;
+      void* p = nullptr;
+      cudaError_t err = cudaHostAlloc(&p, size, flags);
+      if (err != cudaSuccess) {
+        cudaGetLastError();
+        throw cuda_init(std::string("cudaHostAlloc failed: ") + cudaGetErrorString(err));
+      }
+      ptr_ = static_cast<uint8_t*>(p);
+      size_ = size;
+      break;
+    }
+    case PinKind::kHugePagesRegistered: {
+      const size_t hp = huge_page_size();
+      if (hp == 0) {
+        throw cuda_init("cannot determine huge page size: Hugepagesize not found in /proc/meminfo");
+      }
+      const size_t aligned = (size + hp - 1) & ~(hp - 1);
+      void* p = mmap(nullptr, aligned, PROT_READ | PROT_WRITE,
+                     MAP_PRIVATE | MAP_ANONYMOUS | MAP_HUGETLB, -1, 0);
+      if (p == MAP_FAILED) throw cuda_init("mmap failed (MAP_HUGETLB)");
+      cudaError_t err = cudaHostRegister(p, aligned, cudaHostRegisterPortable | cudaHostRegisterMapped);
+      if (err != cudaSuccess) {
+        cudaGetLastError();
+        munmap(p, aligned);
+        throw cuda_init(std::string("cudaHostRegister failed: ") + cudaGetErrorString(err));
+      }
+      ptr_ = static_cast<uint8_t*>(p);
+      size_ = aligned;
+      break;
+    }
+    case PinKind::kPlainHost: {
+      void* p = nullptr;
+      if (posix_memalign(&p, 4096, size) != 0) throw std::bad_alloc();
+      ptr_ = static_cast<uint8_t*>(p);
+      size_ = size;
+      break;
+    }
+  }
+  if (kind != PinKind::kPlainHost) pinned_register(ptr_, size_);
+}
+
+PinnedMemory::~PinnedMemory() {
+  if (!ptr_) return;
+  if (kind_ != PinKind::kPlainHost) pinned_unregister(ptr_);
+  switch (kind_) {
+    case PinKind::kCudaHostAlloc:
+      if (cudaFreeHost(ptr_) != cudaSuccess) {
+        fprintf(stderr, "pegaflow_b200: cudaFreeHost failed\n");
+        cudaGetLastError();
+      }
+      break;
+    case PinKind::kHugePagesRegistered:
+      if (cudaHostUnregister(ptr_) != cudaSuccess) cudaGetLastError();
+      munmap(ptr_, size_);
+      break;
+    case PinKind::kPlainHost:
+      free(ptr_);
+      break;
+  }
+}
+
+}  // namespace pf

@@ -1,0 +1,361 @@
+#include "storage.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+
+#include "common.h"
+
+namespace pf {
+
+namespace {
+
+uint64_t fnv1a(const std::string& a, const std::string& b) {
+  uint64_t h = 1469598103934665603ull;
+  for (unsigned char c : a) {
+    h ^= c;
+    h *= 1099511628211ull;
+  }
+  h ^= 0xffu;
+  h *= 1099511628211ull;
+  for (unsigned char c : b) {
+    h ^= c;
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+uint64_t splitmix64(uint64_t x) {
+  x += 0x9e3779b97f4a7c15ull;
+  x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+  x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+  return x ^ (x >> 31);
+}
+
+constexpr uint64_t kDefaultBytesPerValue = 128ull << 20;  // cache.rs:14
+constexpr uint64_t kReclaimBatch = 64;                      // storage.rs:41
+constexpr uint64_t kPoolMinUnit = 64;
+constexpr uint32_t kPoolMaxAllocs = 4000000;  // pinned_pool.rs:61
+
+}  // namespace
+
+size_t BlockKeyHash::operator()(const BlockKey& k) const { return static_cast<size_t>(fnv1a(k.ns, k.hash)); }
+
+// ---------------------------------------------------------------------------
+// Pool
+// ---------------------------------------------------------------------------
+
+PoolAllocation::~PoolAllocation() {
+  if (pool) pool->free_internal(a);
+}
+
+std::shared_ptr<PinnedPool> PinnedPool::create(uint64_t bytes, PinKind kind, bool write_combined,
+                                               uint64_t unit_hint) {
+  if (bytes == 0) throw invalid_argument("Pinned memory pool size must be greater than zero");
+  auto mem = std::make_unique<PinnedMemory>(bytes, kind, write_combined);
+  const uint64_t actual = mem->size();
+  uint64_t unit = unit_hint;
+  if (unit == 0) unit = actual > 0xffffffffull ? (actual + 0xfffffffeull) / 0xffffffffull : 1;
+  unit = std::max(unit, kPoolMinUnit);
+  auto alloc = ScaledOffsetAllocator::make(actual, unit, false, kPoolMaxAllocs);
+  return std::shared_ptr<PinnedPool>(new PinnedPool(std::move(mem), std::move(alloc)));
+}
+
+std::shared_ptr<PoolAllocation> PinnedPool::allocate(uint64_t size) {
+  ScaledOffsetAllocator::Allocation a{};
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    try {
+      if (!alloc_.allocate(size, &a)) return nullptr;
+    } catch (const Error&) {
+      return nullptr;  // RequestTooLarge is logged and treated as exhaustion (pinned_pool.rs:130-138)
+    }
+  }
+  auto out = std::make_shared<PoolAllocation>();
+  out->pool = shared_from_this();
+  out->a = a;
+  out->ptr = mem_->data() + a.offset_bytes;
+  return out;
+}
+
+void PinnedPool::free_internal(const ScaledOffsetAllocator::Allocation& a) {
+  std::lock_guard<std::mutex> g(mu_);
+  alloc_.free(a);
+}
+
+void PinnedPool::usage(uint64_t* used, uint64_t* total) {
+  std::lock_guard<std::mutex> g(mu_);
+  *total = alloc_.total_bytes();
+  *used = *total - alloc_.total_free_bytes();
+}
+
+uint64_t PinnedPool::largest_free() {
+  std::lock_guard<std::mutex> g(mu_);
+  return alloc_.largest_free_bytes();
+}
+
+// ---------------------------------------------------------------------------
+// TinyLFU
+// ---------------------------------------------------------------------------
+
+TinyLfu::TinyLfu(uint64_t cache_size) : window_limit_(cache_size * 8) {
+  // Estimator::optimal_paras (cache.rs:105-122)
+  const double items = static_cast<double>(cache_size);
+  const double err = 1.0 / items;
+  const double fail = 1.0 / items;
+  slots_ = std::max<uint64_t>(static_cast<uint64_t>(std::ceil(M_E / err)), 16);
+  const uint64_t hashes = std::max<uint64_t>(static_cast<uint64_t>(std::ceil(std::log(fail) / std::log(0.5))), 2);
+  rows_.resize(hashes);
+  for (auto& r : rows_) {
+    std::vector<std::atomic<uint8_t>> v(slots_);
+    for (auto& c : v) c.store(0, std::memory_order_relaxed);
+    r.swap(v);
+  }
+}
+
+uint8_t TinyLfu::get(const BlockKey& k) const {
+  const uint64_t h = fnv1a(k.ns, k.hash);
+  uint8_t m = 255;
+  for (size_t r = 0; r < rows_.size(); ++r) {
+    const uint64_t idx = splitmix64(h ^ (0x51ed2701ull * (r + 1))) % slots_;
+    m = std::min<uint8_t>(m, rows_[r][idx].load(std::memory_order_relaxed));
+  }
+  return m;
+}
+
+uint8_t TinyLfu::incr(const BlockKey& k) {
+  // TinyLfu::incr (cache.rs:217-224): age every window_limit increments.
+  const uint64_t w = window_.fetch_add(1, std::memory_order_relaxed);
+  if (w == window_limit_ || w > window_limit_ * 2) {
+    window_.store(0, std::memory_order_relaxed);
+    age();
+  }
+  const uint64_t h = fnv1a(k.ns, k.hash);
+  uint8_t m = 255;
+  for (size_t r = 0; r < rows_.size(); ++r) {
+    const uint64_t idx = splitmix64(h ^ (0x51ed2701ull * (r + 1))) % slots_;
+    auto& c = rows_[r][idx];
+    uint8_t cur = c.load(std::memory_order_relaxed);
+    uint8_t nv = cur;
+    while (cur != 255) {  // saturating increment (cache.rs:185-204)
+      nv = static_cast<uint8_t>(cur + 1);
+      if (c.compare_exchange_weak(cur, nv, std::memory_order_acquire, std::memory_order_relaxed)) break;
+      nv = cur;
+    }
+    if (cur == 255) nv = 255;
+    m = std::min(m, nv);
+  }
+  return m;
+}
+
+void TinyLfu::age() {
+  for (auto& r : rows_) {
+    for (auto& c : r) c.store(static_cast<uint8_t>(c.load(std::memory_order_relaxed) >> 1), std::memory_order_relaxed);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Storage
+// ---------------------------------------------------------------------------
+
+Storage::Storage(std::shared_ptr<PinnedPool> pool, const StorageConfig& cfg) : pool_(std::move(pool)), cfg_(cfg) {
+  if (cfg_.enable_lfu_admission) {
+    const uint64_t per_value = cfg_.hint_value_size_bytes ? cfg_.hint_value_size_bytes : kDefaultBytesPerValue;
+    const uint64_t items = std::max<uint64_t>(1, cfg_.capacity_bytes / per_value);  // cache.rs:39-42
+    lfu_ = std::make_unique<TinyLfu>(items);
+  }
+  if (cfg_.pre_evict_enabled) pre_evict_ = std::thread([this] { pre_evict_loop(); });
+}
+
+Storage::~Storage() {
+  {
+    std::lock_guard<std::mutex> g(stop_mu_);
+    stop_ = true;
+  }
+  stop_cv_.notify_all();
+  if (pre_evict_.joinable()) pre_evict_.join();
+}
+
+std::shared_ptr<PoolAllocation> Storage::allocate(uint64_t size) {
+  // The allocator succeeds exactly when its largest-free report covers the
+  // request, so the retry below is taken at most once per reclaim that freed
+  // something; a retry that frees nothing ends the loop (the reference would
+  // spin if the allocator ran out of nodes).
+  for (;;) {
+    if (auto a = pool_->allocate(size)) return a;
+    uint64_t freed = 0;
+    reclaim_until_fits(size, &freed);
+    if (pool_->largest_free() >= size && freed > 0) continue;
+    if (pool_->largest_free() >= size) {
+      if (auto a = pool_->allocate(size)) return a;
+    }
+    counters_.pool_alloc_failures.fetch_add(1);
+    return nullptr;
+  }
+}
+
+void Storage::reclaim_until_fits(uint64_t required, uint64_t* freed_blocks) {
+  // reclaim_until_allocator_can_allocate (storage.rs:565-608)
+  *freed_blocks = 0;
+  if (required == 0) return;
+  while (pool_->largest_free() < required) {
+    std::vector<SealedBlockPtr> evicted;
+    {
+      std::lock_guard<std::mutex> g(cache_mu_);
+      for (uint64_t i = 0; i < kReclaimBatch && !lru_.empty(); ++i) {
+        evicted.push_back(std::move(lru_.front().second));
+        index_.erase(lru_.front().first);
+        lru_.pop_front();
+      }
+    }
+    if (evicted.empty()) break;
+    *freed_blocks += evicted.size();
+    counters_.evictions.fetch_add(evicted.size());
+    evicted.clear();  // drop outside the cache lock: frees pool memory
+  }
+}
+
+void Storage::pre_evict_loop() {
+  // pre_evict_monitor (storage.rs:646-686)
+  std::unique_lock<std::mutex> lk(stop_mu_);
+  while (!stop_) {
+    stop_cv_.wait_for(lk, std::chrono::milliseconds(cfg_.pre_evict_interval_ms));
+    if (stop_) break;
+    lk.unlock();
+    uint64_t used = 0, total = 0;
+    pool_->usage(&used, &total);
+    const uint64_t free_bytes = total > used ? total - used : 0;
+    if (free_bytes < cfg_.pre_evict_threshold_bytes) {
+      const uint64_t need = cfg_.pre_evict_target_bytes > free_bytes ? cfg_.pre_evict_target_bytes - free_bytes : 0;
+      std::vector<SealedBlockPtr> evicted;
+      uint64_t freed = 0;
+      {
+        std::lock_guard<std::mutex> g(cache_mu_);
+        while (freed < need && !lru_.empty()) {
+          freed += lru_.front().second->footprint;
+          evicted.push_back(std::move(lru_.front().second));
+          index_.erase(lru_.front().first);
+          lru_.pop_front();
+        }
+      }
+      counters_.evictions.fetch_add(evicted.size());
+      evicted.clear();
+    }
+    lk.lock();
+  }
+}
+
+bool Storage::inflight_has_slot(const std::string& ns, const std::string& hash, uint64_t slot) {
+  std::lock_guard<std::mutex> g(inflight_mu_);
+  auto it = inflight_.find(BlockKey{ns, hash});
+  if (it == inflight_.end()) return false;
+  return slot < it->second.slots.size() && it->second.slots[slot] != nullptr;
+}
+
+bool Storage::cache_insert_locked(const BlockKey& key, SealedBlockPtr block) {
+  // TinyLfuCache::insert (cache.rs:66-90)
+  if (lfu_) lfu_->incr(key);
+  auto it = index_.find(key);
+  if (it != index_.end()) {
+    it->second->second = std::move(block);
+    lru_.splice(lru_.end(), lru_, it->second);
+    return true;
+  }
+  if (lfu_ && !lru_.empty()) {
+    if (lfu_->get(key) < lfu_->get(lru_.front().first)) return false;
+  }
+  lru_.emplace_back(key, std::move(block));
+  index_[key] = std::prev(lru_.end());
+  return true;
+}
+
+bool Storage::insert_slot(const std::string& ns, const std::string& hash, uint64_t slot, LayerBlockPtr block,
+                          uint64_t total_slots) {
+  BlockKey key{ns, hash};
+  {
+    std::lock_guard<std::mutex> g(cache_mu_);
+    if (index_.count(key)) return false;
+  }
+  SealedBlockPtr sealed;
+  {
+    std::lock_guard<std::mutex> g(inflight_mu_);
+    auto it = inflight_.find(key);
+    if (it == inflight_.end()) {
+      Inflight fresh;
+      fresh.slots.assign(total_slots, nullptr);
+      fresh.remaining = total_slots;
+      fresh.total_slots = total_slots;
+      it = inflight_.emplace(key, std::move(fresh)).first;
+    }
+    Inflight& ib = it->second;
+    if (slot < ib.slots.size() && ib.slots[slot]) return false;
+    // InflightBlock::insert_slot (storage.rs:161-193)
+    if (total_slots != ib.total_slots) {
+      throw storage_error("slot count mismatch: expected " + std::to_string(ib.total_slots) + ", got " +
+                          std::to_string(total_slots));
+    }
+    if (slot >= ib.total_slots) {
+      throw storage_error("slot_id " + std::to_string(slot) + " out of bounds (" + std::to_string(ib.total_slots) +
+                          " slots)");
+    }
+    ib.footprint += block->size;
+    ib.slots[slot] = std::move(block);
+    ib.remaining -= 1;
+    if (ib.remaining == 0) {
+      sealed = std::make_shared<SealedBlock>();
+      sealed->slots = std::move(ib.slots);
+      sealed->footprint = ib.footprint;
+      inflight_.erase(it);
+    }
+  }
+  if (sealed) {
+    std::lock_guard<std::mutex> g(cache_mu_);
+    if (cache_insert_locked(key, std::move(sealed))) {
+      counters_.insertions.fetch_add(1);
+    } else {
+      counters_.admission_rejections.fetch_add(1);
+    }
+  }
+  return true;
+}
+
+bool Storage::cache_contains(const std::string& ns, const std::string& hash) {
+  std::lock_guard<std::mutex> g(cache_mu_);
+  return index_.count(BlockKey{ns, hash}) != 0;
+}
+
+std::vector<SealedBlockPtr> Storage::cache_lookup_many(const std::string& ns, const std::vector<std::string>& hashes) {
+  std::vector<SealedBlockPtr> out;
+  out.reserve(hashes.size());
+  std::lock_guard<std::mutex> g(cache_mu_);
+  for (size_t i = 0; i < hashes.size(); ++i) {
+    BlockKey key{ns, hashes[i]};
+    auto it = index_.find(key);
+    if (it == index_.end()) {
+      throw storage_error("missing KV block hash at index " + std::to_string(i) + " (namespace=" + ns +
+                          ", hash_len=" + std::to_string(hashes[i].size()) + ")");
+    }
+    lru_.splice(lru_.end(), lru_, it->second);  // LruCache::get moves to MRU
+    if (lfu_) lfu_->incr(key);
+    out.push_back(it->second->second);
+  }
+  return out;
+}
+
+SealedBlockPtr Storage::cache_peek(const std::string& ns, const std::string& hash) {
+  std::lock_guard<std::mutex> g(cache_mu_);
+  auto it = index_.find(BlockKey{ns, hash});
+  return it == index_.end() ? nullptr : it->second->second;
+}
+
+uint64_t Storage::inflight_count() {
+  std::lock_guard<std::mutex> g(inflight_mu_);
+  return inflight_.size();
+}
+
+uint64_t Storage::cached_count() {
+  std::lock_guard<std::mutex> g(cache_mu_);
+  return lru_.size();
+}
+
+}  // namespace pf

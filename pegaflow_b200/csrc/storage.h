@@ -1,0 +1,168 @@
+// Pinned pool + block store (pegaflow-core/src/pinned_pool.rs, storage.rs, cache.rs).
+//
+// Lifecycle of a block (storage.rs:1-13): allocate -> write (inflight, one
+// slot per (layer, tp_rank)) -> seal when every slot is filled -> cache
+// (read-only, LRU with optional TinyLFU admission) -> evict. Sealing is a
+// one-way gate. Pool memory is reference counted: a LayerBlock keeps its
+// allocation alive, and an allocation is returned to the pool when the last
+// LayerBlock sharing it is dropped.
+#pragma once
+
+#include <atomic>
+#include <condition_variable>
+#include <cstdint>
+#include <list>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "offset_allocator.h"
+#include "pinned.h"
+
+namespace pf {
+
+class PinnedPool;
+
+// RAII pool allocation (PinnedAllocation, pinned_pool.rs:16-52).
+struct PoolAllocation {
+  std::shared_ptr<PinnedPool> pool;
+  ScaledOffsetAllocator::Allocation a;
+  uint8_t* ptr;
+  ~PoolAllocation();
+};
+
+class PinnedPool : public std::enable_shared_from_this<PinnedPool> {
+ public:
+  // PinnedMemoryPool::new (pinned_pool.rs:67-113). The allocator unit is
+  // max(reference unit, 64 B) so every allocation starts 64-byte aligned.
+  static std::shared_ptr<PinnedPool> create(uint64_t bytes, PinKind kind, bool write_combined,
+                                            uint64_t unit_hint);
+  std::shared_ptr<PoolAllocation> allocate(uint64_t size);  // null when it cannot fit
+  void usage(uint64_t* used, uint64_t* total);
+  uint64_t largest_free();
+  uint8_t* base() const { return mem_->data(); }
+  PinKind kind() const { return mem_->kind(); }
+  void free_internal(const ScaledOffsetAllocator::Allocation& a);
+
+ private:
+  PinnedPool(std::unique_ptr<PinnedMemory> mem, ScaledOffsetAllocator alloc)
+      : mem_(std::move(mem)), alloc_(std::move(alloc)) {}
+  std::unique_ptr<PinnedMemory> mem_;
+  std::mutex mu_;
+  ScaledOffsetAllocator alloc_;
+};
+
+// Host bytes of one (block, slot) (LayerBlock, storage.rs:249-310).
+struct LayerBlock {
+  uint8_t* k_ptr;
+  uint8_t* v_ptr;  // null for contiguous blocks
+  uint64_t size;   // block_size_bytes (memory_footprint)
+  std::shared_ptr<PoolAllocation> k_alloc;
+  std::shared_ptr<PoolAllocation> v_alloc;
+};
+using LayerBlockPtr = std::shared_ptr<LayerBlock>;
+
+struct SealedBlock {
+  std::vector<LayerBlockPtr> slots;
+  uint64_t footprint = 0;
+};
+using SealedBlockPtr = std::shared_ptr<SealedBlock>;
+
+struct BlockKey {
+  std::string ns;
+  std::string hash;
+  bool operator==(const BlockKey& o) const { return ns == o.ns && hash == o.hash; }
+};
+struct BlockKeyHash {
+  size_t operator()(const BlockKey& k) const;
+};
+
+struct StorageConfig {
+  bool enable_lfu_admission = true;
+  uint64_t capacity_bytes = 0;
+  uint64_t hint_value_size_bytes = 0;
+  bool pre_evict_enabled = false;
+  uint64_t pre_evict_threshold_bytes = 5ull << 30;  // storage.rs:35
+  uint64_t pre_evict_target_bytes = 8ull << 30;     // storage.rs:37
+  uint64_t pre_evict_interval_ms = 100;             // storage.rs:39
+};
+
+struct StorageCounters {
+  std::atomic<uint64_t> insertions{0};
+  std::atomic<uint64_t> admission_rejections{0};
+  std::atomic<uint64_t> evictions{0};
+  std::atomic<uint64_t> pool_alloc_failures{0};
+};
+
+// Count-min-sketch TinyLFU (cache.rs:99-243), deterministic hashing.
+class TinyLfu {
+ public:
+  explicit TinyLfu(uint64_t cache_size);
+  uint8_t get(const BlockKey& k) const;
+  uint8_t incr(const BlockKey& k);
+
+ private:
+  void age();
+  uint64_t slots_;
+  std::vector<std::vector<std::atomic<uint8_t>>> rows_;
+  std::atomic<uint64_t> window_{0};
+  uint64_t window_limit_;
+};
+
+class Storage {
+ public:
+  Storage(std::shared_ptr<PinnedPool> pool, const StorageConfig& cfg);
+  ~Storage();
+
+  // StorageEngine::allocate (storage.rs:405-433): evicts LRU blocks until the
+  // allocator reports a large enough free region.
+  std::shared_ptr<PoolAllocation> allocate(uint64_t size);
+  bool inflight_has_slot(const std::string& ns, const std::string& hash, uint64_t slot);
+  // StorageEngine::insert_slot (storage.rs:457-514). Throws pf::Error(Storage)
+  // on SlotOutOfBounds / SlotCountMismatch.
+  bool insert_slot(const std::string& ns, const std::string& hash, uint64_t slot, LayerBlockPtr block,
+                   uint64_t total_slots);
+  bool cache_contains(const std::string& ns, const std::string& hash);
+  // cache_lookup_many (storage.rs:529-547): bumps recency/frequency.
+  std::vector<SealedBlockPtr> cache_lookup_many(const std::string& ns, const std::vector<std::string>& hashes);
+  // Read-only peek (no LRU/frequency update), for introspection.
+  SealedBlockPtr cache_peek(const std::string& ns, const std::string& hash);
+
+  uint64_t inflight_count();
+  uint64_t cached_count();
+  StorageCounters& counters() { return counters_; }
+  PinnedPool& pool() { return *pool_; }
+
+ private:
+  bool cache_insert_locked(const BlockKey& key, SealedBlockPtr block);  // TinyLFU admission
+  void reclaim_until_fits(uint64_t required, uint64_t* freed_blocks);
+  void pre_evict_loop();
+
+  struct Inflight {
+    std::vector<LayerBlockPtr> slots;
+    uint64_t remaining;
+    uint64_t total_slots;
+    uint64_t footprint = 0;
+  };
+  using LruList = std::list<std::pair<BlockKey, SealedBlockPtr>>;
+
+  std::shared_ptr<PinnedPool> pool_;
+  StorageConfig cfg_;
+  std::mutex inflight_mu_;
+  std::unordered_map<BlockKey, Inflight, BlockKeyHash> inflight_;
+  std::mutex cache_mu_;
+  LruList lru_;  // front = least recently used
+  std::unordered_map<BlockKey, LruList::iterator, BlockKeyHash> index_;
+  std::unique_ptr<TinyLfu> lfu_;
+  StorageCounters counters_;
+
+  std::thread pre_evict_;
+  std::mutex stop_mu_;
+  std::condition_variable stop_cv_;
+  bool stop_ = false;
+};
+
+}  // namespace pf

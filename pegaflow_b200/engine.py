@@ -1,0 +1,274 @@
+"""In-process engine and load-state classes with the reference's Python surface.
+
+``PegaEngine`` and ``PyLoadState`` keep the names, argument order and error
+behaviour (``RuntimeError`` carrying the engine's message) of the PyO3 classes
+in python/src/lib.rs:89-261 and :539-574. ``PegaEngine`` adds the save calls
+of the core engine (pegaflow-core/src/lib.rs:497-550), which the reference only
+reaches through its gRPC server.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, byref, c_char_p, c_int32, c_uint8, c_uint64, c_void_p
+from typing import Iterable, Optional, Sequence
+
+from . import _native as N
+from .transfer import Executor
+
+DEFAULT_POOL_BYTES = 30 * 1024 * 1024 * 1024  # pegaflow-core/src/lib.rs:56
+
+
+def _ids(block_ids: Sequence[int]):
+    arr = (c_int32 * max(1, len(block_ids)))(*block_ids)
+    return arr
+
+
+class PegaEngine:
+    """PegaEngine (python/src/lib.rs:89-261) backed by the B200 C++ engine.
+
+    With no arguments it allocates the reference's default 30 GiB pinned pool.
+    ``pool_kind="host"`` builds the engine over plain pageable memory for
+    host-logic tests: registration, queries and bookkeeping work, transfers
+    raise.
+    """
+
+    def __init__(
+        self,
+        pool_size: int = DEFAULT_POOL_BYTES,
+        use_hugepages: bool = False,
+        *,
+        write_combined: bool = True,
+        enable_lfu_admission: bool = True,
+        hint_value_size_bytes: int = 0,
+        pre_evict: Optional[tuple[int, int, int]] = None,
+        pool_kind: str = "pinned",
+        executor: Optional[dict] = None,
+    ):
+        cfg = N.EngineConfig()
+        N.lib.pf_engine_config_default(byref(cfg))
+        cfg.pool_bytes = pool_size
+        cfg.use_hugepages = 1 if use_hugepages else 0
+        cfg.write_combined = 1 if write_combined else 0
+        cfg.enable_lfu_admission = 1 if enable_lfu_admission else 0
+        cfg.hint_value_size_bytes = hint_value_size_bytes
+        cfg.pool_kind = N.PF_POOL_HOST if pool_kind == "host" else N.PF_POOL_PINNED
+        if pre_evict is not None:
+            cfg.pre_evict_enabled = 1
+            cfg.pre_evict_threshold_bytes, cfg.pre_evict_target_bytes, cfg.pre_evict_interval_ms = pre_evict
+        if executor:
+            modes = {"auto": N.PF_MODE_AUTO, "staged": N.PF_MODE_STAGED, "direct": N.PF_MODE_DIRECT}
+            for k, v in executor.items():
+                setattr(cfg.executor, k, modes[v] if k.endswith("_mode") else v)
+        h = c_void_p()
+        N.check(N.lib.pf_engine_create(byref(cfg), byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            N.lib.pf_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- reference PyO3 surface ------------------------------------------------
+
+    def register_context_layer(
+        self,
+        instance_id: str,
+        namespace: str,
+        device_id: int,
+        layer_name: str,
+        data_ptr: int,
+        size_bytes: int,
+        num_blocks: int,
+        bytes_per_block: int,
+        kv_stride_bytes: int,
+        segments: int,
+        tp_rank: int,
+        tp_size: int,
+        num_layers: int,
+    ) -> None:
+        N.check(
+            N.lib.pf_engine_register_context_layer(
+                self._h,
+                instance_id.encode(),
+                namespace.encode(),
+                device_id,
+                layer_name.encode(),
+                data_ptr,
+                size_bytes,
+                num_blocks,
+                bytes_per_block,
+                kv_stride_bytes,
+                segments,
+                tp_rank,
+                tp_size,
+                num_layers,
+            )
+        )
+
+    def unregister_instance(self, instance_id: str) -> None:
+        N.check(N.lib.pf_engine_unregister_instance(self._h, instance_id.encode()))
+
+    def count_prefix_hit_blocks(self, instance_id: str, block_hashes: Sequence[bytes]) -> int:
+        arr, keep = N.bytes_array(block_hashes)
+        out = c_uint64()
+        N.check(N.lib.pf_engine_count_prefix_hit_blocks(self._h, instance_id.encode(), arr, len(block_hashes), byref(out)))
+        del keep
+        return out.value
+
+    def batch_load_kv_blocks(
+        self,
+        instance_id: str,
+        tp_rank: int,
+        device_id: int,
+        load_state_shm: str,
+        layer_names: Sequence[str],
+        block_ids: Sequence[int],
+        block_hashes: Sequence[bytes],
+    ) -> None:
+        names = (c_char_p * max(1, len(layer_names)))(*[n.encode() for n in layer_names])
+        ids = _ids(block_ids)
+        arr, keep = N.bytes_array(block_hashes)
+        N.check(
+            N.lib.pf_engine_batch_load_kv_blocks(
+                self._h,
+                instance_id.encode(),
+                tp_rank,
+                device_id,
+                load_state_shm.encode(),
+                names,
+                len(layer_names),
+                ids,
+                arr,
+                len(block_hashes),
+            )
+        )
+        del keep
+
+    # -- core engine calls the reference exposes through its server ------------
+
+    def batch_save_kv_blocks(
+        self,
+        instance_id: str,
+        tp_rank: int,
+        device_id: int,
+        saves: Iterable[tuple[str, Sequence[int], Sequence[bytes]]],
+    ) -> None:
+        """PegaEngine::batch_save_kv_blocks_from_ipc (pegaflow-core/src/lib.rs:497-520)."""
+        saves = list(saves)
+        entries = (N.SaveEntry * max(1, len(saves)))()
+        keep = []
+        for i, (layer, ids, hashes) in enumerate(saves):
+            name = layer.encode()
+            id_arr = _ids(list(ids))
+            h_arr, hk = N.bytes_array(list(hashes))
+            keep += [name, id_arr, h_arr, hk]
+            entries[i].layer_name = name
+            entries[i].block_ids = ctypes.cast(id_arr, POINTER(c_int32))
+            entries[i].block_hashes = ctypes.cast(h_arr, POINTER(N.Bytes))
+            entries[i].n = len(ids)
+            if len(ids) != len(hashes):
+                # Preserve the reference's length check (lib.rs:563-569).
+                entries[i].n = min(len(ids), len(hashes))
+                raise RuntimeError(
+                    f"invalid argument: block_ids length {len(ids)} does not match block_hashes {len(hashes)}"
+                )
+        N.check(N.lib.pf_engine_batch_save_kv_blocks(self._h, instance_id.encode(), tp_rank, device_id, entries, len(saves)))
+        del keep
+
+    def save_kv_blocks(
+        self,
+        instance_id: str,
+        tp_rank: int,
+        device_id: int,
+        layer_name: str,
+        block_ids: Sequence[int],
+        block_hashes: Sequence[bytes],
+    ) -> None:
+        """PegaEngine::save_kv_blocks_from_ipc (pegaflow-core/src/lib.rs:528-550)."""
+        self.batch_save_kv_blocks(instance_id, tp_rank, device_id, [(layer_name, block_ids, block_hashes)])
+
+    # -- extras -----------------------------------------------------------------
+
+    def wait_loads(self, device_id: int, timeout_s: float = 60.0) -> None:
+        N.check(N.lib.pf_engine_wait_loads(self._h, device_id, timeout_s))
+
+    def pool_usage(self) -> tuple[int, int, int]:
+        used, total, largest = c_uint64(), c_uint64(), c_uint64()
+        N.check(N.lib.pf_engine_pool_usage(self._h, byref(used), byref(total), byref(largest)))
+        return used.value, total.value, largest.value
+
+    def slot_info(self, namespace: str, block_hash: bytes, slot: int) -> tuple[int, int, int]:
+        """(k_ptr, v_ptr, size) of a sealed block's slot; v_ptr 0 when contiguous."""
+        buf = (c_uint8 * max(1, len(block_hash))).from_buffer_copy(block_hash or b"\0")
+        k, v, s = c_uint64(), c_uint64(), c_uint64()
+        N.check(
+            N.lib.pf_engine_slot_info(
+                self._h, namespace.encode(), buf, len(block_hash), slot, byref(k), byref(v), byref(s)
+            )
+        )
+        return k.value, v.value, s.value
+
+    def metrics(self) -> dict:
+        m = N.EngineMetrics()
+        N.check(N.lib.pf_engine_metrics_get(self._h, byref(m)))
+        return {f: getattr(m, f) for f, _ in N.EngineMetrics._fields_}
+
+    def executor(self, device_id: int) -> Executor:
+        h = c_void_p()
+        N.check(N.lib.pf_engine_executor(self._h, device_id, byref(h)))
+        return Executor(device_id, _handle=h.value)
+
+
+class PyLoadState:
+    """Batch-level load completion flag in shared memory (python/src/lib.rs:539-574).
+
+    State values: 0 pending, 1 success, <0 error. The creating object owns the
+    shared-memory object and unlinks it when closed or collected.
+    """
+
+    def __init__(self):
+        h = c_void_p()
+        N.check(N.lib.pf_load_state_create(byref(h)))
+        self._h = h
+
+    @classmethod
+    def attach(cls, shm_name: str) -> "PyLoadState":
+        """LoadState::attach (pegaflow-core/src/sync_state.rs:145-155); does not own the object."""
+        self = cls.__new__(cls)
+        h = c_void_p()
+        N.check(N.lib.pf_load_state_attach(shm_name.encode(), byref(h)))
+        self._h = h
+        return self
+
+    def shm_name(self) -> str:
+        return N.lib.pf_load_state_name(self._h).decode()
+
+    def get_state(self) -> int:
+        return int(N.lib.pf_load_state_get(self._h))
+
+    def is_ready(self) -> bool:
+        return self.get_state() != 0
+
+    def set_completed(self) -> None:
+        N.lib.pf_load_state_set_completed(self._h)
+
+    def set_error(self) -> None:
+        N.lib.pf_load_state_set_error(self._h)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            N.lib.pf_load_state_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

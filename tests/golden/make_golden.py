@@ -1,0 +1,191 @@
+"""Generate golden fixtures from the reference's own Python connector code.
+
+Runs the reference's vLLM worker connector (python/pegaflow/connector/worker.py
+in the xiaguan/pegaflow tree) with its Rust extension and CUDA IPC wrapper
+replaced by recording stubs, and records what it sends to the engine:
+
+  * registration.json — register_context(...) arguments the worker derives
+    from KV tensors of the benchmark shapes (worker.py:80-146);
+  * save_batches.json — the (layer, block_ids, block_hashes) list one save
+    RPC carries for a batch of per-layer save tasks (worker.py:372-427);
+  * load_requests.json — the load RPC arguments of start_load_kv
+    (worker.py:217-286).
+
+Usage (needs the reference tree; not run by the test suite):
+    python tests/golden/make_golden.py /path/to/pegaflow
+"""
+
+from __future__ import annotations
+
+import json
+import sys
+import types
+from pathlib import Path
+
+import torch
+
+OUT = Path(__file__).resolve().parent
+
+
+class _Recorder:
+    calls: list = []
+
+
+class FakeEngineRpcClient:
+    def __init__(self, endpoint=None):
+        self.endpoint = endpoint
+
+    def register_context(self, *args):
+        _Recorder.calls.append(("register_context", args))
+        return True, ""
+
+    def save(self, *args):
+        _Recorder.calls.append(("save", args))
+        return True, ""
+
+    def load(self, *args):
+        _Recorder.calls.append(("load", args))
+        return True, ""
+
+    def query(self, *args):
+        return {"ok": True, "message": "", "hit_blocks": 0, "prefetch_state": "ready", "loading_blocks": 0,
+                "missing_blocks": 0}
+
+    def unregister_context(self, *args):
+        return True, ""
+
+
+class FakeLoadState:
+    def shm_name(self):
+        return "pega_load_golden"
+
+    def get_state(self):
+        return 0
+
+    def is_ready(self):
+        return False
+
+
+class CudaIPCWrapper:  # picklable stand-in for pegaflow.ipc_wrapper.CudaIPCWrapper
+    def __init__(self, tensor):
+        self.shape = tuple(tensor.shape)
+
+
+def install_stubs(ref_python: Path) -> None:
+    ext = types.ModuleType("pegaflow.pegaflow")
+    ext.EngineRpcClient = FakeEngineRpcClient
+    ext.PegaEngine = None
+    ext.PyLoadState = FakeLoadState
+    sys.modules["pegaflow.pegaflow"] = ext
+    ipc = types.ModuleType("pegaflow.ipc_wrapper")
+    CudaIPCWrapper.__module__ = "pegaflow.ipc_wrapper"
+    ipc.CudaIPCWrapper = CudaIPCWrapper
+    sys.modules["pegaflow.ipc_wrapper"] = ipc
+    sys.path.insert(0, str(ref_python))
+    torch.cuda.synchronize = lambda *a, **k: None  # CPU-only generation
+
+
+# (name, shape, dtype) — the BASELINE.json config shapes, plus layout edge cases.
+CASES = [
+    ("gpt2_k_separate", (256, 16, 12, 64), torch.float16),
+    ("gpt2_kv_first", (2, 256, 16, 12, 64), torch.float16),
+    ("llama8b_kv_first", (2, 8192, 16, 8, 128), torch.bfloat16),
+    ("llama8b_blocks_first", (8192, 2, 16, 8, 128), torch.bfloat16),
+    ("qwen3_8b_kv_first", (2, 2048, 16, 8, 128), torch.bfloat16),
+    ("llama70b_tp8_kv_first", (2, 4096, 16, 1, 128), torch.bfloat16),
+    ("llama70b_tp2_kv_first", (2, 4096, 16, 4, 128), torch.bfloat16),
+    ("llama8b_fp8_kv_first", (2, 4096, 16, 8, 128), torch.uint8),
+    ("fp32_scale_per_block", (4096,), torch.float32),
+    ("two_blocks_ambiguous", (2, 2, 16, 8, 128), torch.bfloat16),
+]
+
+
+def main(argv: list[str]) -> int:
+    ref_root = Path(argv[1] if len(argv) > 1 else "/root/reference")
+    install_stubs(ref_root / "python")
+    from pegaflow.connector.common import ConnectorContext, LoadIntent, PegaConnectorMetadata, SaveIntent
+    from pegaflow.connector.worker import SaveTask, WorkerConnector
+
+    # ---- registration -------------------------------------------------------
+    reg_out = []
+    for name, shape, dtype in CASES:
+        ctx = ConnectorContext("inst", "ns", 16, 1, 1, 0, 0, FakeEngineRpcClient())
+        w = WorkerConnector(ctx)
+        t = torch.empty(shape, dtype=dtype, device="meta")
+        _Recorder.calls = []
+        w.register_kv_caches({name: t})
+        (_, args), = _Recorder.calls
+        (instance_id, namespace, tp_rank, tp_size, device_id, num_layers, layer_name, _wrapper,
+         num_blocks, bytes_per_block, kv_stride_bytes, segments) = args
+        reg_out.append({
+            "case": name, "shape": list(shape), "stride": list(t.stride()), "element_size": t.element_size(),
+            "num_blocks": num_blocks, "bytes_per_block": bytes_per_block, "kv_stride_bytes": kv_stride_bytes,
+            "segments": segments,
+        })
+        w._save_queue.put(None)
+        w._save_thread.join()
+    (OUT / "registration.json").write_text(json.dumps(reg_out, indent=1) + "\n")
+
+    # ---- save batching ------------------------------------------------------
+    ctx = ConnectorContext("inst", "ns", 16, 3, 1, 0, 0, FakeEngineRpcClient())
+    w = WorkerConnector(ctx)
+    meta = PegaConnectorMetadata(save_intents={
+        "reqA": SaveIntent(block_ids=(5, 9, 2), block_hashes=(b"hA0", b"hA1", b"hA2")),
+        "reqB": SaveIntent(block_ids=(), block_hashes=()),
+        "reqC": SaveIntent(block_ids=(7, -1), block_hashes=(b"hC0", b"hC1")),
+    })
+    attn = types.SimpleNamespace(block_table=object())
+    no_table = types.SimpleNamespace(block_table=None)
+    tasks = [
+        SaveTask("layer.0", attn, meta, ["reqA", "reqB", "reqC"]),
+        SaveTask("layer.1", attn, meta, ["reqA", "reqB", "reqC"]),
+        SaveTask("layer.2", no_table, meta, ["reqA", "reqB", "reqC"]),
+        SaveTask("layer.0", attn, meta, ["reqA"]),
+    ]
+    _Recorder.calls = []
+    w._process_save_batch(tasks)
+    saves = [a for n, a in _Recorder.calls if n == "save"]
+    save_out = {
+        "tasks": [{"layer": t.layer_name, "has_block_table": t.attn_metadata.block_table is not None} for t in tasks],
+        "save_intents": {k: {"block_ids": list(v.block_ids), "block_hashes": [h.hex() for h in v.block_hashes]}
+                         for k, v in meta.save_intents.items()},
+        "rpc": [{"instance_id": a[0], "tp_rank": a[1], "device_id": a[2],
+                 "saves": [[ln, list(ids), [h.hex() for h in hs]] for ln, ids, hs in a[3]]} for a in saves],
+    }
+    (OUT / "save_batches.json").write_text(json.dumps(save_out, indent=1) + "\n")
+    w._save_queue.put(None)
+    w._save_thread.join()
+
+    # ---- load request -------------------------------------------------------
+    w = WorkerConnector(ctx)
+    meta = PegaConnectorMetadata(
+        load_intents={
+            "r1": LoadIntent(block_ids=(3, 4, 5), block_hashes=(b"a", b"b", b"c"), num_tokens=48),
+            "r2": LoadIntent(block_ids=(11,), block_hashes=(b"z",), num_tokens=16),
+        },
+        save_intents={"r3": SaveIntent(block_ids=(1,), block_hashes=(b"q",))},
+    )
+    layers = {"model.layers.0.attn": types.SimpleNamespace(kv_cache=[None]),
+              "model.layers.0.mlp": types.SimpleNamespace(),
+              "model.layers.1.attn": types.SimpleNamespace(kv_cache=[None])}
+    fwd = types.SimpleNamespace(no_compile_layers=layers)
+    _Recorder.calls = []
+    w.start_load_kv(meta, fwd)
+    loads = [a for n, a in _Recorder.calls if n == "load"]
+    load_out = {
+        "load_intents": {k: {"block_ids": list(v.block_ids), "block_hashes": [h.hex() for h in v.block_hashes]}
+                         for k, v in meta.load_intents.items()},
+        "layers": {k: hasattr(v, "kv_cache") for k, v in layers.items()},
+        "rpc": [{"instance_id": a[0], "tp_rank": a[1], "device_id": a[2], "load_state_shm": a[3],
+                 "layer_names": list(a[4]), "block_ids": list(a[5]), "block_hashes": [h.hex() for h in a[6]]}
+                for a in loads],
+    }
+    (OUT / "load_requests.json").write_text(json.dumps(load_out, indent=1) + "\n")
+    w._save_queue.put(None)
+    w._save_thread.join()
+    print("wrote", [p.name for p in sorted(OUT.glob("*.json"))])
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main(sys.argv))
