@@ -315,8 +315,11 @@ def main() -> int:
     ap.add_argument("--no-refcopy", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling runs)")
     args = ap.parse_args()
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.layers:
+        wl["layers"] = args.layers
     args.warmup = max(args.warmup, 0)
 
     if args.impl == "reference":

@@ -89,8 +89,8 @@ typedef enum pf_transfer_mode {
 } pf_transfer_mode;
 
 typedef struct pf_executor_config {
-  uint64_t staging_chunk_bytes; /* 0 = default (16 MiB) */
-  uint32_t staging_slots;       /* 0 = default (4) */
+  uint64_t staging_chunk_bytes; /* 0 = default (64 MiB) */
+  uint32_t staging_slots;       /* 0 = default (3) */
   uint32_t save_mode;           /* pf_transfer_mode */
   uint32_t load_mode;           /* pf_transfer_mode */
   uint32_t ctas_per_sm;         /* 0 = default */
@@ -286,12 +286,16 @@ int pf_engine_register_context_layer(
 int pf_engine_unregister_instance(pf_engine* e, const char* instance_id);
 
 /* One (layer_name, block_ids, block_hashes) entry of a batch save
- * (lib.rs:502; engine.proto SaveLayer). */
+ * (lib.rs:502; engine.proto SaveLayer). The two lists carry their own
+ * lengths; an entry whose lengths differ fails with the reference's
+ * "block_ids length .. does not match block_hashes .." after the entries
+ * before it have been saved (lib.rs:563-569). */
 typedef struct pf_save_entry {
   const char* layer_name;
   const int32_t* block_ids;
+  uint64_t n_ids;
   const pf_bytes* block_hashes;
-  uint64_t n;
+  uint64_t n_hashes;
 } pf_save_entry;
 
 /* PegaEngine::batch_save_kv_blocks_from_ipc (lib.rs:497-520). Blocking. */

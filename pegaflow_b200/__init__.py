@@ -3,33 +3,36 @@
 Public surface (mirrors the reference's ``pegaflow.pegaflow`` module):
   PegaEngine, PyLoadState        in-process engine + shm load flag
   Executor, Layout, SaveSpec ... transfer executor (C ABI pf_executor_*)
+
+The native library is loaded on first use of any of these names, so
+``pegaflow_b200.build`` can run before the library exists. A missing or
+broken library raises ImportError at that first use; there is no fallback.
 """
 
-from ._native import PegaError, LIB_PATH  # noqa: F401  (loads the native library)
-from .engine import PegaEngine, PyLoadState  # noqa: F401
-from .transfer import (  # noqa: F401
-    Executor,
-    Layout,
-    LoadSpec,
-    PinnedBuffer,
-    SaveSpec,
-    refcopy_load,
-    refcopy_save,
-    segment_offset,
-    validate,
-)
+import importlib
 
-__all__ = [
-    "PegaEngine",
-    "PyLoadState",
-    "PegaError",
-    "Executor",
-    "Layout",
-    "LoadSpec",
-    "SaveSpec",
-    "PinnedBuffer",
-    "refcopy_save",
-    "refcopy_load",
-    "segment_offset",
-    "validate",
-]
+_EXPORTS = {
+    "PegaEngine": ".engine",
+    "PyLoadState": ".engine",
+    "PegaError": "._native",
+    "LIB_PATH": "._native",
+    "Executor": ".transfer",
+    "Layout": ".transfer",
+    "LoadSpec": ".transfer",
+    "SaveSpec": ".transfer",
+    "PinnedBuffer": ".transfer",
+    "refcopy_save": ".transfer",
+    "refcopy_load": ".transfer",
+    "segment_offset": ".transfer",
+    "validate": ".transfer",
+}
+
+__all__ = sorted(_EXPORTS)
+
+
+def __getattr__(name):
+    if name in _EXPORTS:
+        value = getattr(importlib.import_module(_EXPORTS[name], __name__), name)
+        globals()[name] = value
+        return value
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

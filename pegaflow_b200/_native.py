@@ -128,8 +128,9 @@ class SaveEntry(Structure):
     _fields_ = [
         ("layer_name", c_char_p),
         ("block_ids", POINTER(c_int32)),
+        ("n_ids", c_uint64),
         ("block_hashes", POINTER(Bytes)),
-        ("n", c_uint64),
+        ("n_hashes", c_uint64),
     ]
 
 
@@ -263,14 +264,34 @@ def check(rc: int) -> None:
         raise PegaError(rc, msg.decode("utf-8", "replace") if msg else f"pf_status {rc}")
 
 
-def bytes_array(items) -> tuple[ctypes.Array, list]:
-    """Build a pf_bytes[] over Python bytes objects; returns (array, keepalive)."""
-    keep = []
-    arr = (Bytes * max(1, len(items)))()
-    for i, b in enumerate(items):
-        b = bytes(b)
-        buf = (c_uint8 * max(1, len(b))).from_buffer_copy(b if b else b"\0")
-        keep.append(buf)
-        arr[i].data = ctypes.cast(buf, POINTER(c_uint8))
-        arr[i].len = len(b)
-    return arr, keep
+def bytes_array(items):
+    """A pf_bytes[] over a sequence of bytes-like objects, built without a
+    per-item ctypes object: the items are joined into one buffer and the
+    (pointer, length) pairs are computed with numpy. Returns (pointer,
+    keepalive); the keepalive must outlive the C call."""
+    import numpy as np
+
+    n = len(items)
+    if n == 0:
+        empty = (Bytes * 1)()
+        return ctypes.cast(empty, POINTER(Bytes)), empty
+    items = [x if isinstance(x, bytes) else bytes(x) for x in items]
+    blob = b"".join(items)
+    lens = np.fromiter(map(len, items), dtype=np.uint64, count=n)
+    buf = np.frombuffer(blob, dtype=np.uint8) if blob else np.zeros(1, np.uint8)
+    pairs = np.empty((n, 2), dtype=np.uint64)
+    pairs[0, 0] = 0
+    np.cumsum(lens[:-1], out=pairs[1:, 0])
+    pairs[:, 0] += np.uint64(buf.ctypes.data)
+    pairs[:, 1] = lens
+    return pairs.ctypes.data_as(POINTER(Bytes)), (buf, pairs, blob)
+
+
+def int32_array(values):
+    """A contiguous int32 array and its pointer (values must fit in i32)."""
+    import numpy as np
+
+    a = np.ascontiguousarray(values, dtype=np.int32)
+    if a.size == 0:
+        a = np.zeros(1, np.int32)
+    return a.ctypes.data_as(POINTER(c_int32)), a

@@ -85,8 +85,8 @@ int pf_segment_offset(const pf_layer_desc* layer, uint64_t block_idx, uint64_t s
 void pf_executor_config_default(pf_executor_config* cfg) {
   if (!cfg) return;
   std::memset(cfg, 0, sizeof(*cfg));
-  cfg->staging_chunk_bytes = 16ull << 20;
-  cfg->staging_slots = 4;
+  cfg->staging_chunk_bytes = 64ull << 20;
+  cfg->staging_slots = 3;
   cfg->save_mode = PF_MODE_AUTO;
   cfg->load_mode = PF_MODE_AUTO;
   cfg->ctas_per_sm = 4;
@@ -321,13 +321,14 @@ int pf_engine_batch_save_kv_blocks(pf_engine* e, const char* instance_id, uint64
   return guarded([&] {
     std::vector<pf::Engine::SaveEntry> entries(n_saves);
     for (uint64_t i = 0; i < n_saves; ++i) {
-      entries[i].layer_name = str(saves[i].layer_name);
-      if (saves[i].n && (!saves[i].block_ids || !saves[i].block_hashes)) {
+      const pf_save_entry& s = saves[i];
+      entries[i].layer_name = str(s.layer_name);
+      if ((s.n_ids && !s.block_ids) || (s.n_hashes && !s.block_hashes)) {
         throw pf::invalid_argument("null block_ids or block_hashes");
       }
-      entries[i].block_ids.assign(saves[i].block_ids, saves[i].block_ids + saves[i].n);
-      entries[i].hashes.reserve(saves[i].n);
-      for (uint64_t k = 0; k < saves[i].n; ++k) entries[i].hashes.push_back(bytes_str(saves[i].block_hashes[k]));
+      entries[i].block_ids.assign(s.block_ids, s.block_ids + s.n_ids);
+      entries[i].hashes.reserve(s.n_hashes);
+      for (uint64_t k = 0; k < s.n_hashes; ++k) entries[i].hashes.push_back(bytes_str(s.block_hashes[k]));
     }
     e->impl->batch_save(str(instance_id), tp_rank, device_id, entries);
   });
@@ -336,7 +337,7 @@ int pf_engine_batch_save_kv_blocks(pf_engine* e, const char* instance_id, uint64
 int pf_engine_save_kv_blocks(pf_engine* e, const char* instance_id, uint64_t tp_rank, int32_t device_id,
                              const char* layer_name, const int32_t* block_ids, const pf_bytes* block_hashes,
                              uint64_t n) {
-  pf_save_entry entry{layer_name, block_ids, block_hashes, n};
+  pf_save_entry entry{layer_name, block_ids, n, block_hashes, n};
   return pf_engine_batch_save_kv_blocks(e, instance_id, tp_rank, device_id, &entry, 1);
 }
 

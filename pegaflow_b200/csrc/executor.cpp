@@ -152,8 +152,8 @@ Executor::Executor(int device, const pf_executor_config& cfg) : device_(device),
   }
   cuda_check(cudaSetDevice(device), "cudaSetDevice");
   cuda_check(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
-  if (cfg_.staging_chunk_bytes == 0) cfg_.staging_chunk_bytes = 16ull << 20;
-  if (cfg_.staging_slots == 0) cfg_.staging_slots = 4;
+  if (cfg_.staging_chunk_bytes == 0) cfg_.staging_chunk_bytes = 64ull << 20;
+  if (cfg_.staging_slots == 0) cfg_.staging_slots = 3;
   if (cfg_.ctas_per_sm == 0) cfg_.ctas_per_sm = 4;
   if (cfg_.copy_streams == 0) cfg_.copy_streams = 2;
   if (cfg_.save_mode == PF_MODE_AUTO) cfg_.save_mode = PF_MODE_STAGED;
@@ -343,6 +343,7 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
     if (g.unit_bytes > kMaxUnitBytes) throw invalid_argument("block larger than 2 GiB");
     const bool split = is_split_layout(l);
 
+    uint64_t max_id = 0;
     for (uint64_t i = 0; i < s.n; ++i) {
       const int64_t bi = s.block_idx[i];
       if (bi < 0) throw invalid_argument("negative block index " + std::to_string(bi));
@@ -353,7 +354,60 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
       // ... plus the copy's own end (see check_unit_range).
       for (uint32_t u = 0; u < g.units; ++u) check_unit_range(l, blk, u, g);
       if (s.k_src[i] == nullptr) throw invalid_argument("null source pointer for block " + std::to_string(bi));
+      max_id = std::max(max_id, blk);
     }
+
+    // The reference copies a layer's blocks in list order on one stream, so
+    // where destinations coincide the later block wins (gpu_worker.rs:223-283).
+    // Warps run in no order, so: in layouts where every block owns its bytes,
+    // a repeated destination keeps only its last occurrence; in layouts whose
+    // blocks share bytes (several segments without the split predicate, or a
+    // K->V stride shorter than the K region) overlapping lists are copied in
+    // list order by the copy engine instead of the kernel.
+    std::vector<uint64_t> keep;
+    keep.reserve(s.n);
+    uint64_t k_region = 0;
+    const bool owns_bytes = max_id < l.num_blocks &&
+                            (split ? !mul_ovf(l.num_blocks, l.bytes_per_block, &k_region) &&
+                                         l.kv_stride_bytes >= k_region
+                                   : l.segments == 1);
+    bool serial = false;
+    if (owns_bytes) {
+      std::vector<uint64_t> seen((max_id >> 6) + 1, 0);
+      for (uint64_t i = s.n; i-- > 0;) {
+        const uint64_t blk = static_cast<uint64_t>(s.block_idx[i]);
+        if (seen[blk >> 6] & (1ull << (blk & 63))) continue;
+        seen[blk >> 6] |= 1ull << (blk & 63);
+        keep.push_back(i);
+      }
+      std::reverse(keep.begin(), keep.end());
+    } else {
+      std::vector<std::pair<uint64_t, uint64_t>> spans;  // [start, end) of every unit
+      for (uint64_t i = 0; i < s.n; ++i) {
+        const uint64_t blk = static_cast<uint64_t>(s.block_idx[i]);
+        for (uint32_t u = 0; u < g.units; ++u) {
+          const uint64_t st = blk * l.bytes_per_block + u * g.unit_stride;
+          spans.emplace_back(st, st + g.unit_bytes);
+        }
+      }
+      std::sort(spans.begin(), spans.end());
+      for (size_t j = 1; j < spans.size() && !serial; ++j) serial = spans[j].first < spans[j - 1].second;
+      for (uint64_t i = 0; i < s.n; ++i) keep.push_back(i);
+    }
+    if (serial) {
+      SerialLoad sl;
+      sl.layer = l;
+      sl.done_index = static_cast<uint32_t>(li);
+      for (uint64_t i = 0; i < s.n; ++i) {
+        sl.ids.push_back(s.block_idx[i]);
+        sl.k.push_back(reinterpret_cast<uint64_t>(s.k_src[i]));
+        const void* v = s.v_src ? s.v_src[i] : nullptr;
+        sl.v.push_back(v ? reinterpret_cast<uint64_t>(v) : reinterpret_cast<uint64_t>(s.k_src[i]) + l.bytes_per_block);
+      }
+      b->serial.push_back(std::move(sl));
+      continue;
+    }
+    const uint64_t n = keep.size();
 
     PlanLayer p{};
     p.cache_base = l.data_ptr;
@@ -361,10 +415,10 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
     p.unit_stride = g.unit_stride;
     p.unit_bytes = static_cast<uint32_t>(g.unit_bytes);
     p.units = g.units;
-    p.n = static_cast<uint32_t>(s.n);
+    p.n = static_cast<uint32_t>(n);
     p.tiles_per_unit = static_cast<uint32_t>((g.unit_bytes + kTileBytes - 1) / kTileBytes);
     p.tile_start = b->total_tiles;
-    p.tile_count = static_cast<uint64_t>(g.units) * s.n * p.tiles_per_unit;
+    p.tile_count = static_cast<uint64_t>(g.units) * n * p.tiles_per_unit;
     if (p.tile_count > 0xffffffffull) throw invalid_argument("layer transfer too large for one plan");
     p.ids_off = static_cast<uint32_t>(b->ids.size());
     p.side_off = static_cast<uint32_t>(b->side_base.size());
@@ -375,11 +429,12 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
     dense = align_up(dense, kDenseAlign);
     const uint64_t dense_layer = dense;
     p.side_pitch = g.unit_bytes;
-    for (uint32_t u = 0; u < g.units; ++u) b->side_base.push_back(dense_layer + u * s.n * g.unit_bytes);
-    for (uint64_t i = 0; i < s.n; ++i) b->ids.push_back(static_cast<uint32_t>(s.block_idx[i]));
+    for (uint32_t u = 0; u < g.units; ++u) b->side_base.push_back(dense_layer + u * n * g.unit_bytes);
+    for (uint64_t j = 0; j < n; ++j) b->ids.push_back(static_cast<uint32_t>(s.block_idx[keep[j]]));
 
     for (uint32_t u = 0; u < g.units; ++u) {
-      for (uint64_t i = 0; i < s.n; ++i) {
+      for (uint64_t j = 0; j < n; ++j) {
+        const uint64_t i = keep[j];
         uint64_t h;
         if (u == 0) {
           h = reinterpret_cast<uint64_t>(s.k_src[i]);
@@ -391,7 +446,7 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
           b->side_ptrs.push_back(h);
           vec = vec && aligned16(h);
         }
-        const uint64_t d = dense_layer + (u * s.n + i) * g.unit_bytes;
+        const uint64_t d = dense_layer + (u * n + j) * g.unit_bytes;
         if (!b->runs.empty()) {
           Run& r = b->runs.back();
           if (r.dense + r.bytes == d && r.host + r.bytes == h) {
@@ -403,11 +458,45 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
       }
     }
     p.flags = vec ? kFlagVector : 0u;
-    dense = dense_layer + static_cast<uint64_t>(g.units) * s.n * g.unit_bytes;
+    dense = dense_layer + static_cast<uint64_t>(g.units) * n * g.unit_bytes;
     b->total_tiles += p.tile_count;
-    b->total_bytes += static_cast<uint64_t>(g.units) * s.n * g.unit_bytes;
-    unit_base += g.units * static_cast<uint32_t>(s.n);
+    b->total_bytes += static_cast<uint64_t>(g.units) * n * g.unit_bytes;
+    unit_base += g.units * static_cast<uint32_t>(n);
     b->layers.push_back(p);
+  }
+}
+
+namespace {
+void CUDART_CB raise_flag(void* p) { *static_cast<volatile int64_t*>(p) = 1; }
+}  // namespace
+
+void Executor::issue_serial(const Built& b, cudaStream_t s, int64_t* layer_done) {
+  // Copies in list order, merged into runs, exactly as batch_copy_segments_to_gpu
+  // (transfer.rs:116-198): K list then V list for the split layout, one
+  // block_size_bytes list otherwise.
+  for (const SerialLoad& sl : b.serial) {
+    const pf_layer_desc& l = sl.layer;
+    const bool split = is_split_layout(l);
+    const uint64_t unit = split ? l.bytes_per_block : l.bytes_per_block * l.segments;
+    for (int u = 0; u < (split ? 2 : 1); ++u) {
+      const std::vector<uint64_t>& host = u == 0 ? sl.k : sl.v;
+      size_t i = 0;
+      while (i < sl.ids.size()) {
+        const uint64_t g0 = static_cast<uint64_t>(sl.ids[i]) * l.bytes_per_block + u * l.kv_stride_bytes;
+        size_t c = 1;
+        while (i + c < sl.ids.size() &&
+               static_cast<uint64_t>(sl.ids[i + c]) * l.bytes_per_block + u * l.kv_stride_bytes == g0 + c * unit &&
+               host[i + c] == host[i] + c * unit) {
+          ++c;
+        }
+        cuda_check(cudaMemcpyAsync(reinterpret_cast<void*>(l.data_ptr + g0), reinterpret_cast<void*>(host[i]),
+                                   c * unit, cudaMemcpyHostToDevice, s),
+                   "cudaMemcpyAsync H2D (ordered)");
+        stats_.copy_calls += 1;
+        i += c;
+      }
+    }
+    if (layer_done) cuda_check(cudaLaunchHostFunc(s, raise_flag, layer_done + sl.done_index), "cudaLaunchHostFunc");
   }
 }
 
@@ -636,11 +725,12 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     // Layers without blocks are complete at once.
     std::vector<bool> has(n_layers, false);
     for (const PlanLayer& p : b.layers) has[p.done_index] = true;
+    for (const SerialLoad& sl : b.serial) has[sl.done_index] = true;
     for (uint64_t l = 0; l < n_layers; ++l) {
       if (!has[l]) reinterpret_cast<volatile int64_t*>(layer_done)[l] = 1;
     }
   }
-  if (b.total_tiles == 0) return;
+  if (b.total_tiles == 0 && b.serial.empty()) return;
   if (!staged) {
     for (const Run& r : b.runs) {
       if (!pinned_contains(reinterpret_cast<void*>(r.host), r.bytes)) {
@@ -655,9 +745,14 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     cuda_check(cudaStreamWaitEvent(cs, ev_start_, 0), "cudaStreamWaitEvent");
     cuda_check(cudaStreamWaitEvent(cs, ev_done_, 0), "cudaStreamWaitEvent");
   }
-  CopyArgs args = upload(b, layer_done != nullptr, kstream_);
-  args.layer_done = layer_done;
-  if (!staged) {
+  CopyArgs args{};
+  if (b.total_tiles > 0) {
+    args = upload(b, layer_done != nullptr, kstream_);
+    args.layer_done = layer_done;
+  }
+  if (b.total_tiles == 0) {
+    // only ordered copies below
+  } else if (!staged) {
     launch(kUnpack, true, args, 0, b.total_tiles, 0, kstream_);
     stats_.kernel_bytes += b.total_bytes;
   } else {
@@ -678,12 +773,16 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     }
     stats_.kernel_bytes += 2 * b.total_bytes;
   }
+  issue_serial(b, kstream_, layer_done);
   cuda_check(cudaEventRecord(ev_done_, kstream_), "cudaEventRecord");
   cuda_check(cudaStreamWaitEvent(caller, ev_done_, 0), "cudaStreamWaitEvent");
   for (size_t j = 0; j < cstreams_.size(); ++j) {
     cuda_check(cudaEventRecord(ev_copy_done_[j], cstreams_[j]), "cudaEventRecord");
   }
   stats_.bytes_loaded += b.total_bytes;
+  for (const SerialLoad& sl : b.serial) {
+    stats_.bytes_loaded += sl.ids.size() * load_geometry(sl.layer).unit_bytes * load_geometry(sl.layer).units;
+  }
 }
 
 void Executor::save_sync(const pf_save_layer* layers, uint64_t n_layers) {

@@ -62,12 +62,20 @@ class Executor {
     uint64_t tile_begin, tile_end;
     uint64_t dense_begin, dense_end;
   };
+  // A load layer whose destination blocks share bytes: copied in list order.
+  struct SerialLoad {
+    pf_layer_desc layer;
+    uint32_t done_index;
+    std::vector<int64_t> ids;
+    std::vector<uint64_t> k, v;
+  };
   struct Built {
     std::vector<PlanLayer> layers;
     std::vector<uint32_t> ids;
     std::vector<uint64_t> side_base;
     std::vector<uint64_t> side_ptrs;
     std::vector<Run> runs;  // staged mode only
+    std::vector<SerialLoad> serial;
     uint64_t total_tiles = 0;
     uint64_t total_bytes = 0;
   };
@@ -81,6 +89,7 @@ class Executor {
   int grid_for(uint64_t tiles) const;
   void copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h,
                  cudaStream_t s);
+  void issue_serial(const Built& b, cudaStream_t s, int64_t* layer_done);
 
   int device_;
   pf_executor_config cfg_;

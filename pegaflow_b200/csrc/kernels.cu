@@ -32,6 +32,9 @@ constexpr int kWarpsPerCta = 8;
 constexpr int kThreads = kWarpsPerCta * 32;
 constexpr int kVecPerLane = kTileBytes / (32 * 16);  // 8
 static_assert(kVecPerLane == 8, "tile = 32 lanes x 8 x 16 B");
+static_assert(sizeof(PlanLayer) % 16 == 0, "layer table is copied in 16-byte words");
+// Layer tables up to 48 KiB (512 layers) go to shared memory without opt-in.
+constexpr size_t kMaxSmemTableBytes = 48 * 1024;
 
 // Streaming 16-byte load: the source is read exactly once, so keep it out of L1.
 __device__ __forceinline__ uint4 ld_v4(const char* p) {
@@ -71,8 +74,8 @@ __device__ __forceinline__ void copy_tile(char* dst, const char* src,
 // raises its flag in host memory after a system-scope fence, so a host poller
 // that sees the flag also sees every byte of the layer.
 __device__ __forceinline__ void flush_layer(const CopyArgs& a, uint32_t l,
-                                            uint64_t layer_tiles, uint32_t done,
-                                            int lane) {
+                                            uint64_t layer_tiles, uint32_t done_index,
+                                            uint32_t done, int lane) {
   if (a.layer_tiles_done == nullptr || done == 0) return;
   __threadfence();
   __syncwarp();
@@ -80,17 +83,32 @@ __device__ __forceinline__ void flush_layer(const CopyArgs& a, uint32_t l,
     const unsigned long long prev = atomicAdd(&a.layer_tiles_done[l], (unsigned long long)done);
     if (prev + done == layer_tiles) {
       __threadfence_system();
-      *reinterpret_cast<volatile int64_t*>(a.layer_done + a.layers[l].done_index) = 1;
+      *reinterpret_cast<volatile int64_t*>(a.layer_done + done_index) = 1;
       __threadfence_system();
     }
   }
   __syncwarp();
 }
 
-template <int DIR, bool TABLE>
+extern __shared__ __align__(16) unsigned char g_smem[];
+
+// SMEM: the CTA first copies the plan's layer table into shared memory with
+// coalesced 16-byte loads (one round trip), so the per-warp layer lookups
+// below hit shared memory instead of chaining dependent global loads.
+template <int DIR, bool TABLE, bool SMEM>
 __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyArgs a) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+
+  const PlanLayer* layers = a.layers;
+  if (SMEM) {
+    const uint32_t n16 = a.n_layers * (uint32_t)(sizeof(PlanLayer) / 16);
+    const uint4* src = reinterpret_cast<const uint4*>(a.layers);
+    uint4* dst = reinterpret_cast<uint4*>(g_smem);
+    for (uint32_t i = threadIdx.x; i < n16; i += kThreads) dst[i] = src[i];
+    __syncthreads();
+    layers = reinterpret_cast<const PlanLayer*>(g_smem);
+  }
 
   const uint64_t total = a.tile_end - a.tile_begin;
   const uint64_t per_cta = (total + gridDim.x - 1) / gridDim.x;
@@ -105,18 +123,18 @@ __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyArgs a) {
   uint32_t lo = 0, hi = a.n_layers;
   while (hi - lo > 1) {
     const uint32_t mid = (lo + hi) >> 1;
-    if (a.layers[mid].tile_start <= tile) lo = mid; else hi = mid;
+    if (layers[mid].tile_start <= tile) lo = mid; else hi = mid;
   }
   uint32_t l = lo;
-  PlanLayer L = a.layers[l];
+  PlanLayer L = layers[l];
   uint32_t done_in_layer = 0;
 
   for (; tile < cta_end; tile += kWarpsPerCta) {
     while (tile >= L.tile_start + L.tile_count) {
-      flush_layer(a, l, L.tile_count, done_in_layer, lane);
+      flush_layer(a, l, L.tile_count, L.done_index, done_in_layer, lane);
       done_in_layer = 0;
       ++l;
-      L = a.layers[l];
+      L = layers[l];
     }
     const uint32_t local = (uint32_t)(tile - L.tile_start);
     const uint32_t unit_local = local / L.tiles_per_unit;
@@ -144,7 +162,7 @@ __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyArgs a) {
     }
     ++done_in_layer;
   }
-  flush_layer(a, l, L.tile_count, done_in_layer, lane);
+  flush_layer(a, l, L.tile_count, L.done_index, done_in_layer, lane);
 }
 
 }  // namespace
@@ -153,19 +171,24 @@ cudaError_t launch_copy(Dir dir, bool table, const CopyArgs& args, int grid,
                         cudaStream_t stream) {
   if (args.tile_end <= args.tile_begin) return cudaSuccess;
   if (grid < 1) grid = 1;
+  const size_t table_bytes = static_cast<size_t>(args.n_layers) * sizeof(PlanLayer);
+  const bool smem = table_bytes <= kMaxSmemTableBytes;
+  const size_t shm = smem ? table_bytes : 0;
+#define PF_LAUNCH(D, T, S) kv_copy_kernel<D, T, S><<<grid, kThreads, shm, stream>>>(args)
   if (dir == kPack) {
     if (table) {
-      kv_copy_kernel<kPack, true><<<grid, kThreads, 0, stream>>>(args);
+      if (smem) PF_LAUNCH(kPack, true, true); else PF_LAUNCH(kPack, true, false);
     } else {
-      kv_copy_kernel<kPack, false><<<grid, kThreads, 0, stream>>>(args);
+      if (smem) PF_LAUNCH(kPack, false, true); else PF_LAUNCH(kPack, false, false);
     }
   } else {
     if (table) {
-      kv_copy_kernel<kUnpack, true><<<grid, kThreads, 0, stream>>>(args);
+      if (smem) PF_LAUNCH(kUnpack, true, true); else PF_LAUNCH(kUnpack, true, false);
     } else {
-      kv_copy_kernel<kUnpack, false><<<grid, kThreads, 0, stream>>>(args);
+      if (smem) PF_LAUNCH(kUnpack, false, true); else PF_LAUNCH(kUnpack, false, false);
     }
   }
+#undef PF_LAUNCH
   return cudaGetLastError();
 }
 

@@ -10,18 +10,13 @@ reaches through its gRPC server.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, byref, c_char_p, c_int32, c_uint8, c_uint64, c_void_p
+from ctypes import byref, c_char_p, c_uint8, c_uint64, c_void_p
 from typing import Iterable, Optional, Sequence
 
 from . import _native as N
 from .transfer import Executor
 
 DEFAULT_POOL_BYTES = 30 * 1024 * 1024 * 1024  # pegaflow-core/src/lib.rs:56
-
-
-def _ids(block_ids: Sequence[int]):
-    arr = (c_int32 * max(1, len(block_ids)))(*block_ids)
-    return arr
 
 
 class PegaEngine:
@@ -133,7 +128,7 @@ class PegaEngine:
         block_hashes: Sequence[bytes],
     ) -> None:
         names = (c_char_p * max(1, len(layer_names)))(*[n.encode() for n in layer_names])
-        ids = _ids(block_ids)
+        ids, ids_keep = N.int32_array(block_ids)
         arr, keep = N.bytes_array(block_hashes)
         N.check(
             N.lib.pf_engine_batch_load_kv_blocks(
@@ -149,7 +144,7 @@ class PegaEngine:
                 len(block_hashes),
             )
         )
-        del keep
+        del keep, ids_keep
 
     # -- core engine calls the reference exposes through its server ------------
 
@@ -164,21 +159,19 @@ class PegaEngine:
         saves = list(saves)
         entries = (N.SaveEntry * max(1, len(saves)))()
         keep = []
+        converted = {}  # the same hash list object is often shared by every layer
         for i, (layer, ids, hashes) in enumerate(saves):
             name = layer.encode()
-            id_arr = _ids(list(ids))
-            h_arr, hk = N.bytes_array(list(hashes))
-            keep += [name, id_arr, h_arr, hk]
+            id_ptr, id_keep = N.int32_array(ids)
+            if id(hashes) not in converted:
+                converted[id(hashes)] = (hashes, *N.bytes_array(hashes))
+            _, h_ptr, hk = converted[id(hashes)]
+            keep += [name, id_keep, hk]
             entries[i].layer_name = name
-            entries[i].block_ids = ctypes.cast(id_arr, POINTER(c_int32))
-            entries[i].block_hashes = ctypes.cast(h_arr, POINTER(N.Bytes))
-            entries[i].n = len(ids)
-            if len(ids) != len(hashes):
-                # Preserve the reference's length check (lib.rs:563-569).
-                entries[i].n = min(len(ids), len(hashes))
-                raise RuntimeError(
-                    f"invalid argument: block_ids length {len(ids)} does not match block_hashes {len(hashes)}"
-                )
+            entries[i].block_ids = id_ptr
+            entries[i].n_ids = len(ids)
+            entries[i].block_hashes = h_ptr
+            entries[i].n_hashes = len(hashes)
         N.check(N.lib.pf_engine_batch_save_kv_blocks(self._h, instance_id.encode(), tp_rank, device_id, entries, len(saves)))
         del keep
 

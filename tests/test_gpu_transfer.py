@@ -174,6 +174,53 @@ def test_empty_and_single_block_layers(cuda, oracle):
     load_and_check(torch, oracle, ex, layers, regions, [np.array([], dtype=np.int64), np.array([3]), np.array([5])])
 
 
+@pytest.mark.parametrize("mode", MODES)
+def test_repeated_destinations_keep_the_last_block(cuda, oracle, mode):
+    """The reference copies a layer's blocks in list order, so a destination
+    listed twice ends up with the later block; the kernels keep that."""
+    torch = cuda
+    from pegaflow_b200 import Executor, Layout, LoadSpec, PinnedBuffer
+
+    t = kv(torch, (2, 16, 16, 8, 128), torch.bfloat16, 1)
+    lay = Layout.from_tensor(t)
+    pool = PinnedBuffer(8 * 65536)
+    pool.numpy()[:] = np.random.default_rng(0).integers(0, 256, pool.nbytes, dtype=np.uint8)
+    ids = np.array([3, 5, 3, 9, 5, 3])
+    ks = np.array([pool.ptr + i * 32768 for i in range(6)], np.uint64)
+    vs = ks + 6 * 32768
+    ref = host_bytes(t)
+    oracle.load_layer(olayout(oracle, lay), ref, ids, [int(x) for x in ks], [int(x) for x in vs])
+    Executor(0, load_mode=mode).load([LoadSpec(lay, ids, ks, vs)])
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host_bytes(t), ref)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_self_overlapping_layouts_load_in_list_order(cuda, oracle, mode):
+    """Layouts whose blocks share bytes (K/V interleaved with stride ==
+    bytes_per_block, or 3 strided segments) take the ordered copy path and end
+    byte-identical to the reference's sequential copies."""
+    torch = cuda
+    from pegaflow_b200 import Executor, Layout, LoadSpec, PinnedBuffer
+
+    raw = kv(torch, (40 * 4096,), torch.uint8, 2)
+    layouts = [Layout(raw.data_ptr(), 33 * 4096, 32, 4096, 4096, 2),      # contiguous, 8 KiB blocks overlap
+               Layout(raw.data_ptr(), 40 * 4096, 8, 4096, 9 * 4096, 3)]   # 3 strided segments
+    rng = np.random.default_rng(7)
+    for lay in layouts:
+        pool = PinnedBuffer(40 * lay.block_size_bytes)
+        pool.numpy()[:] = rng.integers(0, 256, pool.nbytes, dtype=np.uint8)
+        nb_ok = [b for b in range(lay.num_blocks) if b * lay.bytes_per_block + lay.block_size_bytes <= lay.size_bytes]
+        ids = rng.choice(nb_ok, size=12)
+        ks = np.array([pool.ptr + i * lay.block_size_bytes for i in range(12)], np.uint64)
+        ref = host_bytes(raw)
+        ol = oracle.Layout(lay.size_bytes, lay.num_blocks, lay.bytes_per_block, lay.kv_stride_bytes, lay.segments)
+        oracle.load_layer(ol, ref, ids, [int(x) for x in ks], None)
+        Executor(0, load_mode=mode).load([LoadSpec(lay, ids, ks, None)])
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(host_bytes(raw), ref)
+
+
 def test_out_of_range_ids_fail_before_any_copy(cuda):
     torch = cuda
     from pegaflow_b200 import Executor, Layout, PinnedBuffer, SaveSpec
