@@ -155,6 +155,23 @@ int pf_save_blocks_async(pf_executor* exec, const pf_save_layer* layers,
 int pf_load_blocks_async(pf_executor* exec, const pf_load_layer* layers,
                          uint64_t n_layers, void* stream, int64_t* layer_done);
 
+/* Save without allocating: for callers that cannot call cudaMalloc while
+ * they save, e.g. an inference engine whose caching allocator or KV pool owns
+ * all free HBM, or code under a pool policy that forbids out-of-band device
+ * allocations. No counterpart in the reference (its saves always go through
+ * its worker threads). Same copies and pool bytes as pf_save_blocks, issued in
+ * order on `stream` (a cudaStream_t; NULL = legacy default stream); the call
+ * returns once they are queued. Scratch is two fixed file-scope device arrays
+ * that every GPU loading this library holds until exit: a 1 MiB plan area and
+ * an 8 MiB staging slot. A save whose plan (layer table + block ids + offsets)
+ * exceeds 1 MiB, or with a copy unit above 4 MiB, fails with
+ * PF_ERR_INVALID_ARGUMENT. The first call on a device resolves the arrays'
+ * addresses (cudaGetSymbolAddress) and should come before any stream capture.
+ * All calls on a device share the arrays, so calls that overlap on the GPU
+ * race; keep them ordered on one stream. Calls no cudaMalloc or cudaFree. */
+int pf_save_blocks_noalloc(int32_t device_id, const pf_save_layer* layers,
+                           uint64_t n_layers, void* stream);
+
 /* Counters since creation (or the last reset). kernel_ms is the sum of the
  * pack/unpack kernels' CUDA-event durations, collected only while timing is
  * on; kernel_bytes counts the algorithmic HBM bytes those kernels moved

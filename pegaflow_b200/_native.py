@@ -168,6 +168,7 @@ _SIGNATURES = {
     "pf_load_blocks": (c_int, [c_void_p, POINTER(LoadLayer), c_uint64]),
     "pf_save_blocks_async": (c_int, [c_void_p, POINTER(SaveLayer), c_uint64, c_void_p]),
     "pf_load_blocks_async": (c_int, [c_void_p, POINTER(LoadLayer), c_uint64, c_void_p, c_void_p]),
+    "pf_save_blocks_noalloc": (c_int, [c_int32, POINTER(SaveLayer), c_uint64, c_void_p]),
     "pf_executor_stats_get": (c_int, [c_void_p, POINTER(ExecutorStats)]),
     "pf_executor_stats_reset": (c_int, [c_void_p]),
     "pf_executor_set_timing": (c_int, [c_void_p, c_int]),
