@@ -150,8 +150,15 @@ def link_peaks(torch, device: int) -> dict:
 
 
 def make_workload(torch, wl: dict, device: int, rank: int, world: int, order: str):
-    """KV tensors on the GPU plus seeded src/dst block lists."""
-    heads = wl["heads"] // world if wl.get("tp") else wl["heads"]
+    """KV tensors on the GPU plus seeded src/dst block lists. For the TP
+    workload each rank holds its own slice of the KV heads."""
+    from pegaflow_b200.ranks import block_lists, tp_heads
+
+    if wl.get("tp"):
+        lo, hi = tp_heads(wl["heads"], rank, world)
+        heads = hi - lo
+    else:
+        heads = wl["heads"]
     nb, bs, hd = wl["num_blocks"], wl["block_size"], wl["head_dim"]
     gen = torch.Generator(device=f"cuda:{device}").manual_seed(1000 + rank)
     tensors = []
@@ -159,14 +166,7 @@ def make_workload(torch, wl: dict, device: int, rank: int, world: int, order: st
         shape = (nb, bs, heads, hd) if wl.get("separate") else (2, nb, bs, heads, hd)
         dt = torch.float16 if wl.get("separate") else torch.bfloat16
         tensors.append(torch.randn(shape, generator=gen, device=f"cuda:{device}", dtype=torch.float32).to(dt))
-    cpu_gen = torch.Generator().manual_seed(3 + rank)
-    n = wl["blocks"]
-    if order == "sorted":
-        src = np.arange(n)
-        dst = (np.arange(n) + n) % nb
-    else:
-        src = torch.randperm(nb, generator=cpu_gen)[:n].numpy()
-        dst = torch.randperm(nb, generator=torch.Generator().manual_seed(4 + rank))[:n].numpy()
+    src, dst = block_lists(nb, wl["blocks"], rank, order)
     return tensors, src, dst
 
 
@@ -311,6 +311,7 @@ def main() -> int:
     ap.add_argument("--slots", type=int, default=0)
     ap.add_argument("--copy-streams", type=int, default=0)
     ap.add_argument("--ctas-per-sm", type=int, default=0)
+    ap.add_argument("--cache-streaming", action="store_true", help="evict-first loads/stores in the kernels")
     ap.add_argument("--e2e-steps", type=int, default=0, help="engine-API steps (default: --steps)")
     ap.add_argument("--no-refcopy", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -327,33 +328,20 @@ def main() -> int:
         return 0
 
     import torch
-    import torch.distributed as dist
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
+    from pegaflow_b200.ranks import Ranks
+
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device(f"cuda:{local}"))
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def min_over_ranks(x: float) -> float:
-        return -max_over_ranks(-x)
+    ranks = Ranks.from_env("nccl", timeout_s=600)
+    rank, world, local = ranks.rank, ranks.world, ranks.local
+    barrier, max_over_ranks, min_over_ranks = ranks.barrier, ranks.max, ranks.min
 
     from pegaflow_b200 import Executor, PegaEngine, PinnedBuffer, PyLoadState, refcopy_load, refcopy_save
 
+    from pegaflow_b200.ranks import bind_to_gpu_cpus
+
+    cpus = bind_to_gpu_cpus(local)
     peaks = measured_peaks()
     link = link_peaks(torch, local)
     tensors, src, dst = make_workload(torch, wl, local, rank, world, args.order)
@@ -363,7 +351,8 @@ def main() -> int:
 
     ex = Executor(local, save_mode=args.save_mode, load_mode=args.load_mode,
                   staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
-                  copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm)
+                  copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm,
+                  cache_streaming=args.cache_streaming)
     pool = PinnedBuffer(payload + wl["layers"] * 8192 + (1 << 20), write_combined=True)
     saves, loads, _ = executor_specs(tensors, src, dst, pool.ptr)
     stream = torch.cuda.Stream(local)
@@ -417,7 +406,8 @@ def main() -> int:
     eng = PegaEngine(2 * payload + (256 << 20), enable_lfu_admission=False,
                      executor=dict(save_mode=args.save_mode, load_mode=args.load_mode,
                                    staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
-                                   copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm))
+                                   copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm,
+                                   cache_streaming=1 if args.cache_streaming else 0))
     names = [f"model.layers.{i}.self_attn" for i in range(len(tensors))]
     from pegaflow_b200 import Layout
 
@@ -500,6 +490,7 @@ def main() -> int:
                     "d2h_bytes_per_step": payload, "p50_load_ms": round(e2e_load_p50, 3), "steps": e2e_steps,
                     "api": "PegaEngine.batch_save_kv_blocks + batch_load_kv_blocks + PyLoadState"},
             "gpu_launches": st["kernel_launches"],
+            "host_cpus": (f"{len(cpus)} CPUs local to the GPU (NVML affinity)" if cpus else "unbound"),
             "copy_calls": st["copy_calls"],
             "reference_copy_path": ref,
             "cpu_baseline": cpu,
@@ -508,8 +499,7 @@ def main() -> int:
                                                            "cache_block_evictions")},
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    ranks.close()
     return 0
 
 

@@ -95,7 +95,7 @@ typedef struct pf_executor_config {
   uint32_t load_mode;           /* pf_transfer_mode */
   uint32_t ctas_per_sm;         /* 0 = default */
   uint32_t copy_streams;        /* 0 = default (2) */
-  uint32_t reserved;
+  uint32_t cache_streaming;     /* 1 = evict-first loads/stores in the kernels */
 } pf_executor_config;
 
 /* Fill *cfg with the library defaults. */
@@ -248,6 +248,16 @@ typedef struct pf_load_state pf_load_state;
 int pf_load_state_create(pf_load_state** out);
 /* LoadState::attach (sync_state.rs:145-155) with the same checks. */
 int pf_load_state_attach(const char* shm_name, pf_load_state** out);
+/* LoadState with a per-layer extension (no reference counterpart; the
+ * reference has no per-layer signal, worker.py:288-289). The first 32 bytes
+ * are the version-1 mapping unchanged, so a reference reader still attaches;
+ * after them: u32 'PFL2', u32 n_layers, 8 reserved bytes, then one i64 per
+ * layer of the load request (in layer_names order): 0 pending, 1 in place. */
+int pf_load_state_create_layers(uint32_t n_layers, pf_load_state** out);
+/* Layers in the extension (0 for a version-1-only mapping). */
+uint32_t pf_load_state_layer_count(const pf_load_state* s);
+/* Word of one layer (PF_LOAD_STATE_ERROR when out of range). */
+int64_t pf_load_state_layer_get(const pf_load_state* s, uint32_t layer);
 const char* pf_load_state_name(const pf_load_state* s);
 int64_t pf_load_state_get(const pf_load_state* s);
 void pf_load_state_set_completed(pf_load_state* s);

@@ -67,7 +67,7 @@ class ExecutorConfig(Structure):
         ("load_mode", c_uint32),
         ("ctas_per_sm", c_uint32),
         ("copy_streams", c_uint32),
-        ("reserved", c_uint32),
+        ("cache_streaming", c_uint32),
     ]
 
 
@@ -186,6 +186,9 @@ _SIGNATURES = {
     ),
     "pf_load_state_create": (c_int, [POINTER(c_void_p)]),
     "pf_load_state_attach": (c_int, [c_char_p, POINTER(c_void_p)]),
+    "pf_load_state_create_layers": (c_int, [c_uint32, POINTER(c_void_p)]),
+    "pf_load_state_layer_count": (c_uint32, [c_void_p]),
+    "pf_load_state_layer_get": (c_int64, [c_void_p, c_uint32]),
     "pf_load_state_name": (c_char_p, [c_void_p]),
     "pf_load_state_get": (c_int64, [c_void_p]),
     "pf_load_state_set_completed": (None, [c_void_p]),

@@ -244,7 +244,12 @@ void pf_allocator_report(pf_allocator* a, uint64_t* total_free_bytes, uint64_t* 
 
 int pf_load_state_create(pf_load_state** out) {
   if (!out) return null_arg("out");
-  return guarded([&] { *out = pf::load_state_create(); });
+  return guarded([&] { *out = pf::load_state_create(0); });
+}
+
+int pf_load_state_create_layers(uint32_t n_layers, pf_load_state** out) {
+  if (!out) return null_arg("out");
+  return guarded([&] { *out = pf::load_state_create(n_layers); });
 }
 
 int pf_load_state_attach(const char* shm_name, pf_load_state** out) {

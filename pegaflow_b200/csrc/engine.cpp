@@ -6,6 +6,7 @@
 #include <utility>
 
 #include "common.h"
+#include "pinned.h"
 
 namespace pf {
 
@@ -84,6 +85,30 @@ void DeviceWorker::process(LoadTask& task) {
   const auto t0 = Clock::now();
   bool ok = true;
   uint64_t bytes = 0;
+  // A LoadState with a per-layer extension covering every requested layer
+  // gets its words raised by the kernels as layers land: its page is pinned
+  // and mapped for the device for the duration of the task.
+  pf_load_state* ls = nullptr;
+  try {
+    ls = load_state_attach(task.shm);
+  } catch (const std::exception& e) {
+    fprintf(stderr, "pegaflow_b200: failed to attach LoadState %s: %s\n", task.shm.c_str(), e.what());
+  }
+  int64_t* words = nullptr;
+  void* pinned_base = nullptr;
+  if (ls && load_state_layers(ls) >= task.layers.size() && !task.layers.empty()) {
+    size_t len = 0;
+    void* base = load_state_base(ls, &len);
+    const size_t page = 4096;
+    len = (len + page - 1) / page * page;
+    if (cudaHostRegister(base, len, cudaHostRegisterPortable | cudaHostRegisterMapped) == cudaSuccess) {
+      pinned_register(base, len);
+      pinned_base = base;
+      words = load_state_layer_words(ls);
+    } else {
+      cudaGetLastError();  // per-layer words are then raised together at the end
+    }
+  }
   try {
     std::vector<pf_load_layer> layers;
     std::vector<std::vector<const void*>> ks(task.layers.size()), vs(task.layers.size());
@@ -105,20 +130,24 @@ void DeviceWorker::process(LoadTask& task) {
       layers.push_back(pl);
       bytes += load_geometry(L.reg).unit_bytes * load_geometry(L.reg).units * L.ids.size();
     }
-    exec_->load_sync(layers.data(), layers.size());
+    exec_->load_sync(layers.data(), layers.size(), words);
   } catch (const std::exception& e) {
     ok = false;
     fprintf(stderr, "pegaflow_b200: load task failed: %s\n", e.what());
   }
-  pf_load_state* ls = nullptr;
-  try {
-    ls = load_state_attach(task.shm);
-  } catch (const std::exception& e) {
-    fprintf(stderr, "pegaflow_b200: failed to attach LoadState %s: %s\n", task.shm.c_str(), e.what());
-    counters_->load_failures.fetch_add(1);
+  if (pinned_base) {
+    pinned_unregister(pinned_base);
+    if (cudaHostUnregister(pinned_base) != cudaSuccess) cudaGetLastError();
   }
-  if (ls) {
+  if (!ls) {
+    counters_->load_failures.fetch_add(1);
+  } else {
     if (ok) {
+      const uint32_t n = load_state_layers(ls);
+      if (n >= task.layers.size() && !words) {
+        int64_t* w = load_state_layer_words(ls);
+        for (size_t l = 0; l < task.layers.size(); ++l) reinterpret_cast<volatile int64_t*>(w)[l] = 1;
+      }
       load_state_set(ls, PF_LOAD_STATE_SUCCESS);
     } else {
       counters_->load_failures.fetch_add(1);
@@ -501,10 +530,18 @@ void Engine::batch_load_inner(const std::string& instance_id, uint64_t tp_rank, 
       L.ids.push_back(block_ids[k]);
       L.blocks.push_back(cache[k]->slots[slot]);
     }
-    if (!L.ids.empty()) task.layers.push_back(std::move(L));
+    // Layers without blocks stay in the task (as empty entries) so per-layer
+    // completion words line up with layer_names; the executor raises them at once.
+    task.layers.push_back(std::move(L));
   }
-  if (task.layers.empty()) {
+  bool any = false;
+  for (const LoadLayer& L : task.layers) any = any || !L.ids.empty();
+  if (!any) {
+    // lib.rs:1054-1060: nothing to load completes immediately.
     pf_load_state* ls = attach_or_storage_error(shm);
+    const uint32_t nw = load_state_layers(ls);
+    int64_t* w = load_state_layer_words(ls);
+    for (uint32_t l = 0; l < nw && l < task.layers.size(); ++l) reinterpret_cast<volatile int64_t*>(w)[l] = 1;
     load_state_set(ls, PF_LOAD_STATE_SUCCESS);
     load_state_close(ls);
     return;

@@ -21,11 +21,14 @@ struct pf_load_state;
 
 namespace pf {
 
-pf_load_state* load_state_create();
+pf_load_state* load_state_create(uint32_t n_layers);
 pf_load_state* load_state_attach(const std::string& name);
 void load_state_close(pf_load_state* s);
 int64_t load_state_get(const pf_load_state* s);
 void load_state_set(pf_load_state* s, int64_t v);
+uint32_t load_state_layers(const pf_load_state* s);
+int64_t* load_state_layer_words(pf_load_state* s);
+void* load_state_base(pf_load_state* s, size_t* len);
 
 struct EngineCounters {
   std::atomic<uint64_t> save_bytes{0}, save_calls{0}, load_bytes{0}, load_calls{0}, load_failures{0};

@@ -628,7 +628,8 @@ void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_
     e1 = take();
     cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
   }
-  cuda_check(launch_copy(dir, table, a, grid_for(tile_end - tile_begin), s), "kernel launch");
+  cuda_check(launch_copy(dir, table, a, grid_for(tile_end - tile_begin), s, cfg_.cache_streaming != 0),
+             "kernel launch");
   if (timing_) {
     cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
     timed_.emplace_back(e0, e1);
@@ -748,7 +749,12 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
   CopyArgs args{};
   if (b.total_tiles > 0) {
     args = upload(b, layer_done != nullptr, kstream_);
-    args.layer_done = layer_done;
+    if (layer_done) {
+      // The kernel writes through the device view of the pinned words.
+      void* dev = nullptr;
+      cuda_check(cudaHostGetDevicePointer(&dev, layer_done, 0), "cudaHostGetDevicePointer(layer_done)");
+      args.layer_done = static_cast<int64_t*>(dev);
+    }
   }
   if (b.total_tiles == 0) {
     // only ordered copies below
@@ -790,8 +796,8 @@ void Executor::save_sync(const pf_save_layer* layers, uint64_t n_layers) {
   cuda_check(cudaStreamSynchronize(own_stream_), "cudaStreamSynchronize(save)");
 }
 
-void Executor::load_sync(const pf_load_layer* layers, uint64_t n_layers) {
-  load(layers, n_layers, own_stream_, nullptr);
+void Executor::load_sync(const pf_load_layer* layers, uint64_t n_layers, int64_t* layer_done) {
+  load(layers, n_layers, own_stream_, layer_done);
   cuda_check(cudaStreamSynchronize(own_stream_), "cudaStreamSynchronize(load)");
 }
 

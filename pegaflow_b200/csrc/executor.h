@@ -46,7 +46,7 @@ class Executor {
             int64_t* layer_done);
   // Blocking wrappers on the executor's own stream.
   void save_sync(const pf_save_layer* layers, uint64_t n_layers);
-  void load_sync(const pf_load_layer* layers, uint64_t n_layers);
+  void load_sync(const pf_load_layer* layers, uint64_t n_layers, int64_t* layer_done = nullptr);
 
   void stats(pf_executor_stats* out);
   void reset_stats();

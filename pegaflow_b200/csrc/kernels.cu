@@ -36,33 +36,47 @@ static_assert(sizeof(PlanLayer) % 16 == 0, "layer table is copied in 16-byte wor
 // Layer tables up to 48 KiB (512 layers) go to shared memory without opt-in.
 constexpr size_t kMaxSmemTableBytes = 48 * 1024;
 
-// Streaming 16-byte load: the source is read exactly once, so keep it out of L1.
+// 16-byte load of data read exactly once: kept out of L1; with CS (cache
+// streaming) also marked evict-first in L2.
+template <bool CS>
 __device__ __forceinline__ uint4 ld_v4(const char* p) {
   uint4 v;
-  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+  if (CS) {
+    asm volatile("ld.global.cs.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+  } else {
+    asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+  }
   return v;
 }
 
+template <bool CS>
 __device__ __forceinline__ void st_v4(char* p, const uint4& v) {
-  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x),
-               "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
+  if (CS) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+  } else {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+  }
 }
 
+template <bool CS>
 __device__ __forceinline__ void copy_tile(char* dst, const char* src,
                                           uint32_t bytes, bool vec, int lane) {
   if (vec) {
     if (bytes == kTileBytes) {
       uint4 r[kVecPerLane];
 #pragma unroll
-      for (int k = 0; k < kVecPerLane; ++k) r[k] = ld_v4(src + (k * 32 + lane) * 16);
+      for (int k = 0; k < kVecPerLane; ++k) r[k] = ld_v4<CS>(src + (k * 32 + lane) * 16);
 #pragma unroll
-      for (int k = 0; k < kVecPerLane; ++k) st_v4(dst + (k * 32 + lane) * 16, r[k]);
+      for (int k = 0; k < kVecPerLane; ++k) st_v4<CS>(dst + (k * 32 + lane) * 16, r[k]);
     } else {
       // Tail of a unit: bytes is a multiple of 16 below one tile.
-      for (uint32_t off = lane * 16u; off < bytes; off += 512u) st_v4(dst + off, ld_v4(src + off));
+      for (uint32_t off = lane * 16u; off < bytes; off += 512u) st_v4<CS>(dst + off, ld_v4<CS>(src + off));
     }
   } else {
     // Unaligned layouts (e.g. 4-byte per-block scales): byte granularity.
@@ -95,7 +109,7 @@ extern __shared__ __align__(16) unsigned char g_smem[];
 // SMEM: the CTA first copies the plan's layer table into shared memory with
 // coalesced 16-byte loads (one round trip), so the per-warp layer lookups
 // below hit shared memory instead of chaining dependent global loads.
-template <int DIR, bool TABLE, bool SMEM>
+template <int DIR, bool TABLE, bool SMEM, bool CS>
 __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyArgs a) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -156,39 +170,56 @@ __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyArgs a) {
                                      in_unit + a.side_shift);
     }
     if (DIR == kPack) {
-      copy_tile(side, cache, bytes, (L.flags & kFlagVector) != 0, lane);
+      copy_tile<CS>(side, cache, bytes, (L.flags & kFlagVector) != 0, lane);
     } else {
-      copy_tile(cache, side, bytes, (L.flags & kFlagVector) != 0, lane);
+      copy_tile<CS>(cache, side, bytes, (L.flags & kFlagVector) != 0, lane);
     }
     ++done_in_layer;
   }
   flush_layer(a, l, L.tile_count, L.done_index, done_in_layer, lane);
 }
 
+// Runtime flags -> template instance.
+template <int DIR, bool TABLE, bool SMEM>
+void launch_cs(bool cs, const CopyArgs& a, int grid, size_t shm, cudaStream_t s) {
+  if (cs) {
+    kv_copy_kernel<DIR, TABLE, SMEM, true><<<grid, kThreads, shm, s>>>(a);
+  } else {
+    kv_copy_kernel<DIR, TABLE, SMEM, false><<<grid, kThreads, shm, s>>>(a);
+  }
+}
+
+template <int DIR, bool TABLE>
+void launch_smem(bool smem, bool cs, const CopyArgs& a, int grid, size_t shm, cudaStream_t s) {
+  if (smem) {
+    launch_cs<DIR, TABLE, true>(cs, a, grid, shm, s);
+  } else {
+    launch_cs<DIR, TABLE, false>(cs, a, grid, shm, s);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_copy(Dir dir, bool table, const CopyArgs& args, int grid,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, bool streaming) {
   if (args.tile_end <= args.tile_begin) return cudaSuccess;
   if (grid < 1) grid = 1;
   const size_t table_bytes = static_cast<size_t>(args.n_layers) * sizeof(PlanLayer);
   const bool smem = table_bytes <= kMaxSmemTableBytes;
   const size_t shm = smem ? table_bytes : 0;
-#define PF_LAUNCH(D, T, S) kv_copy_kernel<D, T, S><<<grid, kThreads, shm, stream>>>(args)
   if (dir == kPack) {
     if (table) {
-      if (smem) PF_LAUNCH(kPack, true, true); else PF_LAUNCH(kPack, true, false);
+      launch_smem<kPack, true>(smem, streaming, args, grid, shm, stream);
     } else {
-      if (smem) PF_LAUNCH(kPack, false, true); else PF_LAUNCH(kPack, false, false);
+      launch_smem<kPack, false>(smem, streaming, args, grid, shm, stream);
     }
   } else {
     if (table) {
-      if (smem) PF_LAUNCH(kUnpack, true, true); else PF_LAUNCH(kUnpack, true, false);
+      launch_smem<kUnpack, true>(smem, streaming, args, grid, shm, stream);
     } else {
-      if (smem) PF_LAUNCH(kUnpack, false, true); else PF_LAUNCH(kUnpack, false, false);
+      launch_smem<kUnpack, false>(smem, streaming, args, grid, shm, stream);
     }
   }
-#undef PF_LAUNCH
   return cudaGetLastError();
 }
 

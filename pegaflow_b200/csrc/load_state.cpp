@@ -40,6 +40,22 @@ struct Record {
 };
 static_assert(sizeof(Record) == kRecordSize, "record layout");
 
+// Per-layer extension, placed after the 32 bytes a version-1 reader maps
+// (a reader built against sync_state.rs only checks that the mapping is at
+// least 32 bytes, so it still attaches):
+//   [32, 36)  u32 magic 0x324C4650 ('PFL2')
+//   [36, 40)  u32 layer count n
+//   [40, 48)  reserved
+//   [48, 48 + 8n)  i64 per layer: 0 pending, 1 bytes in place
+constexpr uint32_t kLayerMagic = 0x324C4650u;
+constexpr size_t kLayerHeader = 16;
+struct LayerHeader {
+  std::atomic<uint32_t> magic;
+  std::atomic<uint32_t> count;
+  uint64_t reserved;
+};
+static_assert(sizeof(LayerHeader) == kLayerHeader, "layer header layout");
+
 std::string uuid_v4_simple() {
   unsigned char b[16];
   bool ok = false;
@@ -73,21 +89,24 @@ struct pf_load_state {
   size_t len = 0;
   pf::Record* rec = nullptr;
   bool owner = false;
+  uint32_t layers = 0;              // per-layer extension size (0: version-1 only)
+  int64_t* layer_words = nullptr;   // the extension's per-layer words
 };
 
 namespace pf {
 
-pf_load_state* load_state_create() {
+pf_load_state* load_state_create(uint32_t n_layers) {
   const std::string name = "pega_load_" + uuid_v4_simple();
+  const size_t size = n_layers ? kAllocSize + kLayerHeader + 8ull * n_layers : kAllocSize;
   const int fd = shm_open(name.c_str(), O_CREAT | O_EXCL | O_RDWR, S_IRUSR | S_IWUSR);
   if (fd < 0) throw ls_error("failed to create shared memory: " + std::string(strerror(errno)));
-  if (ftruncate(fd, static_cast<off_t>(kAllocSize)) != 0) {
+  if (ftruncate(fd, static_cast<off_t>(size)) != 0) {
     const int e = errno;
     close(fd);
     shm_unlink(name.c_str());
     throw ls_error("failed to create shared memory: " + std::string(strerror(e)));
   }
-  void* base = mmap(nullptr, kAllocSize, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+  void* base = mmap(nullptr, size, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
   close(fd);
   if (base == MAP_FAILED) {
     shm_unlink(name.c_str());
@@ -105,9 +124,17 @@ pf_load_state* load_state_create() {
   auto* s = new pf_load_state();
   s->name = name;
   s->base = base;
-  s->len = kAllocSize;
+  s->len = size;
   s->rec = rec;
   s->owner = true;
+  if (n_layers) {
+    auto* lh = reinterpret_cast<LayerHeader*>(static_cast<uint8_t*>(base) + kAllocSize);
+    s->layer_words = reinterpret_cast<int64_t*>(static_cast<uint8_t*>(base) + kAllocSize + kLayerHeader);
+    for (uint32_t i = 0; i < n_layers; ++i) s->layer_words[i] = 0;
+    lh->count.store(n_layers, std::memory_order_relaxed);
+    lh->magic.store(kLayerMagic, std::memory_order_release);
+    s->layers = n_layers;
+  }
   return s;
 }
 
@@ -162,6 +189,15 @@ pf_load_state* load_state_attach(const std::string& name) {
   s->len = len;
   s->rec = rec;
   s->owner = false;
+  if (len >= kAllocSize + kLayerHeader) {
+    auto* lh = reinterpret_cast<LayerHeader*>(static_cast<uint8_t*>(base) + kAllocSize);
+    const uint32_t n = lh->count.load(std::memory_order_relaxed);
+    if (lh->magic.load(std::memory_order_acquire) == kLayerMagic && n > 0 &&
+        kAllocSize + kLayerHeader + 8ull * n <= len) {
+      s->layers = n;
+      s->layer_words = reinterpret_cast<int64_t*>(static_cast<uint8_t*>(base) + kAllocSize + kLayerHeader);
+    }
+  }
   return s;
 }
 
@@ -174,7 +210,20 @@ void load_state_close(pf_load_state* s) {
 
 int64_t load_state_get(const pf_load_state* s) { return s->rec->state.load(std::memory_order_acquire); }
 void load_state_set(pf_load_state* s, int64_t v) { s->rec->state.store(v, std::memory_order_release); }
+uint32_t load_state_layers(const pf_load_state* s) { return s->layers; }
+int64_t* load_state_layer_words(pf_load_state* s) { return s->layer_words; }
+void* load_state_base(pf_load_state* s, size_t* len) {
+  *len = s->len;
+  return s->base;
+}
 
 }  // namespace pf
 
 extern "C" const char* pf_load_state_name(const pf_load_state* s) { return s ? s->name.c_str() : ""; }
+
+extern "C" uint32_t pf_load_state_layer_count(const pf_load_state* s) { return s ? s->layers : 0; }
+
+extern "C" int64_t pf_load_state_layer_get(const pf_load_state* s, uint32_t layer) {
+  if (!s || layer >= s->layers) return PF_LOAD_STATE_ERROR;
+  return reinterpret_cast<volatile const int64_t*>(s->layer_words)[layer];
+}

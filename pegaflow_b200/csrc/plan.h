@@ -69,8 +69,9 @@ struct CopyArgs {
 enum Dir : int { kPack = 0, kUnpack = 1 };
 
 // Host entry: launch the copy kernel. table = side addresses come from
-// side_ptrs (one per unit) instead of side_base + i*side_pitch.
+// side_ptrs (one per unit) instead of side_base + i*side_pitch; streaming =
+// evict-first (.cs) loads and stores.
 cudaError_t launch_copy(Dir dir, bool table, const CopyArgs& args, int grid,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool streaming = false);
 
 }  // namespace pf

@@ -226,9 +226,15 @@ class PyLoadState:
     shared-memory object and unlinks it when closed or collected.
     """
 
-    def __init__(self):
+    def __init__(self, n_layers: int = 0):
+        """n_layers > 0 adds one completion word per layer of the load request
+        (an extension after the version-1 bytes, which stay readable by the
+        reference's LoadState::attach)."""
         h = c_void_p()
-        N.check(N.lib.pf_load_state_create(byref(h)))
+        if n_layers:
+            N.check(N.lib.pf_load_state_create_layers(n_layers, byref(h)))
+        else:
+            N.check(N.lib.pf_load_state_create(byref(h)))
         self._h = h
 
     @classmethod
@@ -248,6 +254,27 @@ class PyLoadState:
 
     def is_ready(self) -> bool:
         return self.get_state() != 0
+
+    def layer_count(self) -> int:
+        return int(N.lib.pf_load_state_layer_count(self._h))
+
+    def layer_ready(self, layer: int) -> bool:
+        """True once the bytes of layer `layer` (index into the load's
+        layer_names) are in place."""
+        return int(N.lib.pf_load_state_layer_get(self._h, layer)) == 1
+
+    def wait_layer(self, layer: int, timeout_s: float = 5.0) -> bool:
+        """Poll until layer `layer` is in place (True), the load failed or the
+        timeout ran out (False)."""
+        import time
+
+        deadline = time.monotonic() + timeout_s
+        while True:
+            if self.layer_ready(layer):
+                return True
+            if self.get_state() < 0 or time.monotonic() > deadline:
+                return False
+            time.sleep(0)
 
     def set_completed(self) -> None:
         N.lib.pf_load_state_set_completed(self._h)

@@ -133,6 +133,7 @@ class Executor:
         load_mode: str = "auto",
         ctas_per_sm: int = 0,
         copy_streams: int = 0,
+        cache_streaming: bool = False,
         _handle: Optional[int] = None,
     ):
         self.device_id = device_id
@@ -152,6 +153,7 @@ class Executor:
             cfg.ctas_per_sm = ctas_per_sm
         if copy_streams:
             cfg.copy_streams = copy_streams
+        cfg.cache_streaming = 1 if cache_streaming else 0
         h = c_void_p()
         N.check(N.lib.pf_executor_create(device_id, byref(cfg), byref(h)))
         self._h = h

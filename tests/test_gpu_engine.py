@@ -166,6 +166,31 @@ def test_save_batch_golden_replay(cuda, oracle):
     p.check_caches()
 
 
+def test_layer_wise_completion_words(cuda, oracle):
+    """A LoadState with the per-layer extension gets each layer's word raised
+    by the kernels as that layer lands (before the batch state turns 1);
+    layers with no blocks are raised at once."""
+    torch = cuda
+    from pegaflow_b200 import PyLoadState
+
+    p = Pair(torch, oracle)
+    names = [f"L{i}" for i in range(6)]
+    for i, n in enumerate(names):
+        p.register(n, kv(torch, (2, 256, 16, 8, 128), torch.bfloat16, 30 + i), num_layers=6)
+    ids = list(range(0, 200))
+    hs = hashes_for("lw", 200)
+    p.save([(n, ids, hs) for n in names])
+    s = PyLoadState(len(names))
+    dst = list(range(40, 240))
+    p.e.batch_load_kv_blocks("inst", 0, 0, s.shm_name(), names, dst, hs)
+    for li in range(len(names)):
+        assert s.wait_layer(li, timeout_s=60), li
+    assert wait_state(s) == 1
+    assert all(s.layer_ready(i) for i in range(len(names)))
+    p.m.batch_load("inst", 0, 0, names, dst, hs)
+    p.check_caches()
+
+
 def test_load_errors_match_model(cuda, oracle):
     torch = cuda
     p = Pair(torch, oracle)

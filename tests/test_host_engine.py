@@ -136,3 +136,6 @@ def test_load_with_no_blocks_completes_immediately(engine):
     s = PyLoadState()
     engine.batch_load_kv_blocks("i", 0, 0, s.shm_name(), ["L0"], [], [])
     assert s.get_state() == 1
+    layered = PyLoadState(1)
+    engine.batch_load_kv_blocks("i", 0, 0, layered.shm_name(), ["L0"], [-1], [])
+    assert layered.get_state() == 1 and layered.layer_ready(0)

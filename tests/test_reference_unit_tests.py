@@ -86,6 +86,24 @@ def test_load_state_byte_layout_matches_reference(native):
     assert not (Path("/dev/shm") / name).exists(), "the creating handle unlinks on close"
 
 
+def test_load_state_layer_extension_keeps_version_1_bytes(native):
+    """The per-layer extension sits after the 32 version-1 bytes; a reader that
+    validates only those (sync_state.rs:244-292) attaches unchanged."""
+    from pegaflow_b200 import PyLoadState
+
+    s = PyLoadState(5)
+    raw = (Path("/dev/shm") / s.shm_name()).read_bytes()
+    assert len(raw) == 32 + 16 + 5 * 8
+    assert raw[0:8] == (8).to_bytes(8, "little") and raw[8:12] == (0x50464C44).to_bytes(4, "little")
+    assert raw[12:16] == (1).to_bytes(4, "little")
+    assert raw[32:36] == b"PFL2" and int.from_bytes(raw[36:40], "little") == 5
+    a = PyLoadState.attach(s.shm_name())
+    assert a.layer_count() == 5 and not any(a.layer_ready(i) for i in range(5))
+    assert PyLoadState().layer_count() == 0
+    a.close()
+    s.close()
+
+
 # --------------------------------------------------------------------------- allocator
 
 
