@@ -14,6 +14,8 @@ import importlib
 _EXPORTS = {
     "PegaEngine": ".engine",
     "PyLoadState": ".engine",
+    "EngineRpcClient": ".client",
+    "CudaIPCWrapper": ".ipc",
     "PegaError": "._native",
     "LIB_PATH": "._native",
     "Executor": ".transfer",

@@ -2,7 +2,7 @@
 
 #include <chrono>
 #include <cstdio>
-#include <set>
+#include <unordered_set>
 #include <utility>
 
 #include "common.h"
@@ -361,7 +361,7 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
     std::shared_ptr<DeviceWorker> worker;
   };
   std::vector<Planned> planned;
-  std::set<std::pair<std::string, uint64_t>> planned_slots;  // (hash, slot) inserted by earlier entries
+  std::unordered_map<uint64_t, std::unordered_set<std::string>> planned_slots;  // slot -> hashes planned
   std::exception_ptr pending;
   const auto t0 = Clock::now();
 
@@ -390,6 +390,8 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
       p.slot = slot;
       p.total_slots = total_slots;
       p.split = is_split_layout(reg);
+      std::vector<size_t> cand;
+      cand.reserve(e.block_ids.size());
       for (size_t i = 0; i < e.block_ids.size(); ++i) {
         const int32_t id = e.block_ids[i];
         if (id < 0) continue;
@@ -397,13 +399,20 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
           throw invalid_argument("block " + std::to_string(id) + " out of range for layer " + e.layer_name + " (" +
                                  std::to_string(reg.num_blocks) + " blocks registered)");
         }
-        const std::string& h = e.hashes[i];
-        const bool needs = !storage_->cache_contains(ns, h) && !storage_->inflight_has_slot(ns, h, slot) &&
-                           !planned_slots.count({h, slot});
-        if (needs) {
-          p.ids.push_back(id);
-          p.hashes.push_back(h);
-        }
+        cand.push_back(i);
+      }
+      // Dedup (lib.rs:613-616): not sealed, not inflight for this slot, and
+      // not planned for this slot by an earlier entry of this batch (which
+      // the reference would already have inserted).
+      const std::vector<char> needs = storage_->needs_save(ns, e.hashes, cand, slot);
+      const std::unordered_set<std::string>* earlier = nullptr;
+      auto ps = planned_slots.find(slot);
+      if (ps != planned_slots.end()) earlier = &ps->second;
+      for (size_t j = 0; j < cand.size(); ++j) {
+        const std::string& h = e.hashes[cand[j]];
+        if (!needs[j] || (earlier && earlier->count(h))) continue;
+        p.ids.push_back(e.block_ids[cand[j]]);
+        p.hashes.push_back(h);
       }
       if (p.ids.empty()) continue;
       const uint64_t n = p.ids.size();
@@ -419,7 +428,14 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
         if (!p.k_alloc) throw storage_error("pinned pool exhausted while allocating contiguous block buffer");
       }
       p.worker = gpu->worker;
-      for (const auto& h : p.hashes) planned_slots.insert({h, slot});
+      // Remember planned hashes only when another entry of this batch uses
+      // the same slot (a layer listed twice); usually none does.
+      for (size_t k = 0; k < saves.size(); ++k) {
+        if (&saves[k] != &e && saves[k].layer_name == e.layer_name && &saves[k] > &e) {
+          planned_slots[slot].insert(p.hashes.begin(), p.hashes.end());
+          break;
+        }
+      }
       planned.push_back(std::move(p));
     } catch (...) {
       pending = std::current_exception();
@@ -442,9 +458,10 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
     }
     worker->executor().save_sync(layers.data(), layers.size());
 
-    // LayerBlocks + insert_slot (lib.rs:687-705, 755-770).
+    // LayerBlocks + insert_slot (lib.rs:687-705, 755-770), one entry at a time.
     for (Planned& p : planned) {
       const uint64_t block_size = p.reg.bytes_per_block * p.reg.segments;
+      std::vector<LayerBlockPtr> blocks(p.ids.size());
       for (size_t i = 0; i < p.ids.size(); ++i) {
         auto lb = std::make_shared<LayerBlock>();
         if (p.split) {
@@ -457,8 +474,9 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
         }
         lb->size = block_size;
         lb->k_alloc = p.k_alloc;
-        storage_->insert_slot(ns, p.hashes[i], p.slot, std::move(lb), p.total_slots);
+        blocks[i] = std::move(lb);
       }
+      storage_->insert_slots(ns, p.hashes, p.slot, blocks, p.total_slots);
       counters_.save_bytes.fetch_add(block_size * p.ids.size());
       counters_.save_calls.fetch_add(1);
     }

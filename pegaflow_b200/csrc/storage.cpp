@@ -252,6 +252,91 @@ bool Storage::inflight_has_slot(const std::string& ns, const std::string& hash, 
   return slot < it->second.slots.size() && it->second.slots[slot] != nullptr;
 }
 
+std::vector<char> Storage::needs_save(const std::string& ns, const std::vector<std::string>& hashes,
+                                      const std::vector<size_t>& idx, uint64_t slot) {
+  std::vector<char> out(idx.size(), 1);
+  BlockKey key{ns, std::string()};
+  {
+    std::lock_guard<std::mutex> g(cache_mu_);
+    for (size_t j = 0; j < idx.size(); ++j) {
+      key.hash = hashes[idx[j]];
+      if (index_.count(key)) out[j] = 0;
+    }
+  }
+  std::lock_guard<std::mutex> g(inflight_mu_);
+  if (inflight_.empty()) return out;
+  for (size_t j = 0; j < idx.size(); ++j) {
+    if (!out[j]) continue;
+    key.hash = hashes[idx[j]];
+    auto it = inflight_.find(key);
+    if (it != inflight_.end() && slot < it->second.slots.size() && it->second.slots[slot]) out[j] = 0;
+  }
+  return out;
+}
+
+void Storage::insert_slots(const std::string& ns, const std::vector<std::string>& hashes, uint64_t slot,
+                           std::vector<LayerBlockPtr>& blocks, uint64_t total_slots) {
+  // Same per-block steps as insert_slot (storage.rs:457-514), with the locks
+  // taken once for the whole list instead of once per block.
+  std::vector<std::pair<BlockKey, SealedBlockPtr>> sealed;
+  {
+    std::unique_lock<std::mutex> gc(cache_mu_);
+    std::vector<char> cached(hashes.size(), 0);
+    BlockKey probe{ns, std::string()};
+    for (size_t i = 0; i < hashes.size(); ++i) {
+      probe.hash = hashes[i];
+      cached[i] = index_.count(probe) ? 1 : 0;
+    }
+    gc.unlock();
+    std::lock_guard<std::mutex> gi(inflight_mu_);
+    std::unordered_map<std::string, bool> sealed_here;  // a repeated hash finds its block sealed
+    for (size_t i = 0; i < hashes.size(); ++i) {
+      if (cached[i]) continue;
+      if (!sealed.empty() && sealed_here.count(hashes[i])) continue;
+      BlockKey key{ns, hashes[i]};
+      auto it = inflight_.find(key);
+      if (it == inflight_.end()) {
+        Inflight fresh;
+        fresh.slots.assign(total_slots, nullptr);
+        fresh.remaining = total_slots;
+        fresh.total_slots = total_slots;
+        it = inflight_.emplace(key, std::move(fresh)).first;
+      }
+      Inflight& ib = it->second;
+      if (slot < ib.slots.size() && ib.slots[slot]) continue;
+      if (total_slots != ib.total_slots) {
+        throw storage_error("slot count mismatch: expected " + std::to_string(ib.total_slots) + ", got " +
+                            std::to_string(total_slots));
+      }
+      if (slot >= ib.total_slots) {
+        throw storage_error("slot_id " + std::to_string(slot) + " out of bounds (" +
+                            std::to_string(ib.total_slots) + " slots)");
+      }
+      ib.footprint += blocks[i]->size;
+      ib.slots[slot] = std::move(blocks[i]);
+      ib.remaining -= 1;
+      if (ib.remaining == 0) {
+        auto sb = std::make_shared<SealedBlock>();
+        sb->slots = std::move(ib.slots);
+        sb->footprint = ib.footprint;
+        inflight_.erase(it);
+        sealed_here[key.hash] = true;
+        sealed.emplace_back(std::move(key), std::move(sb));
+      }
+    }
+  }
+  if (!sealed.empty()) {
+    std::lock_guard<std::mutex> g(cache_mu_);
+    for (auto& kv : sealed) {
+      if (cache_insert_locked(kv.first, std::move(kv.second))) {
+        counters_.insertions.fetch_add(1);
+      } else {
+        counters_.admission_rejections.fetch_add(1);
+      }
+    }
+  }
+}
+
 bool Storage::cache_insert_locked(const BlockKey& key, SealedBlockPtr block) {
   // TinyLfuCache::insert (cache.rs:66-90)
   if (lfu_) lfu_->incr(key);

@@ -121,6 +121,14 @@ class Storage {
   // allocator reports a large enough free region.
   std::shared_ptr<PoolAllocation> allocate(uint64_t size);
   bool inflight_has_slot(const std::string& ns, const std::string& hash, uint64_t slot);
+  // For each hash: !cache_contains && !inflight_has_slot, checked under one
+  // acquisition of each lock (the reference checks each block separately,
+  // lib.rs:613-616; the answers are the same).
+  std::vector<char> needs_save(const std::string& ns, const std::vector<std::string>& hashes,
+                               const std::vector<size_t>& idx, uint64_t slot);
+  // insert_slot for many (hash, block) pairs of one slot, in order.
+  void insert_slots(const std::string& ns, const std::vector<std::string>& hashes, uint64_t slot,
+                    std::vector<LayerBlockPtr>& blocks, uint64_t total_slots);
   // StorageEngine::insert_slot (storage.rs:457-514). Throws pf::Error(Storage)
   // on SlotOutOfBounds / SlotCountMismatch.
   bool insert_slot(const std::string& ns, const std::string& hash, uint64_t slot, LayerBlockPtr block,

@@ -1,0 +1,239 @@
+"""gRPC ``pegaflow.Engine`` server over the B200 engine.
+
+Restates the reference server (pegaflow-server/src): the seven RPCs of
+engine.proto on the same wire schema (pegaflow_b200.proto), the EngineError ->
+gRPC status mapping (service.rs:77-88), the CUDA IPC tensor registry that
+keeps the vLLM workers' KV tensors mapped in this process (registry.rs), and
+the command line (lib.rs:43-113). Run with ``python -m pegaflow_b200.server``.
+
+Not served: the DFS/Redis persistence tier and OTel export (their flags are
+accepted; --redis-url is refused).
+"""
+
+from __future__ import annotations
+
+import argparse
+import logging
+import threading
+from concurrent import futures
+from typing import Callable, Optional
+
+import grpc
+
+from . import proto as P
+
+log = logging.getLogger("pegaflow_b200.server")
+
+DEFAULT_ADDR = "127.0.0.1:50055"
+
+
+def parse_memory_size(s: str) -> int:
+    """Size with an optional kb/mb/gb/tb suffix (pegaflow-server/src/utils.rs:3-34)."""
+    s = s.strip()
+    boundary = next((i for i, c in enumerate(s) if c.isascii() and c.isalpha()), len(s))
+    num, unit = s[:boundary], s[boundary:]
+    try:
+        value = float(num.strip())
+    except ValueError:
+        raise ValueError(f"Invalid number: '{num}'") from None
+    if value < 0:
+        raise ValueError("Memory size cannot be negative")
+    unit = unit.strip().lower()
+    mult = {"": 1, "b": 1, "kb": 1 << 10, "mb": 1 << 20, "gb": 1 << 30, "tb": 1 << 40}.get(unit)
+    if mult is None:
+        raise ValueError(f"Unknown unit: '{unit}'. Use kb, mb, gb, or tb")
+    return int(value * mult)
+
+
+class TensorRegistry:
+    """KV tensors mapped from the workers' CUDA IPC handles, kept alive per
+    context "{instance}:tp{rank}:dev{device}" (registry.rs:30-175)."""
+
+    def __init__(self, materialize: Optional[Callable[[int, bytes], tuple]] = None):
+        self._materialize = materialize or self._from_ipc
+        self._contexts: dict[str, dict] = {}
+        self._lock = threading.Lock()
+
+    @staticmethod
+    def _from_ipc(device_id: int, wrapper_bytes: bytes):
+        import torch
+
+        from .ipc import loads_wrapper
+
+        torch.cuda.set_device(device_id)
+        tensor = loads_wrapper(wrapper_bytes).to_tensor()
+        device = tensor.device.index if tensor.device.index is not None else device_id
+        return tensor, tensor.data_ptr(), tensor.untyped_storage().nbytes(), device
+
+    def register_layer(self, context_key: str, layer_name: str, device_id: int, wrapper_bytes: bytes):
+        keep, data_ptr, size_bytes, device = self._materialize(device_id, wrapper_bytes)
+        with self._lock:
+            ctx = self._contexts.setdefault(context_key, {"device": device, "tensors": {}})
+            if ctx["device"] != device:
+                raise ValueError(f"context {context_key} is pinned to device {ctx['device']} but got {device}")
+            ctx["tensors"][layer_name] = keep
+        return data_ptr, size_bytes, device
+
+    def drop_instance(self, instance_id: str) -> int:
+        prefix = f"{instance_id}:"
+        with self._lock:
+            keys = [k for k in self._contexts if k.startswith(prefix)]
+            count = sum(len(self._contexts[k]["tensors"]) for k in keys)
+            for k in keys:
+                del self._contexts[k]
+        return count
+
+    def clear(self) -> None:
+        with self._lock:
+            self._contexts.clear()
+
+
+def _status_code(err) -> grpc.StatusCode:
+    """EngineError -> gRPC code (service.rs:77-88)."""
+    from . import _native as N
+
+    code = getattr(err, "code", None)
+    if code == N.PF_ERR_INVALID_ARGUMENT:
+        return grpc.StatusCode.INVALID_ARGUMENT
+    if code in (N.PF_ERR_INSTANCE_MISSING, N.PF_ERR_WORKER_MISSING, N.PF_ERR_TOPOLOGY_MISMATCH):
+        return grpc.StatusCode.FAILED_PRECONDITION
+    return grpc.StatusCode.INTERNAL
+
+
+class EngineService:
+    """Handlers of service pegaflow.Engine (service.rs:133-405)."""
+
+    def __init__(self, engine, registry: Optional[TensorRegistry] = None, on_shutdown: Optional[Callable] = None):
+        self.engine = engine
+        self.registry = registry or TensorRegistry()
+        self.on_shutdown = on_shutdown
+
+    @staticmethod
+    def _ok():
+        return P.ResponseStatus(ok=True, message="")
+
+    def _engine_call(self, context, fn, *args):
+        from ._native import PegaError
+
+        try:
+            return fn(*args)
+        except PegaError as e:
+            context.abort(_status_code(e), str(e))
+
+    def RegisterContext(self, req, context):
+        try:
+            data_ptr, size_bytes, device = self.registry.register_layer(
+                f"{req.instance_id}:tp{req.tp_rank}:dev{req.device_id}", req.layer_name, req.device_id,
+                req.wrapper_bytes)
+        except Exception as e:  # map_py_error (service.rs:90-93)
+            context.abort(grpc.StatusCode.INTERNAL, f"register tensor failed: {e}")
+        self._engine_call(context, self.engine.register_context_layer, req.instance_id, req.namespace, device,
+                          req.layer_name, data_ptr, size_bytes, req.num_blocks, req.bytes_per_block,
+                          req.kv_stride_bytes, req.segments, req.tp_rank, req.tp_size, req.num_layers)
+        return P.RegisterContextResponse(status=self._ok())
+
+    def Save(self, req, context):
+        saves = [(s.layer_name, list(s.block_ids), list(s.block_hashes)) for s in req.saves]
+        self._engine_call(context, self.engine.batch_save_kv_blocks, req.instance_id, req.tp_rank, req.device_id,
+                          saves)
+        return P.SaveResponse(status=self._ok())
+
+    def Load(self, req, context):
+        self._engine_call(context, self.engine.batch_load_kv_blocks, req.instance_id, req.tp_rank, req.device_id,
+                          req.load_state_shm, list(req.layer_names), list(req.block_ids), list(req.block_hashes))
+        return P.LoadResponse(status=self._ok())
+
+    def Query(self, req, context):
+        hits = self._engine_call(context, self.engine.count_prefix_hit_blocks, req.instance_id,
+                                 list(req.block_hashes))
+        return P.QueryResponse(status=self._ok(), hit_blocks=hits, prefetch_state=P.PREFETCH_READY,
+                               loading_blocks=0, missing_blocks=0)
+
+    def UnregisterContext(self, req, context):
+        dropped = self.registry.drop_instance(req.instance_id)
+        if dropped:
+            log.info("Dropped %d CUDA tensors for instance %s", dropped, req.instance_id)
+        self._engine_call(context, self.engine.unregister_instance, req.instance_id)
+        return P.UnregisterResponse(status=self._ok())
+
+    def Shutdown(self, req, context):
+        self.registry.clear()
+        log.warning("Shutdown requested via RPC")
+        if self.on_shutdown:
+            threading.Thread(target=self.on_shutdown, daemon=True).start()
+        return P.ShutdownResponse(status=self._ok())
+
+    def Health(self, req, context):
+        return P.HealthResponse(status=self._ok())
+
+    def handler(self) -> grpc.GenericRpcHandler:
+        methods = {}
+        for rpc, (req_name, resp_name) in P.METHODS.items():
+            methods[rpc] = grpc.unary_unary_rpc_method_handler(
+                getattr(self, rpc), request_deserializer=P.M[req_name].FromString,
+                response_serializer=P.M[resp_name].SerializeToString)
+        return grpc.method_handlers_generic_handler(P.SERVICE, methods)
+
+
+def serve(engine, addr: str = DEFAULT_ADDR, registry: Optional[TensorRegistry] = None, max_workers: int = 32):
+    """Start the service on `addr`; returns (server, service, bound port)."""
+    server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers),
+                         options=[("grpc.max_receive_message_length", 256 << 20),
+                                  ("grpc.max_send_message_length", 256 << 20)])
+    service = EngineService(engine, registry, on_shutdown=lambda: server.stop(grace=1.0))
+    server.add_generic_rpc_handlers((service.handler(),))
+    port = server.add_insecure_port(addr)
+    if port == 0:
+        raise RuntimeError(f"cannot bind {addr}")
+    server.start()
+    return server, service, port
+
+
+def build_parser() -> argparse.ArgumentParser:
+    ap = argparse.ArgumentParser(prog="pegaflow_b200.server",
+                                 description="PegaEngine gRPC server with CUDA IPC registry (B200 engine)")
+    ap.add_argument("--addr", default=DEFAULT_ADDR)
+    ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--pool-size", type=parse_memory_size, default=parse_memory_size("30gb"))
+    ap.add_argument("--hint-value-size", type=parse_memory_size, default=None)
+    ap.add_argument("--use-hugepages", action="store_true")
+    ap.add_argument("--pre-evict", action="store_true")
+    ap.add_argument("--pre-evict-threshold", type=parse_memory_size, default=parse_memory_size("5gb"))
+    ap.add_argument("--pre-evict-target", type=parse_memory_size, default=parse_memory_size("8gb"))
+    ap.add_argument("--pre-evict-interval-ms", type=int, default=100)
+    ap.add_argument("--disable-lfu-admission", action="store_true")
+    ap.add_argument("--metrics-otel-endpoint", default="http://127.0.0.1:4321")
+    ap.add_argument("--metrics-period-secs", type=int, default=5)
+    ap.add_argument("--log-level", default="info")
+    ap.add_argument("--redis-url", default=None)
+    ap.add_argument("--dfs-root", default="/tmp/pega")
+    ap.add_argument("--dfs-quota", type=parse_memory_size, default=parse_memory_size("50gb"))
+    ap.add_argument("--dfs-scan-interval-ms", type=int, default=100)
+    return ap
+
+
+def main(argv=None) -> int:
+    args = build_parser().parse_args(argv)
+    logging.basicConfig(level=getattr(logging, args.log_level.upper(), logging.INFO),
+                        format="%(asctime)s %(levelname)s %(name)s: %(message)s")
+    if args.redis_url:
+        raise SystemExit("--redis-url: the DFS/Redis persistence tier is not part of this build")
+    import torch
+
+    if torch.cuda.is_available():
+        torch.cuda.init()
+        torch.cuda.set_device(args.device)
+    from .engine import PegaEngine
+
+    pre_evict = (args.pre_evict_threshold, args.pre_evict_target, args.pre_evict_interval_ms) if args.pre_evict else None
+    engine = PegaEngine(args.pool_size, args.use_hugepages, enable_lfu_admission=not args.disable_lfu_admission,
+                        hint_value_size_bytes=args.hint_value_size or 0, pre_evict=pre_evict)
+    server, _, port = serve(engine, args.addr)
+    log.info("pegaflow_b200 engine server listening on %s (port %d)", args.addr, port)
+    server.wait_for_termination()
+    engine.close()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
