@@ -286,6 +286,110 @@ def run_reference_arm(args, wl) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_pd(args) -> None:
+    """Qwen3-8B-shaped prefill -> decode handoff in one
+    process over two GPUs. 36 layers of KV-first [2, 2048, 16, 8, 128] bf16 on
+    each GPU; 200 requests x 313 blocks, each moved from seeded block ids on
+    GPU0 into seeded free ids on GPU1. Three ways: NVLink P2P pull (kernel on
+    GPU1 reads GPU0), P2P push (kernel on GPU0 writes GPU1), and the host-pool
+    bounce (save on GPU0 + load on GPU1). Device-timed per request."""
+    import torch
+
+    from pegaflow_b200 import Executor, Layout, LoadSpec, P2PSpec, PinnedBuffer, SaveSpec
+
+    if torch.cuda.device_count() < 2:
+        print(json.dumps({"metric": METRIC, "workload": "qwen3_pd", "unavailable": "needs 2 GPUs in one process"}))
+        return
+    layers, nb, n, requests = 36, 2048, 313, args.pd_requests
+    g0 = torch.Generator(device="cuda:0").manual_seed(7)
+    g1 = torch.Generator(device="cuda:1").manual_seed(8)
+    src = [torch.randn((2, nb, 16, 8, 128), generator=g0, device="cuda:0").to(torch.bfloat16) for _ in range(layers)]
+    dst = [torch.randn((2, nb, 16, 8, 128), generator=g1, device="cuda:1").to(torch.bfloat16) for _ in range(layers)]
+    reqs = [(np.random.default_rng(4 + r).permutation(nb)[:n], np.random.default_rng(10_000 + r).permutation(nb)[:n])
+            for r in range(requests)]
+    payload = n * layers * 2 * 32768
+    ex0, ex1 = Executor(0), Executor(1)
+    s0, s1 = torch.cuda.Stream("cuda:0"), torch.cuda.Stream("cuda:1")
+    sl, dl = [Layout.from_tensor(t) for t in src], [Layout.from_tensor(t) for t in dst]
+
+    # Peer copy peak (1 GiB, best of 3) for the NVLink roofline.
+    a = torch.empty(1 << 30, dtype=torch.uint8, device="cuda:0")
+    b = torch.empty(1 << 30, dtype=torch.uint8, device="cuda:1")
+    peak = 0.0
+    for _ in range(4):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s1):
+            e0.record(s1)
+            b.copy_(a, non_blocking=True)
+            e1.record(s1)
+        e1.synchronize()
+        peak = max(peak, (1 << 30) / (e0.elapsed_time(e1) / 1e3) / 1e9)
+    del a, b
+
+    def timed(fn, stream, reps):
+        ms = []
+        for r in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn(r, stream)
+            e1.record(stream)
+            ms.append((e0, e1))
+        torch.cuda.synchronize(0)
+        torch.cuda.synchronize(1)
+        return [x.elapsed_time(y) for x, y in ms]
+
+    def pull(r, stream):
+        si, di = reqs[r]
+        ex1.p2p([P2PSpec(x, y, si, di) for x, y in zip(sl, dl)], 0, push=False, stream=stream.cuda_stream)
+
+    def push(r, stream):
+        si, di = reqs[r]
+        ex0.p2p([P2PSpec(x, y, si, di) for x, y in zip(sl, dl)], 1, push=True, stream=stream.cuda_stream)
+
+    pool = PinnedBuffer(payload + layers * 4096, write_combined=True)
+    saves, loads = [], []
+    off = 0
+    for x, y in zip(sl, dl):
+        k, v = pool.ptr + off, pool.ptr + off + n * 32768
+        ks = np.arange(n, dtype=np.uint64) * 32768 + k
+        saves.append((x, k, v))
+        loads.append((y, ks, ks + n * 32768))
+        off += 2 * n * 32768 + 4096
+
+    def bounce(r, stream):
+        si, di = reqs[r]
+        go = torch.cuda.Event()
+        go.record(stream)  # the save starts after the request's start event
+        s0.wait_event(go)
+        ex0.save([SaveSpec(x, si, k, v) for x, k, v in saves], stream=s0.cuda_stream)
+        ev = torch.cuda.Event()
+        ev.record(s0)
+        stream.wait_event(ev)
+        ex1.load([LoadSpec(y, di, ks, vs) for y, ks, vs in loads], stream=stream.cuda_stream)
+
+    for fn in (pull, push, bounce):
+        timed(fn, s1 if fn is not push else s0, min(3, requests))
+    res = {}
+    for name, fn, st in (("p2p_pull", pull, s1), ("p2p_push", push, s0), ("host_pool", bounce, s1)):
+        reps = requests if name != "host_pool" else min(requests, args.pd_bounce_requests)
+        ms = timed(fn, st, reps)
+        res[name] = {"GBps": round(payload * reps / (sum(ms) / 1e3) / 1e9, 2),
+                     "p50_request_ms": round(statistics.median(ms), 3), "requests": reps}
+    best = max(("p2p_pull", "p2p_push"), key=lambda k: res[k]["GBps"])
+    line = {
+        "metric": METRIC, "value": res[best]["GBps"], "unit": "GB/s", "n_gpus": 2, "steps": requests,
+        "warmup": 3, "ms_per_step": res[best]["p50_request_ms"], "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded ~N(0,1) bf16 KV)",
+        "config": {"workload": "qwen3_pd", "desc": "Qwen3-8B P/D handoff: 36 layers, [2,2048,16,8,128] bf16 per GPU, "
+                   f"{requests} requests x 313 blocks, GPU0 -> GPU1", "payload_bytes_per_request": payload},
+        "best": best, "p2p_pull": res["p2p_pull"], "p2p_push": res["p2p_push"], "host_pool_bounce": res["host_pool"],
+        "nvlink": {"peer_copy_peak_GBps": round(peak, 1), "frac": round(res[best]["GBps"] / peak, 3),
+                   "how": "1 GiB cudaMemcpyPeer GPU0->GPU1, best of 4"},
+        "gpu_launches": ex0.stats()["kernel_launches"] + ex1.stats()["kernel_launches"],
+    }
+    print(json.dumps(line), flush=True)
+
+
 def config_block(args, wl) -> dict:
     return {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
             "blocks_moved": wl["blocks"], "block_ids": args.order, "kv_dtype": "fp16" if wl.get("separate") else "bf16",
@@ -303,7 +407,9 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama8b")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["qwen3_pd"], default="llama8b")
+    ap.add_argument("--pd-requests", type=int, default=200)
+    ap.add_argument("--pd-bounce-requests", type=int, default=20)
     ap.add_argument("--order", choices=["shuffled", "sorted"], default="shuffled")
     ap.add_argument("--save-mode", default="auto", choices=["auto", "staged", "direct"])
     ap.add_argument("--load-mode", default="auto", choices=["auto", "staged", "direct"])
@@ -318,6 +424,14 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling runs)")
     args = ap.parse_args()
+    if args.workload == "qwen3_pd":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": "qwen3_pd",
+                              "unavailable": "the reference hands P/D blocks over through its host pool; "
+                                             "see host_pool_bounce in the b200 line"}))
+            return 0
+        run_pd(args)
+        return 0
     wl = dict(WORKLOADS[args.workload])
     if args.layers:
         wl["layers"] = args.layers
@@ -495,8 +609,10 @@ def main() -> int:
             "reference_copy_path": ref,
             "cpu_baseline": cpu,
             "clocks": clocks,
-            "engine_metrics": {k: eng_metrics[k] for k in ("save_bytes", "load_bytes", "load_failures",
-                                                           "cache_block_evictions")},
+            "engine_metrics": {k: (round(eng_metrics[k], 2) if isinstance(eng_metrics[k], float) else eng_metrics[k])
+                               for k in ("save_bytes", "load_bytes", "load_failures", "cache_block_evictions",
+                                         "save_plan_ms", "save_transfer_ms", "save_insert_ms", "save_ms",
+                                         "load_ms")},
         }
         print(json.dumps(line), flush=True)
     ranks.close()

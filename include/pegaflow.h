@@ -155,6 +155,27 @@ int pf_save_blocks_async(pf_executor* exec, const pf_save_layer* layers,
 int pf_load_blocks_async(pf_executor* exec, const pf_load_layer* layers,
                          uint64_t n_layers, void* stream, int64_t* layer_done);
 
+/* Prefill -> decode handoff between two GPUs over NVLink, paged cache to
+ * paged cache (no reference counterpart: the reference hands P/D blocks over
+ * through its host pool, docs/pd.md:20-27). For every layer, block
+ * src_idx[i] of `src` (on the source GPU) lands in block dst_idx[i] of `dst`
+ * (on the destination GPU); both layouts must have the same bytes_per_block,
+ * segments and K/V split. One kernel moves the bytes with 16-byte peer loads
+ * (pull: runs on the destination GPU, exec is its executor) or peer stores
+ * (push: runs on the source GPU). A destination listed twice keeps the later
+ * block. Work is ordered after `stream` and `stream` waits for it (NULL =
+ * blocking call). Peer access between the two devices is enabled on first
+ * use; PF_ERR_INVALID_ARGUMENT when the devices cannot reach each other. */
+typedef struct pf_p2p_layer {
+  pf_layer_desc src;
+  pf_layer_desc dst;
+  const int64_t* src_idx;
+  const int64_t* dst_idx;
+  uint64_t n;
+} pf_p2p_layer;
+int pf_p2p_transfer(pf_executor* exec, int32_t peer_device, int push,
+                    const pf_p2p_layer* layers, uint64_t n_layers, void* stream);
+
 /* Save without allocating: for callers that cannot call cudaMalloc while
  * they save, e.g. an inference engine whose caching allocator or KV pool owns
  * all free HBM, or code under a pool policy that forbids out-of-band device
@@ -184,6 +205,7 @@ typedef struct pf_executor_stats {
   uint64_t kernel_bytes;
   double kernel_ms;
   uint64_t timed_launches;
+  uint64_t bytes_p2p;       /* payload moved by pf_p2p_transfer */
 } pf_executor_stats;
 int pf_executor_stats_get(pf_executor* exec, pf_executor_stats* out);
 int pf_executor_stats_reset(pf_executor* exec);
@@ -386,6 +408,9 @@ typedef struct pf_engine_metrics {
   uint64_t pool_alloc_failures;
   uint64_t inflight_blocks;
   uint64_t cached_blocks;
+  double save_plan_ms;      /* dedup + pool allocation (host) */
+  double save_transfer_ms;  /* pack kernels + D2H, waited on */
+  double save_insert_ms;    /* slot bookkeeping after the copy (host) */
 } pf_engine_metrics;
 int pf_engine_metrics_get(pf_engine* e, pf_engine_metrics* out);
 

@@ -22,6 +22,7 @@ _EXPORTS = {
     "Layout": ".transfer",
     "LoadSpec": ".transfer",
     "SaveSpec": ".transfer",
+    "P2PSpec": ".transfer",
     "PinnedBuffer": ".transfer",
     "refcopy_save": ".transfer",
     "refcopy_load": ".transfer",

@@ -100,6 +100,17 @@ class ExecutorStats(Structure):
         ("kernel_bytes", c_uint64),
         ("kernel_ms", c_double),
         ("timed_launches", c_uint64),
+        ("bytes_p2p", c_uint64),
+    ]
+
+
+class P2PLayer(Structure):
+    _fields_ = [
+        ("src", LayerDesc),
+        ("dst", LayerDesc),
+        ("src_idx", POINTER(c_int64)),
+        ("dst_idx", POINTER(c_int64)),
+        ("n", c_uint64),
     ]
 
 
@@ -151,6 +162,9 @@ class EngineMetrics(Structure):
         ("pool_alloc_failures", c_uint64),
         ("inflight_blocks", c_uint64),
         ("cached_blocks", c_uint64),
+        ("save_plan_ms", c_double),
+        ("save_transfer_ms", c_double),
+        ("save_insert_ms", c_double),
     ]
 
 
@@ -169,6 +183,7 @@ _SIGNATURES = {
     "pf_save_blocks_async": (c_int, [c_void_p, POINTER(SaveLayer), c_uint64, c_void_p]),
     "pf_load_blocks_async": (c_int, [c_void_p, POINTER(LoadLayer), c_uint64, c_void_p, c_void_p]),
     "pf_save_blocks_noalloc": (c_int, [c_int32, POINTER(SaveLayer), c_uint64, c_void_p]),
+    "pf_p2p_transfer": (c_int, [c_void_p, c_int32, c_int, POINTER(P2PLayer), c_uint64, c_void_p]),
     "pf_executor_stats_get": (c_int, [c_void_p, POINTER(ExecutorStats)]),
     "pf_executor_stats_reset": (c_int, [c_void_p]),
     "pf_executor_set_timing": (c_int, [c_void_p, c_int]),

@@ -130,6 +130,18 @@ int pf_load_blocks_async(pf_executor* exec, const pf_load_layer* layers, uint64_
   return guarded([&] { exec->get().load(layers, n_layers, static_cast<cudaStream_t>(stream), layer_done); });
 }
 
+int pf_p2p_transfer(pf_executor* exec, int32_t peer_device, int push, const pf_p2p_layer* layers,
+                    uint64_t n_layers, void* stream) {
+  if (!exec || (!layers && n_layers)) return null_arg("executor or layers");
+  return guarded([&] {
+    if (stream) {
+      exec->get().p2p(layers, n_layers, peer_device, push != 0, static_cast<cudaStream_t>(stream));
+    } else {
+      exec->get().p2p_sync(layers, n_layers, peer_device, push != 0);
+    }
+  });
+}
+
 int pf_executor_stats_get(pf_executor* exec, pf_executor_stats* out) {
   if (!exec || !out) return null_arg("argument");
   return guarded([&] { exec->get().stats(out); });

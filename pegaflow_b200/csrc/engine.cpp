@@ -456,12 +456,18 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
       s.k_dst = p.k_alloc->ptr;
       s.v_dst = p.split ? p.v_alloc->ptr : nullptr;
     }
-    worker->executor().save_sync(layers.data(), layers.size());
+    const auto t_plan = Clock::now();
+    Executor& ex = worker->executor();
+    ex.save(layers.data(), layers.size(), ex.own_stream());
 
-    // LayerBlocks + insert_slot (lib.rs:687-705, 755-770), one entry at a time.
-    for (Planned& p : planned) {
+    // LayerBlocks (lib.rs:687-698, 755-763) are built while the copy runs;
+    // their slots are inserted once the bytes are in the pool.
+    std::vector<std::vector<LayerBlockPtr>> built(planned.size());
+    for (size_t k = 0; k < planned.size(); ++k) {
+      Planned& p = planned[k];
       const uint64_t block_size = p.reg.bytes_per_block * p.reg.segments;
-      std::vector<LayerBlockPtr> blocks(p.ids.size());
+      std::vector<LayerBlockPtr>& blocks = built[k];
+      blocks.resize(p.ids.size());
       for (size_t i = 0; i < p.ids.size(); ++i) {
         auto lb = std::make_shared<LayerBlock>();
         if (p.split) {
@@ -476,12 +482,22 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
         lb->k_alloc = p.k_alloc;
         blocks[i] = std::move(lb);
       }
-      storage_->insert_slots(ns, p.hashes, p.slot, blocks, p.total_slots);
-      counters_.save_bytes.fetch_add(block_size * p.ids.size());
+    }
+    cuda_check(cudaStreamSynchronize(ex.own_stream()), "cudaStreamSynchronize(save)");
+    const auto t_xfer = Clock::now();
+
+    // insert_slot (lib.rs:700-705, 765-770), one entry at a time.
+    for (size_t k = 0; k < planned.size(); ++k) {
+      Planned& p = planned[k];
+      storage_->insert_slots(ns, p.hashes, p.slot, built[k], p.total_slots);
+      counters_.save_bytes.fetch_add(p.reg.bytes_per_block * p.reg.segments * p.ids.size());
       counters_.save_calls.fetch_add(1);
     }
     std::lock_guard<std::mutex> g(counters_.ms_mu);
     counters_.save_ms += ms_since(t0);
+    counters_.save_plan_ms += std::chrono::duration<double, std::milli>(t_plan - t0).count();
+    counters_.save_transfer_ms += std::chrono::duration<double, std::milli>(t_xfer - t_plan).count();
+    counters_.save_insert_ms += ms_since(t_xfer);
   }
   if (pending) std::rethrow_exception(pending);
 }
@@ -592,6 +608,9 @@ void Engine::metrics(pf_engine_metrics* out) {
     std::lock_guard<std::mutex> g(counters_.ms_mu);
     out->save_ms = counters_.save_ms;
     out->load_ms = counters_.load_ms;
+    out->save_plan_ms = counters_.save_plan_ms;
+    out->save_transfer_ms = counters_.save_transfer_ms;
+    out->save_insert_ms = counters_.save_insert_ms;
   }
   auto& sc = storage_->counters();
   out->cache_block_insertions = sc.insertions.load();

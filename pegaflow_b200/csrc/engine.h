@@ -35,6 +35,7 @@ struct EngineCounters {
   std::atomic<uint64_t> hits{0}, misses{0};
   std::mutex ms_mu;
   double save_ms = 0, load_ms = 0;
+  double save_plan_ms = 0, save_transfer_ms = 0, save_insert_ms = 0;
 };
 
 // One load task (gpu_worker.rs:12-28): layers with the LayerBlocks they read,

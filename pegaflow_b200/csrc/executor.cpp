@@ -466,6 +466,133 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
   }
 }
 
+void Executor::build_p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push, Built* b) {
+  uint32_t unit_base = 0;
+  for (uint64_t li = 0; li < n_layers; ++li) {
+    const pf_p2p_layer& s = layers[li];
+    const std::string lname = "#" + std::to_string(li);
+    validate_layout(s.src, (lname + ".src").c_str());
+    validate_layout(s.dst, (lname + ".dst").c_str());
+    if (s.n == 0) continue;
+    if (!s.src_idx || !s.dst_idx) throw invalid_argument("null block list");
+    if (s.src.bytes_per_block != s.dst.bytes_per_block || s.src.segments != s.dst.segments ||
+        is_split_layout(s.src) != is_split_layout(s.dst)) {
+      throw invalid_argument("source and destination layouts differ for layer " + lname);
+    }
+    if (!is_split_layout(s.src) && !is_contiguous_layout(s.src)) {
+      throw invalid_argument("peer transfer needs split K/V or contiguous layouts (layer " + lname + ")");
+    }
+    if (s.src.num_blocks > 0xffffffffull || s.dst.num_blocks > 0xffffffffull || s.n > 0xffffffffull) {
+      throw invalid_argument("too many blocks for one layer");
+    }
+    const pf_layer_desc& local = push ? s.src : s.dst;
+    const pf_layer_desc& remote = push ? s.dst : s.src;
+    const int64_t* local_ids = push ? s.src_idx : s.dst_idx;
+    const int64_t* remote_ids = push ? s.dst_idx : s.src_idx;
+    check_device_range(device_, local);
+    check_device_range(peer, remote);
+    const UnitGeometry gl = save_geometry(local);
+    const UnitGeometry gr = save_geometry(remote);
+    if (gl.unit_bytes > kMaxUnitBytes) throw invalid_argument("block larger than 2 GiB");
+    for (uint64_t i = 0; i < s.n; ++i) {
+      for (int side = 0; side < 2; ++side) {
+        const pf_layer_desc& l = side ? s.dst : s.src;
+        const int64_t bi = side ? s.dst_idx[i] : s.src_idx[i];
+        if (bi < 0 || static_cast<uint64_t>(bi) >= l.num_blocks) {
+          throw invalid_argument("block " + std::to_string(bi) + " out of range for layer " + lname +
+                                 (side ? ".dst" : ".src") + " (" + std::to_string(l.num_blocks) +
+                                 " blocks registered)");
+        }
+        const UnitGeometry& g = (&l == &local) ? gl : gr;
+        for (uint32_t u = 0; u < g.units; ++u) check_unit_range(l, static_cast<uint64_t>(bi), u, g);
+      }
+    }
+    // A destination block listed twice keeps the later source block.
+    const int64_t* dst_ids = s.dst_idx;
+    std::vector<uint64_t> seen((s.dst.num_blocks >> 6) + 1, 0);
+    std::vector<uint64_t> keep;
+    for (uint64_t i = s.n; i-- > 0;) {
+      const uint64_t d = static_cast<uint64_t>(dst_ids[i]);
+      if (seen[d >> 6] & (1ull << (d & 63))) continue;
+      seen[d >> 6] |= 1ull << (d & 63);
+      keep.push_back(i);
+    }
+    std::reverse(keep.begin(), keep.end());
+    const uint64_t n = keep.size();
+
+    PlanLayer p{};
+    p.cache_base = local.data_ptr;
+    p.block_pitch = local.bytes_per_block;
+    p.unit_stride = gl.unit_stride;
+    p.unit_bytes = static_cast<uint32_t>(gl.unit_bytes);
+    p.units = gl.units;
+    p.n = static_cast<uint32_t>(n);
+    p.tiles_per_unit = static_cast<uint32_t>((gl.unit_bytes + kTileBytes - 1) / kTileBytes);
+    p.tile_start = b->total_tiles;
+    p.tile_count = static_cast<uint64_t>(gl.units) * n * p.tiles_per_unit;
+    if (p.tile_count > 0xffffffffull) throw invalid_argument("layer transfer too large for one plan");
+    p.ids_off = static_cast<uint32_t>(b->ids.size());
+    p.side_off = static_cast<uint32_t>(b->side_base.size());
+    p.unit_off = unit_base;
+    p.done_index = static_cast<uint32_t>(li);
+    p.side_pitch = gl.unit_bytes;
+    bool vec = aligned16(local.data_ptr) && aligned16(local.bytes_per_block) && aligned16(gl.unit_stride) &&
+               aligned16(gl.unit_bytes) && aligned16(remote.data_ptr) && aligned16(gr.unit_stride);
+    for (uint32_t u = 0; u < gl.units; ++u) b->side_base.push_back(0);
+    for (uint64_t j = 0; j < n; ++j) b->ids.push_back(static_cast<uint32_t>(local_ids[keep[j]]));
+    for (uint32_t u = 0; u < gl.units; ++u) {
+      for (uint64_t j = 0; j < n; ++j) {
+        const uint64_t rb = static_cast<uint64_t>(remote_ids[keep[j]]);
+        b->side_ptrs.push_back(remote.data_ptr + rb * remote.bytes_per_block + u * gr.unit_stride);
+      }
+    }
+    p.flags = vec ? kFlagVector : 0u;
+    b->total_tiles += p.tile_count;
+    b->total_bytes += static_cast<uint64_t>(gl.units) * n * gl.unit_bytes;
+    unit_base += gl.units * static_cast<uint32_t>(n);
+    b->layers.push_back(p);
+  }
+}
+
+void Executor::enable_peer(int peer) {
+  if (peer == device_) return;  // same-device copies need no peer mapping
+  if (std::find(peers_enabled_.begin(), peers_enabled_.end(), peer) != peers_enabled_.end()) return;
+  int can = 0;
+  cuda_check(cudaDeviceCanAccessPeer(&can, device_, peer), "cudaDeviceCanAccessPeer");
+  if (!can) {
+    throw invalid_argument("device " + std::to_string(device_) + " cannot access device " + std::to_string(peer));
+  }
+  const cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+  } else {
+    cuda_check(e, "cudaDeviceEnablePeerAccess");
+  }
+  peers_enabled_.push_back(peer);
+}
+
+void Executor::p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push, cudaStream_t caller) {
+  std::lock_guard<std::mutex> g(mu_);
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  enable_peer(peer);
+  Built b;
+  build_p2p(layers, n_layers, peer, push, &b);
+  if (b.total_tiles == 0) return;
+  cuda_check(cudaEventRecord(ev_start_, caller), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(kstream_, ev_start_, 0), "cudaStreamWaitEvent");
+  const CopyArgs args = upload(b, false, kstream_);
+  launch(push ? kPack : kUnpack, true, args, 0, b.total_tiles, 0, kstream_);
+  cuda_check(cudaEventRecord(ev_done_, kstream_), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(caller, ev_done_, 0), "cudaStreamWaitEvent");
+  stats_.kernel_bytes += b.total_bytes;  // local HBM side; the other side crosses NVLink
+  stats_.bytes_p2p += b.total_bytes;
+}
+
+void Executor::p2p_sync(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push) {
+  p2p(layers, n_layers, peer, push, own_stream_);
+  cuda_check(cudaStreamSynchronize(own_stream_), "cudaStreamSynchronize(p2p)");
+}
+
 namespace {
 void CUDART_CB raise_flag(void* p) { *static_cast<volatile int64_t*>(p) = 1; }
 }  // namespace

@@ -39,11 +39,17 @@ class Executor {
   Executor& operator=(const Executor&) = delete;
 
   int device() const { return device_; }
+  // The executor's private stream (used by the blocking wrappers).
+  cudaStream_t own_stream() const { return own_stream_; }
 
   // Enqueue a save/load ordered after `caller`; `caller` waits for completion.
   void save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t caller);
   void load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t caller,
             int64_t* layer_done);
+  // Paged-to-paged copy between this device and `peer` over NVLink. pull:
+  // this device holds the destination; push: this device holds the source.
+  void p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push, cudaStream_t caller);
+  void p2p_sync(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push);
   // Blocking wrappers on the executor's own stream.
   void save_sync(const pf_save_layer* layers, uint64_t n_layers);
   void load_sync(const pf_load_layer* layers, uint64_t n_layers, int64_t* layer_done = nullptr);
@@ -82,6 +88,8 @@ class Executor {
 
   void build_save(const pf_save_layer* layers, uint64_t n, bool staged, Built* b);
   void build_load(const pf_load_layer* layers, uint64_t n, bool staged, Built* b);
+  void build_p2p(const pf_p2p_layer* layers, uint64_t n, int peer, bool push, Built* b);
+  void enable_peer(int peer);
   void make_chunks(const Built& b, std::vector<Chunk>* chunks);
   CopyArgs upload(const Built& b, bool with_counters, cudaStream_t s);
   void launch(Dir dir, bool table, const CopyArgs& args, uint64_t tile_begin,
@@ -110,6 +118,7 @@ class Executor {
   bool plan_pending_ = false;
 
   std::mutex mu_;
+  std::vector<int> peers_enabled_;
   bool timing_ = false;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed_;  // pending kernel spans
   std::vector<cudaEvent_t> event_pool_;

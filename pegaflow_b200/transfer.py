@@ -86,6 +86,34 @@ class LoadSpec:
     v_src: Optional[np.ndarray] = None
 
 
+@dataclass
+class P2PSpec:
+    """One layer of a GPU-to-GPU handoff: block src_idx[i] of `src` lands in
+    block dst_idx[i] of `dst` (same bytes_per_block, segments and K/V split)."""
+
+    src: Layout
+    dst: Layout
+    src_idx: np.ndarray
+    dst_idx: np.ndarray
+
+
+def _p2p_array(specs: Sequence[P2PSpec]):
+    arr = (N.P2PLayer * max(1, len(specs)))()
+    keep = []
+    for i, s in enumerate(specs):
+        a = np.ascontiguousarray(s.src_idx, dtype=np.int64)
+        b = np.ascontiguousarray(s.dst_idx, dtype=np.int64)
+        if a.size != b.size:
+            raise ValueError("src_idx and dst_idx differ in length")
+        keep += [a, b]
+        arr[i].src = s.src.c()
+        arr[i].dst = s.dst.c()
+        arr[i].src_idx = a.ctypes.data_as(POINTER(c_int64))
+        arr[i].dst_idx = b.ctypes.data_as(POINTER(c_int64))
+        arr[i].n = a.size
+    return arr, keep
+
+
 def _save_array(specs: Sequence[SaveSpec]):
     arr = (N.SaveLayer * max(1, len(specs)))()
     keep = []
@@ -188,6 +216,16 @@ class Executor:
                     self._h, arr, len(specs), c_void_p(stream or 0), c_void_p(layer_done) if layer_done else None
                 )
             )
+        del keep
+
+    def p2p(self, specs: Sequence[P2PSpec], peer_device: int, push: bool = False,
+            stream: Optional[int] = None) -> None:
+        """GPU-to-GPU paged copy over NVLink. pull (default): this executor's
+        device holds the destinations and reads the peer's blocks; push: this
+        device holds the sources and writes into the peer's blocks."""
+        arr, keep = _p2p_array(specs)
+        N.check(N.lib.pf_p2p_transfer(self._h, peer_device, 1 if push else 0, arr, len(specs),
+                                      c_void_p(stream) if stream else None))
         del keep
 
     def stats(self) -> dict:
