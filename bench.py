@@ -390,6 +390,125 @@ def run_pd(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_fp8_evict(args) -> None:
+    """mixed warm/cold restore under eviction, through the
+    engine API. Llama-3.1-8B shape with fp8 (e4m3 bit patterns) KV, 32 layers
+    [2, 2048, 16, 8, 128] uint8 plus one fp32 scale per block per layer (32
+    more layers [2048] fp32, 4-byte units); 64 requests with prefixes of
+    U[1K, 16K] tokens (seed 6), the first half of each request's blocks saved
+    beforehand; 30 GB pool with LRU eviction (admission off). Per request: the
+    warm prefix is restored layer by layer while a dummy per-layer compute
+    kernel (0.5 ms) runs on a second stream as soon as its layer is in place,
+    then the cold half is saved. Compared with waiting for the whole load
+    before computing."""
+    import torch
+
+    from pegaflow_b200 import Layout, PegaEngine, PyLoadState
+
+    torch.cuda.set_device(0)
+    layers, nb, n_req = 32, 2048, args.fp8_requests
+    rng = np.random.default_rng(6)
+    lens = rng.integers(1024, 16385, size=n_req)
+    blocks_per_req = [int(x) // 16 for x in lens]
+    g = torch.Generator(device="cuda:0").manual_seed(0)
+    kv = [torch.randint(0, 256, (2, nb, 16, 8, 128), generator=g, device="cuda:0", dtype=torch.uint8)
+          for _ in range(layers)]
+    sc = [torch.rand((nb,), generator=g, device="cuda:0", dtype=torch.float32) for _ in range(layers)]
+    names = [f"model.layers.{i}.attn" for i in range(layers)] + [f"model.layers.{i}.attn.scale" for i in range(layers)]
+    tensors = kv + sc
+    pool = args.fp8_pool_gb << 30
+    per_block = layers * (2 * 16 * 8 * 128 + 4)
+
+    def hashes(r, lo, hi):
+        return [f"req{r}-blk{i}".encode() for i in range(lo, hi)]
+
+    def ids_for(r, count):
+        return np.random.default_rng(1000 + r).permutation(nb)[:count].tolist()
+
+    def fresh_engine():
+        e = PegaEngine(pool, enable_lfu_admission=False)
+        for nm, t in zip(names, tensors):
+            lay = Layout.from_tensor(t)
+            e.register_context_layer("fp8", "ns", 0, nm, lay.data_ptr, lay.size_bytes, lay.num_blocks,
+                                     lay.bytes_per_block, lay.kv_stride_bytes, lay.segments, 0, 1, len(names))
+        # Warm half of every request, saved beforehand (the pool overflows later).
+        for r in range(n_req):
+            half = blocks_per_req[r] // 2
+            e.batch_save_kv_blocks("fp8", 0, 0, [(nm, ids_for(r, half), hashes(r, 0, half)) for nm in names])
+        return e
+
+    compute = torch.cuda.Stream("cuda:0")
+    cycles = int(args.fp8_compute_ms * 1e-3 * 1.9e9)
+
+    def wait_ready(state, timeout=120.0):
+        deadline = time.perf_counter() + timeout
+        while not state.is_ready():
+            if time.perf_counter() > deadline:
+                raise TimeoutError("load did not complete")
+
+    def serve(r, overlap):
+        nblk = blocks_per_req[r]
+        hs_all = hashes(r, 0, nblk)
+        hit = eng.count_prefix_hit_blocks("fp8", hs_all)
+        dst = ids_for(50_000 + r, nblk)
+        t0 = time.perf_counter()
+        state = PyLoadState(len(names))
+        if hit:
+            eng.batch_load_kv_blocks("fp8", 0, 0, state.shm_name(), names, dst[:hit], hs_all[:hit])
+        else:
+            state.set_completed()
+        for li in range(layers):
+            if hit and overlap:
+                if not (state.wait_layer(li, 60) and state.wait_layer(layers + li, 60)):
+                    raise RuntimeError("layer load failed")
+            elif hit and li == 0:
+                wait_ready(state)
+            with torch.cuda.stream(compute):
+                torch.cuda._sleep(cycles)
+        t_issue = time.perf_counter()
+        wait_ready(state)
+        load_done = time.perf_counter()
+        compute.synchronize()
+        t_end = time.perf_counter()
+        if state.get_state() != 1:
+            raise RuntimeError("load failed")
+        cold = hashes(r, hit, nblk)
+        if cold:
+            eng.batch_save_kv_blocks("fp8", 0, 0, [(nm, dst[hit:], cold) for nm in names])
+        return hit, (load_done - t0) * 1e3, (t_end - t0) * 1e3, (t_issue - t0) * 1e3
+
+    out = {}
+    for mode in ("overlap", "serial"):
+        eng = fresh_engine()  # the same starting cache for both modes
+        with torch.cuda.stream(compute):
+            torch.cuda._sleep(cycles)  # warm the compute stream
+        compute.synchronize()
+        rows = [serve(r, mode == "overlap") for r in range(n_req)]
+        if mode == "overlap":
+            m = eng.metrics()
+        eng.close()
+        hit_blocks = sum(x[0] for x in rows)
+        load_ms = [x[1] for x in rows if x[0]]
+        total = sum(x[2] for x in rows)
+        out[mode] = {"requests": n_req, "hit_blocks": hit_blocks, "p50_load_ms": round(statistics.median(load_ms), 3),
+                     "load_GBps": round(hit_blocks * per_block / (sum(load_ms) / 1e3) / 1e9, 2),
+                     "request_ms_p50": round(statistics.median(x[2] for x in rows), 3),
+                     "total_s": round(total / 1e3, 3)}
+    line = {
+        "metric": METRIC, "value": out["overlap"]["load_GBps"], "unit": "GB/s", "n_gpus": 1, "steps": n_req,
+        "warmup": 0, "ms_per_step": out["overlap"]["request_ms_p50"], "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded e4m3 bit patterns + fp32 scales)",
+        "config": {"workload": "llama8b_fp8_evict", "layers": "32 KV + 32 scale", "pool_gb": args.fp8_pool_gb,
+                   "requests": n_req, "prefix_tokens": "U[1024,16384] seed 6", "warm_fraction": 0.5,
+                   "compute_ms_per_layer": args.fp8_compute_ms},
+        "layerwise_overlap": out["overlap"], "load_then_compute": out["serial"],
+        "overlap_speedup": round(out["serial"]["total_s"] / out["overlap"]["total_s"], 3),
+        "engine": {k: m[k] for k in ("cache_block_evictions", "cache_block_hits", "cache_block_misses",
+                                     "pool_alloc_failures", "load_failures", "cached_blocks")},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def config_block(args, wl) -> dict:
     return {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
             "blocks_moved": wl["blocks"], "block_ids": args.order, "kv_dtype": "fp16" if wl.get("separate") else "bf16",
@@ -407,7 +526,10 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["qwen3_pd"], default="llama8b")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["qwen3_pd", "llama8b_fp8_evict"], default="llama8b")
+    ap.add_argument("--fp8-requests", type=int, default=64)
+    ap.add_argument("--fp8-pool-gb", type=int, default=30)
+    ap.add_argument("--fp8-compute-ms", type=float, default=0.5)
     ap.add_argument("--pd-requests", type=int, default=200)
     ap.add_argument("--pd-bounce-requests", type=int, default=20)
     ap.add_argument("--order", choices=["shuffled", "sorted"], default="shuffled")
@@ -431,6 +553,13 @@ def main() -> int:
                                              "see host_pool_bounce in the b200 line"}))
             return 0
         run_pd(args)
+        return 0
+    if args.workload == "llama8b_fp8_evict":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": "llama8b_fp8_evict",
+                              "unavailable": "engine-level scenario; the reference engine cannot be built here"}))
+            return 0
+        run_fp8_evict(args)
         return 0
     wl = dict(WORKLOADS[args.workload])
     if args.layers:

@@ -183,6 +183,71 @@ def main(argv: list[str]) -> int:
     (OUT / "load_requests.json").write_text(json.dumps(load_out, indent=1) + "\n")
     w._save_queue.put(None)
     w._save_thread.join()
+
+    # ---- request tracker traces (common.py RequestTracker) --------------------
+    from pegaflow.connector.common import RequestTracker, derive_namespace
+
+    import random
+
+    traces = []
+    for seed in range(40):
+        rnd = random.Random(seed)
+        nblk = rnd.randint(1, 12)
+        hashes = [bytes([seed, i]) for i in range(nblk)]
+        t = RequestTracker(f"r{seed}", hashes, 16, 3)
+        ops, outs = [], []
+        next_block = 100
+        for _ in range(rnd.randint(3, 14)):
+            op = rnd.choice(["lookup", "alloc", "load", "sched", "save", "layer", "finish", "hold"])
+            if op == "lookup":
+                args = [rnd.randint(0, nblk + 2), rnd.randint(0, nblk)]
+                t.on_lookup(*args)
+                out = None
+            elif op == "alloc":
+                k = rnd.randint(0, 4)
+                args = [list(range(next_block, next_block + k)), rnd.choice([0, 0, 16, 48])]
+                next_block += k
+                t.on_alloc(*args)
+                out = None
+            elif op == "load":
+                args = []
+                li = t.consume_load_intent()
+                out = None if li is None else [list(li.block_ids), [h.hex() for h in li.block_hashes], li.num_tokens]
+            elif op == "sched":
+                args = [rnd.randint(0, 40)]
+                t.on_scheduled(*args)
+                out = None
+            elif op == "save":
+                args = []
+                si = t.consume_save_intent()
+                out = None if si is None else [list(si.block_ids), [h.hex() for h in si.block_hashes]]
+            elif op == "layer":
+                args = []
+                t.on_layer_saved()
+                out = None
+            elif op == "finish":
+                args = []
+                t.on_finished()
+                out = None
+            else:
+                args = []
+                out = t.should_hold_blocks()
+            ops.append([op, args])
+            outs.append([out, t.phase.value, t.is_done()])
+        traces.append({"hashes": [h.hex() for h in hashes], "block_size": 16, "layers": 3, "ops": ops,
+                       "outs": outs})
+    (OUT / "tracker_traces.json").write_text(json.dumps(traces) + "\n")
+
+    # ---- namespace derivation (common.py:283-302) -----------------------------
+    cfg = types.SimpleNamespace(
+        model_config=types.SimpleNamespace(model="meta-llama/Llama-3.1-8B", dtype="torch.bfloat16",
+                                           get_total_num_kv_heads=lambda: 8, get_head_size=lambda: 128,
+                                           get_total_num_hidden_layers=lambda: 32),
+        cache_config=types.SimpleNamespace(cache_dtype="auto"))
+    ns = {"factors": {"model": "meta-llama/Llama-3.1-8B", "dtype": "torch.bfloat16", "tp_size": 2,
+                      "num_kv_heads": 8, "head_size": 128, "num_hidden_layers": 32, "cache_dtype": "auto"},
+          "namespace": derive_namespace(cfg, 2)}
+    (OUT / "namespace.json").write_text(json.dumps(ns, indent=1) + "\n")
     print("wrote", [p.name for p in sorted(OUT.glob("*.json"))])
     return 0
 

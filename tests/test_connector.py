@@ -1,0 +1,186 @@
+"""The vLLM connector against fixtures recorded from the reference's own
+connector code (tests/golden/, made by make_golden.py): request-tracker
+traces, namespace derivation, registration arguments, save-batch and load RPC
+composition. CPU only; the engine client is a recording fake."""
+
+import json
+import types
+from pathlib import Path
+
+import pytest
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+class Recorder:
+    def __init__(self):
+        self.calls = []
+
+    def register_context(self, *a):
+        self.calls.append(("register_context", a))
+        return True, ""
+
+    def save(self, *a):
+        self.calls.append(("save", a))
+        return True, ""
+
+    def load(self, *a):
+        self.calls.append(("load", a))
+        return True, ""
+
+    def unregister_context(self, *a):
+        self.calls.append(("unregister_context", a))
+        return True, ""
+
+    def query(self, instance_id, hashes):
+        self.calls.append(("query", (instance_id, hashes)))
+        return {"ok": True, "message": "", "hit_blocks": self.hits, "prefetch_state": "ready", "loading_blocks": 0,
+                "missing_blocks": 0}
+
+
+class FakeState:
+    def __init__(self, n=0):
+        self.n = n
+
+    def shm_name(self):
+        return "pega_load_golden"
+
+    def is_ready(self):
+        return False
+
+
+def ctx(client, num_layers=3, layerwise=False):
+    from pegaflow_b200.connector import ConnectorContext
+
+    return ConnectorContext("inst", "ns", 16, num_layers, 1, 0, 0, client, layerwise)
+
+
+def test_request_tracker_matches_reference_traces():
+    from pegaflow_b200.connector import RequestTracker
+
+    traces = json.loads((GOLDEN / "tracker_traces.json").read_text())
+    assert len(traces) == 40
+    for tr in traces:
+        t = RequestTracker("r", [bytes.fromhex(h) for h in tr["hashes"]], tr["block_size"], tr["layers"])
+        for (op, args), (expect, phase, done) in zip(tr["ops"], tr["outs"]):
+            out = None
+            if op == "lookup":
+                t.on_lookup(*args)
+            elif op == "alloc":
+                t.on_alloc(*args)
+            elif op == "load":
+                li = t.consume_load_intent()
+                out = None if li is None else [list(li.block_ids), [h.hex() for h in li.block_hashes], li.num_tokens]
+            elif op == "sched":
+                t.on_scheduled(*args)
+            elif op == "save":
+                si = t.consume_save_intent()
+                out = None if si is None else [list(si.block_ids), [h.hex() for h in si.block_hashes]]
+            elif op == "layer":
+                t.on_layer_saved()
+            elif op == "finish":
+                t.on_finished()
+            else:
+                out = t.should_hold_blocks()
+            assert [out, t.phase.value, t.is_done()] == [expect, phase, done], (tr["ops"], op)
+
+
+def test_namespace_matches_reference():
+    from pegaflow_b200.connector import namespace_from_factors
+
+    g = json.loads((GOLDEN / "namespace.json").read_text())
+    assert namespace_from_factors(g["factors"]) == g["namespace"]
+
+
+def test_registration_arguments_match_reference():
+    import torch
+
+    from pegaflow_b200.connector import WorkerSide
+
+    dtypes = {1: torch.uint8, 2: torch.bfloat16, 4: torch.float32}
+    for case in json.loads((GOLDEN / "registration.json").read_text()):
+        rec = Recorder()
+        w = WorkerSide(ctx(rec, num_layers=1), wrapper_factory=lambda t: b"wrapper")
+        try:
+            w.register_kv_caches({case["case"]: torch.empty(case["shape"], dtype=dtypes[case["element_size"]],
+                                                            device="meta")})
+        finally:
+            w._save_q.put(None)
+            w._save_thread.join()
+        (_, args), = rec.calls
+        assert list(args[8:12]) == [case["num_blocks"], case["bytes_per_block"], case["kv_stride_bytes"],
+                                    case["segments"]], case["case"]
+        assert args[:7] == ("inst", "ns", 0, 1, 0, 1, case["case"])
+
+
+def _meta(intents):
+    from pegaflow_b200.connector import PegaConnectorMetadata, SaveIntent
+
+    return PegaConnectorMetadata(save_intents={
+        k: SaveIntent(tuple(v["block_ids"]), tuple(bytes.fromhex(h) for h in v["block_hashes"]))
+        for k, v in intents.items()})
+
+
+def test_save_batch_rpc_matches_reference():
+    from pegaflow_b200.connector.worker import WorkerSide, _SaveTask
+
+    g = json.loads((GOLDEN / "save_batches.json").read_text())
+    rec = Recorder()
+    w = WorkerSide(ctx(rec))
+    meta = _meta(g["save_intents"])
+    tasks = [_SaveTask(t["layer"], types.SimpleNamespace(block_table=object() if t["has_block_table"] else None),
+                       meta, ["reqA", "reqB", "reqC"] if i < 3 else ["reqA"])
+             for i, t in enumerate(g["tasks"])]
+    w.process_save_batch(tasks)
+    w._save_q.put(None)
+    w._save_thread.join()
+    saves = [a for n, a in rec.calls if n == "save"]
+    assert len(saves) == len(g["rpc"]) == 1
+    (inst, rank, dev, layers), want = saves[0], g["rpc"][0]
+    assert (inst, rank, dev) == (want["instance_id"], want["tp_rank"], want["device_id"])
+    assert [[n, list(ids), [h.hex() for h in hs]] for n, ids, hs in layers] == want["saves"]
+
+
+def test_load_rpc_matches_reference():
+    from pegaflow_b200.connector import LoadIntent, PegaConnectorMetadata, SaveIntent, WorkerSide
+
+    g = json.loads((GOLDEN / "load_requests.json").read_text())
+    rec = Recorder()
+    w = WorkerSide(ctx(rec), load_state_factory=FakeState)
+    meta = PegaConnectorMetadata(
+        load_intents={k: LoadIntent(tuple(v["block_ids"]), tuple(bytes.fromhex(h) for h in v["block_hashes"]),
+                                    16 * len(v["block_ids"])) for k, v in g["load_intents"].items()},
+        save_intents={"r3": SaveIntent((1,), (b"q",))})
+    layers = {k: (types.SimpleNamespace(kv_cache=[None]) if v else types.SimpleNamespace())
+              for k, v in g["layers"].items()}
+    w.start_load_kv(meta, types.SimpleNamespace(no_compile_layers=layers))
+    w._save_q.put(None)
+    w._save_thread.join()
+    (_, args), = [c for c in rec.calls if c[0] == "load"]
+    (want,) = g["rpc"]
+    assert args[0:3] == (want["instance_id"], want["tp_rank"], want["device_id"])
+    assert list(args[4]) == want["layer_names"] and list(args[5]) == want["block_ids"]
+    assert [h.hex() for h in args[6]] == want["block_hashes"]
+
+
+def test_scheduler_flow_async_and_layerwise():
+    from pegaflow_b200.connector import SchedulerSide
+
+    for layerwise in (False, True):
+        rec = Recorder()
+        rec.hits = 3
+        s = SchedulerSide(ctx(rec, layerwise=layerwise))
+        req = types.SimpleNamespace(request_id="r", block_hashes=[b"a", b"b", b"c", b"d"], num_tokens=64)
+        tokens, is_async = s.get_num_new_matched_tokens(req, 16)
+        assert tokens == 32 and is_async is (not layerwise)  # 3 hit blocks, 1 already computed
+        blocks = types.SimpleNamespace(get_block_ids=lambda: ([7, 8, 9, 10],))
+        s.update_state_after_alloc(req, blocks, 32)
+        out = types.SimpleNamespace(scheduled_new_reqs=[types.SimpleNamespace(req_id="r")],
+                                    num_scheduled_tokens={"r": 64},
+                                    scheduled_cached_reqs=types.SimpleNamespace(req_ids=[], new_block_ids=[]))
+        meta = s.build_connector_meta(out)
+        assert meta.load_intents["r"].block_ids == (8, 9) and meta.load_intents["r"].num_tokens == 32
+        assert meta.save_intents["r"].block_ids == (7, 8, 9, 10)
+        assert s.request_finished(req, [])[0] is True  # blocks held until the save lands
+        s.update_connector_output(types.SimpleNamespace(finished_sending={"r"}))
+        assert "r" not in s._trackers
