@@ -513,6 +513,8 @@ def config_block(args, wl) -> dict:
     return {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
             "blocks_moved": wl["blocks"], "block_ids": args.order, "kv_dtype": "fp16" if wl.get("separate") else "bf16",
             "save_mode": args.save_mode, "load_mode": args.load_mode,
+            "staging": {"slot_MiB": args.chunk_mib or 512, "slots": args.slots or 2,
+                        "first_chunk_MiB": args.first_chunk_mib or 64, "growth": "x2 per chunk"},
             "l2": "inputs larger than L2 (payload >= 36 MiB per layer set; KV cache >> 126 MB)",
             "parallelism": f"dp{args.gpus} (independent ranks, weak scaling)"}
 
@@ -536,6 +538,7 @@ def main() -> int:
     ap.add_argument("--save-mode", default="auto", choices=["auto", "staged", "direct"])
     ap.add_argument("--load-mode", default="auto", choices=["auto", "staged", "direct"])
     ap.add_argument("--chunk-mib", type=int, default=0)
+    ap.add_argument("--first-chunk-mib", type=int, default=0)
     ap.add_argument("--slots", type=int, default=0)
     ap.add_argument("--copy-streams", type=int, default=0)
     ap.add_argument("--ctas-per-sm", type=int, default=0)
@@ -595,7 +598,7 @@ def main() -> int:
     ex = Executor(local, save_mode=args.save_mode, load_mode=args.load_mode,
                   staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
                   copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm,
-                  cache_streaming=args.cache_streaming)
+                  cache_streaming=args.cache_streaming, first_chunk_bytes=args.first_chunk_mib << 20)
     pool = PinnedBuffer(payload + wl["layers"] * 8192 + (1 << 20), write_combined=True)
     saves, loads, _ = executor_specs(tensors, src, dst, pool.ptr)
     stream = torch.cuda.Stream(local)
@@ -650,7 +653,8 @@ def main() -> int:
                      executor=dict(save_mode=args.save_mode, load_mode=args.load_mode,
                                    staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
                                    copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm,
-                                   cache_streaming=1 if args.cache_streaming else 0))
+                                   cache_streaming=1 if args.cache_streaming else 0,
+                                   first_chunk_bytes=args.first_chunk_mib << 20))
     names = [f"model.layers.{i}.self_attn" for i in range(len(tensors))]
     from pegaflow_b200 import Layout
 

@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define PF_ABI_VERSION 1
+#define PF_ABI_VERSION 2
 
 /* ------------------------------------------------------------------------ */
 /* Status codes: one per EngineError variant (pegaflow-core/src/lib.rs:58-67) */
@@ -89,13 +89,19 @@ typedef enum pf_transfer_mode {
 } pf_transfer_mode;
 
 typedef struct pf_executor_config {
-  uint64_t staging_chunk_bytes; /* 0 = default (64 MiB) */
-  uint32_t staging_slots;       /* 0 = default (3) */
+  uint64_t staging_chunk_bytes; /* slot size, 0 = default (512 MiB) */
+  uint32_t staging_slots;       /* 0 = default (2) */
   uint32_t save_mode;           /* pf_transfer_mode */
   uint32_t load_mode;           /* pf_transfer_mode */
   uint32_t ctas_per_sm;         /* 0 = default */
   uint32_t copy_streams;        /* 0 = default (2) */
   uint32_t cache_streaming;     /* 1 = evict-first loads/stores in the kernels */
+  uint32_t reserved0;
+  /* Size limit of the first staged chunk of a call; each later chunk may be
+   * twice the previous one, up to staging_chunk_bytes. Small first chunks
+   * start the DMA (and raise the first per-layer flags) early; large later
+   * chunks keep the kernel launch count low. 0 = default (64 MiB). */
+  uint64_t first_chunk_bytes;
 } pf_executor_config;
 
 /* Fill *cfg with the library defaults. */

@@ -68,6 +68,8 @@ class ExecutorConfig(Structure):
         ("ctas_per_sm", c_uint32),
         ("copy_streams", c_uint32),
         ("cache_streaming", c_uint32),
+        ("reserved0", c_uint32),
+        ("first_chunk_bytes", c_uint64),
     ]
 
 

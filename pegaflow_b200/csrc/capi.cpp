@@ -85,12 +85,13 @@ int pf_segment_offset(const pf_layer_desc* layer, uint64_t block_idx, uint64_t s
 void pf_executor_config_default(pf_executor_config* cfg) {
   if (!cfg) return;
   std::memset(cfg, 0, sizeof(*cfg));
-  cfg->staging_chunk_bytes = 64ull << 20;
-  cfg->staging_slots = 3;
+  cfg->staging_chunk_bytes = pf::kDefaultSlotBytes;
+  cfg->staging_slots = pf::kDefaultSlots;
   cfg->save_mode = PF_MODE_AUTO;
   cfg->load_mode = PF_MODE_AUTO;
   cfg->ctas_per_sm = 4;
   cfg->copy_streams = 2;
+  cfg->first_chunk_bytes = pf::kDefaultFirstChunkBytes;
 }
 
 int pf_executor_create(int32_t device_id, const pf_executor_config* cfg, pf_executor** out) {

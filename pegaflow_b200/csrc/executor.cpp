@@ -152,15 +152,19 @@ Executor::Executor(int device, const pf_executor_config& cfg) : device_(device),
   }
   cuda_check(cudaSetDevice(device), "cudaSetDevice");
   cuda_check(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
-  if (cfg_.staging_chunk_bytes == 0) cfg_.staging_chunk_bytes = 64ull << 20;
-  if (cfg_.staging_slots == 0) cfg_.staging_slots = 3;
+  if (cfg_.staging_chunk_bytes == 0) cfg_.staging_chunk_bytes = kDefaultSlotBytes;
+  if (cfg_.staging_slots == 0) cfg_.staging_slots = kDefaultSlots;
   if (cfg_.ctas_per_sm == 0) cfg_.ctas_per_sm = 4;
+  // One full wave: never ask for more CTAs per SM than stay resident.
+  cfg_.ctas_per_sm = std::min<uint32_t>(cfg_.ctas_per_sm, std::max(1, copy_kernel_resident_ctas()));
   if (cfg_.copy_streams == 0) cfg_.copy_streams = 2;
   if (cfg_.save_mode == PF_MODE_AUTO) cfg_.save_mode = PF_MODE_STAGED;
   if (cfg_.load_mode == PF_MODE_AUTO) cfg_.load_mode = PF_MODE_STAGED;
   // A slot must hold one tile plus the alignment slack of a chunk start.
   slot_bytes_ = align_up(std::max<uint64_t>(cfg_.staging_chunk_bytes, 2 * kTileBytes), kDenseAlign);
   slots_ = std::max<uint32_t>(cfg_.staging_slots, 1);
+  if (cfg_.first_chunk_bytes == 0) cfg_.first_chunk_bytes = kDefaultFirstChunkBytes;
+  first_chunk_ = std::min(slot_bytes_, std::max<uint64_t>(cfg_.first_chunk_bytes, 2 * kTileBytes));
 
   cuda_check(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
   cuda_check(cudaStreamCreateWithFlags(&kstream_, cudaStreamNonBlocking), "cudaStreamCreate");
@@ -630,11 +634,18 @@ void Executor::issue_serial(const Built& b, cudaStream_t s, int64_t* layer_done)
 void Executor::make_chunks(const Built& b, std::vector<Chunk>* chunks) {
   chunks->clear();
   if (b.total_tiles == 0) return;
-  // Walk units in order; a chunk is a tile range whose dense span fits a slot.
-  // A chunk's dense start is rounded down to kDenseAlign so the slot shift
-  // (slot - dense_begin) keeps every 16-byte-aligned dense address aligned,
-  // even when the chunk starts inside a layer of unaligned units.
+  // Walk units in order; a chunk is a tile range whose dense span fits the
+  // current limit. The limit starts at first_chunk_ and doubles with each
+  // chunk up to the slot size: the first copy-engine transfer (and, for a
+  // load, the first layer's completion) starts after a small kernel, while
+  // the bulk moves in few launches. Every launch pays a fixed latency of tens
+  // of microseconds while the copy engine is busy, so the launch count, not
+  // the bytes, sets the kernel's cost. A chunk's dense start is rounded down
+  // to kDenseAlign so the slot shift (slot - dense_begin) keeps every
+  // 16-byte-aligned dense address aligned, even when the chunk starts inside
+  // a layer of unaligned units.
   uint64_t cur_tb = 0, cur_db = 0, last_end = 0;
+  uint64_t limit = first_chunk_;
   bool first = true;
   uint64_t dense = 0;
   for (const PlanLayer& p : b.layers) {
@@ -649,17 +660,18 @@ void Executor::make_chunks(const Built& b, std::vector<Chunk>* chunks) {
         cur_db = ud / kDenseAlign * kDenseAlign;
         first = false;
       }
-      if (ue - cur_db <= slot_bytes_) {  // whole unit joins the current chunk
+      if (ue - cur_db <= limit) {  // whole unit joins the current chunk
         last_end = ue;
         continue;
       }
       for (uint32_t t = 0; t < p.tiles_per_unit; ++t) {
         const uint64_t d0 = ud + static_cast<uint64_t>(t) * kTileBytes;
         const uint64_t d1 = std::min<uint64_t>(d0 + kTileBytes, ue);
-        if (d1 - cur_db > slot_bytes_) {
+        if (d1 - cur_db > limit) {
           chunks->push_back({cur_tb, ut + t, cur_db, last_end});
           cur_tb = ut + t;
           cur_db = d0 / kDenseAlign * kDenseAlign;
+          limit = std::min(slot_bytes_, limit * 2);
         }
         last_end = d1;
       }

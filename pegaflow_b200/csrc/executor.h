@@ -26,6 +26,14 @@ UnitGeometry load_geometry(const pf_layer_desc& l);
 bool is_split_layout(const pf_layer_desc& l);       // lib.rs:636
 bool is_contiguous_layout(const pf_layer_desc& l);  // transfer.rs:50-52
 
+// Staging defaults. While the copy engines stream a D2H/H2D, every kernel
+// launch on the device pays a fixed latency of tens of microseconds, so the
+// chunk schedule (first chunk, doubling to the slot size) trades 1 GiB of HBM
+// for five launches per direction on a 1.25 GiB transfer instead of twenty.
+constexpr uint64_t kDefaultSlotBytes = 512ull << 20;
+constexpr uint32_t kDefaultSlots = 2;
+constexpr uint64_t kDefaultFirstChunkBytes = 64ull << 20;
+
 // Layout checks of register_context_layer (lib.rs:389-449).
 void validate_layout(const pf_layer_desc& l, const char* layer_name);
 // transfer::segment_offset (transfer.rs:18-47).
@@ -107,6 +115,7 @@ class Executor {
   std::vector<cudaStream_t> cstreams_;  // copy-engine DMA
   uint8_t* staging_ = nullptr;
   uint64_t slot_bytes_ = 0;
+  uint64_t first_chunk_ = 0;  // limit of a call's first chunk; doubles per chunk up to slot_bytes_
   uint32_t slots_ = 0;
   std::vector<cudaEvent_t> ev_filled_, ev_drained_;
   cudaEvent_t ev_start_ = nullptr, ev_plan_ = nullptr, ev_done_ = nullptr;

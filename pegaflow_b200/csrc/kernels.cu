@@ -30,6 +30,7 @@ namespace {
 
 constexpr int kWarpsPerCta = 8;
 constexpr int kThreads = kWarpsPerCta * 32;
+constexpr int kMinCtasPerSm = 4;
 constexpr int kVecPerLane = kTileBytes / (32 * 16);  // 8
 static_assert(kVecPerLane == 8, "tile = 32 lanes x 8 x 16 B");
 static_assert(sizeof(PlanLayer) % 16 == 0, "layer table is copied in 16-byte words");
@@ -109,8 +110,10 @@ extern __shared__ __align__(16) unsigned char g_smem[];
 // SMEM: the CTA first copies the plan's layer table into shared memory with
 // coalesced 16-byte loads (one round trip), so the per-warp layer lookups
 // below hit shared memory instead of chaining dependent global loads.
+// Four CTAs per SM (64 registers): 32 warps x 4 KiB of loads in flight per SM,
+// and the default grid of 4 x SMs runs as exactly one wave.
 template <int DIR, bool TABLE, bool SMEM, bool CS>
-__global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyArgs a) {
+__global__ void __launch_bounds__(kThreads, kMinCtasPerSm) kv_copy_kernel(const CopyArgs a) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
 
@@ -140,16 +143,20 @@ __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyArgs a) {
     if (layers[mid].tile_start <= tile) lo = mid; else hi = mid;
   }
   uint32_t l = lo;
-  PlanLayer L = layers[l];
+  // The layer entry is read in place (shared memory when SMEM) on every tile
+  // rather than held in 24 registers: a few shared loads per 4 KiB moved keep
+  // the kernel within 64 registers without spilling.
+  const PlanLayer* Lp = &layers[l];
   uint32_t done_in_layer = 0;
 
   for (; tile < cta_end; tile += kWarpsPerCta) {
-    while (tile >= L.tile_start + L.tile_count) {
-      flush_layer(a, l, L.tile_count, L.done_index, done_in_layer, lane);
+    while (tile >= Lp->tile_start + Lp->tile_count) {
+      flush_layer(a, l, Lp->tile_count, Lp->done_index, done_in_layer, lane);
       done_in_layer = 0;
       ++l;
-      L = layers[l];
+      Lp = &layers[l];
     }
+    const PlanLayer& L = *Lp;
     const uint32_t local = (uint32_t)(tile - L.tile_start);
     const uint32_t unit_local = local / L.tiles_per_unit;
     const uint32_t t = local - unit_local * L.tiles_per_unit;
@@ -176,7 +183,7 @@ __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyArgs a) {
     }
     ++done_in_layer;
   }
-  flush_layer(a, l, L.tile_count, L.done_index, done_in_layer, lane);
+  flush_layer(a, l, Lp->tile_count, Lp->done_index, done_in_layer, lane);
 }
 
 // Runtime flags -> template instance.
@@ -199,6 +206,26 @@ void launch_smem(bool smem, bool cs, const CopyArgs& a, int grid, size_t shm, cu
 }
 
 }  // namespace
+
+int copy_kernel_resident_ctas() {
+  // The fewest CTAs per SM any instance keeps resident, with a full 48 KiB
+  // layer table in shared memory (the largest dynamic size launch_copy asks for).
+  int lowest = kMinCtasPerSm * 4;
+  auto take = [&](const void* fn, size_t shm) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, shm) != cudaSuccess) {
+      cudaGetLastError();
+      return;
+    }
+    if (n > 0 && n < lowest) lowest = n;
+  };
+  take(reinterpret_cast<const void*>(&kv_copy_kernel<kPack, false, true, false>), kMaxSmemTableBytes);
+  take(reinterpret_cast<const void*>(&kv_copy_kernel<kUnpack, false, true, false>), kMaxSmemTableBytes);
+  take(reinterpret_cast<const void*>(&kv_copy_kernel<kUnpack, true, true, false>), kMaxSmemTableBytes);
+  take(reinterpret_cast<const void*>(&kv_copy_kernel<kPack, true, true, true>), kMaxSmemTableBytes);
+  take(reinterpret_cast<const void*>(&kv_copy_kernel<kPack, false, false, false>), 0);
+  return lowest;
+}
 
 cudaError_t launch_copy(Dir dir, bool table, const CopyArgs& args, int grid,
                         cudaStream_t stream, bool streaming) {

@@ -55,6 +55,7 @@ struct DeviceScratch {
   uint8_t* plan = nullptr;
   uint8_t* staging = nullptr;
   int sms = 0;
+  int ctas = 1;  // resident CTAs per SM of the copy kernel
 };
 std::mutex g_mu;
 DeviceScratch g_dev[kMaxDevices];
@@ -72,6 +73,7 @@ DeviceScratch& scratch_for(int device) {
     cuda_check(cudaGetSymbolAddress(&p, g_noalloc_staging), "cudaGetSymbolAddress(staging)");
     d.staging = static_cast<uint8_t*>(p);
     cuda_check(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
+    d.ctas = std::max(1, std::min(4, copy_kernel_resident_ctas()));
     d.ready = true;
   }
   return d;
@@ -220,7 +222,7 @@ void save_noalloc(int device, const pf_save_layer* layers, uint64_t n_layers, cu
     a.tile_begin = tb;
     a.tile_end = te;
     a.side_shift = static_cast<int64_t>(reinterpret_cast<uint64_t>(sc.staging)) - static_cast<int64_t>(db);
-    const uint64_t grid = std::min<uint64_t>((te - tb + 7) / 8, static_cast<uint64_t>(sc.sms) * 4);
+    const uint64_t grid = std::min<uint64_t>((te - tb + 7) / 8, static_cast<uint64_t>(sc.sms) * sc.ctas);
     cuda_check(launch_copy(kPack, false, a, static_cast<int>(std::max<uint64_t>(grid, 1)), stream), "kernel launch");
     for (const Extent& e : extents) {
       const uint64_t lo = std::max(e.dense, db), hi = std::min(e.dense + e.bytes, de);

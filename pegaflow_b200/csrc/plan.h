@@ -74,4 +74,8 @@ enum Dir : int { kPack = 0, kUnpack = 1 };
 cudaError_t launch_copy(Dir dir, bool table, const CopyArgs& args, int grid,
                         cudaStream_t stream, bool streaming = false);
 
+// CTAs of kv_copy_kernel resident per SM on the current device (the lowest
+// over its instances); grids beyond SMs x this run as a partial second wave.
+int copy_kernel_resident_ctas();
+
 }  // namespace pf

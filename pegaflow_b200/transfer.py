@@ -162,6 +162,7 @@ class Executor:
         ctas_per_sm: int = 0,
         copy_streams: int = 0,
         cache_streaming: bool = False,
+        first_chunk_bytes: int = 0,
         _handle: Optional[int] = None,
     ):
         self.device_id = device_id
@@ -182,6 +183,8 @@ class Executor:
         if copy_streams:
             cfg.copy_streams = copy_streams
         cfg.cache_streaming = 1 if cache_streaming else 0
+        if first_chunk_bytes:
+            cfg.first_chunk_bytes = first_chunk_bytes
         h = c_void_p()
         N.check(N.lib.pf_executor_create(device_id, byref(cfg), byref(h)))
         self._h = h

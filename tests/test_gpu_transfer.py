@@ -137,14 +137,18 @@ def test_llama_kv_first_layers(cuda, oracle, mode, order):
 
 
 @pytest.mark.parametrize("mode", MODES)
-@pytest.mark.parametrize("chunk", [64 << 10, 200 << 10, 16 << 20])
-def test_many_chunks_and_mixed_layouts(cuda, oracle, mode, chunk):
+@pytest.mark.parametrize("chunk,first", [(64 << 10, 0), (200 << 10, 0), (16 << 20, 0), (1 << 20, 8 << 10),
+                                         (300 << 10, 9 << 10)])
+def test_many_chunks_and_mixed_layouts(cuda, oracle, mode, chunk, first):
     """Small staging chunks split units across chunks and slots wrap many
-    times; layers mix split, blocks-first, 4-byte scales and unaligned units."""
+    times; layers mix split, blocks-first, 4-byte scales and unaligned units.
+    A small first chunk makes every chunk of the growth schedule differ in
+    size (8 KiB, 16 KiB, ... up to the slot)."""
     torch = cuda
     from pegaflow_b200 import Executor, PinnedBuffer
 
-    ex = Executor(0, save_mode=mode, load_mode=mode, staging_chunk_bytes=chunk, staging_slots=2)
+    ex = Executor(0, save_mode=mode, load_mode=mode, staging_chunk_bytes=chunk, staging_slots=2,
+                  first_chunk_bytes=first)
     layers = [
         kv(torch, (2, 64, 16, 2, 128), torch.bfloat16, 1),   # split, 8 KiB units
         kv(torch, (64, 16, 4, 64), torch.float16, 2),         # blocks-first, 8 KiB
