@@ -125,6 +125,22 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
+# DRAM bytes per payload byte of one pack or unpack launch, from one ncu
+# capture of dram__bytes_read.sum / dram__bytes_write.sum on 128 MiB staging
+# chunks (larger than L2; profiles/kv_copy_kernel_llama8b.md, section 2b).
+# Reads equal the payload (no re-reads); writes still in the 126 MB L2 when
+# the kernel ends reach DRAM after it, so the write figure is below 1.
+TRAFFIC_READ_PER_BYTE = 134_251_584 / 134_217_728
+TRAFFIC_WRITE_PER_BYTE = 76_006_592 / 134_217_728
+
+
+def traffic_per_launch(kernel_bytes_per_launch: float) -> int:
+    """ncu-measured DRAM traffic scaled to the average launch (payload = half
+    the algorithmic bytes: each payload byte is read once and written once)."""
+    payload = kernel_bytes_per_launch / 2
+    return round(payload * (TRAFFIC_READ_PER_BYTE + TRAFFIC_WRITE_PER_BYTE))
+
+
 def link_peaks(torch, device: int) -> dict:
     """Pinned host<->device copy-engine bandwidth with 1 GiB buffers (best of 3)."""
     n = 1 << 30
@@ -729,7 +745,11 @@ def main() -> int:
             "roofline": {"bound": "hbm", "achieved": round(kernel_gbps, 1) if kernel_gbps else None,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(kernel_gbps / peaks["hbm_gbs"], 3) if kernel_gbps else None,
-                         "traffic": None, "peak_source": peaks["source"],
+                         "traffic": traffic_per_launch(st["kernel_bytes"] / max(1, st["timed_launches"])),
+                         "traffic_how": "ncu dram__bytes_read.sum + dram__bytes_write.sum per payload byte "
+                                        "(128 MiB chunks) x this run's average launch; writes still in L2 "
+                                        "at kernel end are not counted",
+                         "peak_source": peaks["source"],
                          "kernel": "kv_copy_kernel (pack+unpack)",
                          "bytes_per_launch": round(st["kernel_bytes"] / max(1, st["timed_launches"])),
                          "avg_launch_us": round(st["kernel_ms"] * 1e3 / max(1, st["timed_launches"]), 2)},

@@ -345,8 +345,14 @@ int pf_engine_batch_save_kv_blocks(pf_engine* e, const char* instance_id, uint64
         throw pf::invalid_argument("null block_ids or block_hashes");
       }
       entries[i].block_ids.assign(s.block_ids, s.block_ids + s.n_ids);
-      entries[i].hashes.reserve(s.n_hashes);
-      for (uint64_t k = 0; k < s.n_hashes; ++k) entries[i].hashes.push_back(bytes_str(s.block_hashes[k]));
+      if (i > 0 && s.block_hashes == saves[i - 1].block_hashes && s.n_hashes == saves[i - 1].n_hashes) {
+        entries[i].hashes = entries[i - 1].hashes;  // the caller passed one array for both entries
+        continue;
+      }
+      auto hashes = std::make_shared<std::vector<std::string>>();
+      hashes->reserve(s.n_hashes);
+      for (uint64_t k = 0; k < s.n_hashes; ++k) hashes->push_back(bytes_str(s.block_hashes[k]));
+      entries[i].hashes = std::move(hashes);
     }
     e->impl->batch_save(str(instance_id), tp_rank, device_id, entries);
   });

@@ -356,7 +356,7 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
     uint64_t slot, total_slots;
     bool split;
     std::vector<int64_t> ids;
-    std::vector<std::string> hashes;
+    std::shared_ptr<const std::vector<std::string>> hashes;  // the entry's list when nothing was filtered
     std::shared_ptr<PoolAllocation> k_alloc, v_alloc;
     std::shared_ptr<DeviceWorker> worker;
   };
@@ -364,12 +364,23 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
   std::unordered_map<uint64_t, std::unordered_set<std::string>> planned_slots;  // slot -> hashes planned
   std::exception_ptr pending;
   const auto t0 = Clock::now();
+  // Entries usually carry the same hash list (one request, every layer): the
+  // cache/inflight state of a list is probed once and reused while it repeats.
+  SaveProbe probe;
+  const std::vector<std::string>* probed = nullptr;
+  // A layer listed again later in the batch must see this entry's hashes as
+  // saved (the reference would have inserted them before reaching it).
+  std::unordered_map<std::string, size_t> last_of_layer;
+  for (size_t k = 0; k < saves.size(); ++k) last_of_layer[saves[k].layer_name] = k;
 
-  for (const SaveEntry& e : saves) {
+  for (size_t k_entry = 0; k_entry < saves.size(); ++k_entry) {
+    const SaveEntry& e = saves[k_entry];
     try {
-      if (e.block_ids.size() != e.hashes.size()) {
+      static const std::vector<std::string> kNoHashes;
+      const std::vector<std::string>& hashes = e.hashes ? *e.hashes : kNoHashes;
+      if (e.block_ids.size() != hashes.size()) {
         throw invalid_argument("block_ids length " + std::to_string(e.block_ids.size()) +
-                               " does not match block_hashes " + std::to_string(e.hashes.size()));
+                               " does not match block_hashes " + std::to_string(hashes.size()));
       }
       auto gpu = get_gpu(*inst, device_id);
       if (!gpu) throw worker_missing(instance_id, device_id);
@@ -404,17 +415,30 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
       // Dedup (lib.rs:613-616): not sealed, not inflight for this slot, and
       // not planned for this slot by an earlier entry of this batch (which
       // the reference would already have inserted).
-      const std::vector<char> needs = storage_->needs_save(ns, e.hashes, cand, slot);
+      if (probed == nullptr || (probed != &hashes && *probed != hashes)) {
+        storage_->probe_save(ns, hashes, &probe);
+        probed = &hashes;
+      }
       const std::unordered_set<std::string>* earlier = nullptr;
       auto ps = planned_slots.find(slot);
       if (ps != planned_slots.end()) earlier = &ps->second;
+      std::vector<size_t> keep;
+      keep.reserve(cand.size());
       for (size_t j = 0; j < cand.size(); ++j) {
-        const std::string& h = e.hashes[cand[j]];
-        if (!needs[j] || (earlier && earlier->count(h))) continue;
-        p.ids.push_back(e.block_ids[cand[j]]);
-        p.hashes.push_back(h);
+        if (!probe.needs(cand[j], slot) || (earlier && earlier->count(hashes[cand[j]]))) continue;
+        keep.push_back(cand[j]);
       }
-      if (p.ids.empty()) continue;
+      if (keep.empty()) continue;
+      p.ids.reserve(keep.size());
+      for (size_t i : keep) p.ids.push_back(e.block_ids[i]);
+      if (keep.size() == hashes.size()) {
+        p.hashes = e.hashes;  // nothing filtered: share the caller's list
+      } else {
+        auto kept = std::make_shared<std::vector<std::string>>();
+        kept->reserve(keep.size());
+        for (size_t i : keep) kept->push_back(hashes[i]);
+        p.hashes = std::move(kept);
+      }
       const uint64_t n = p.ids.size();
       if (p.split) {
         const uint64_t bytes = reg.bytes_per_block * n;
@@ -430,12 +454,7 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
       p.worker = gpu->worker;
       // Remember planned hashes only when another entry of this batch uses
       // the same slot (a layer listed twice); usually none does.
-      for (size_t k = 0; k < saves.size(); ++k) {
-        if (&saves[k] != &e && saves[k].layer_name == e.layer_name && &saves[k] > &e) {
-          planned_slots[slot].insert(p.hashes.begin(), p.hashes.end());
-          break;
-        }
-      }
+      if (last_of_layer[e.layer_name] > k_entry) planned_slots[slot].insert(p.hashes->begin(), p.hashes->end());
       planned.push_back(std::move(p));
     } catch (...) {
       pending = std::current_exception();
@@ -460,38 +479,54 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
     Executor& ex = worker->executor();
     ex.save(layers.data(), layers.size(), ex.own_stream());
 
-    // LayerBlocks (lib.rs:687-698, 755-763) are built while the copy runs;
-    // their slots are inserted once the bytes are in the pool.
-    std::vector<std::vector<LayerBlockPtr>> built(planned.size());
+    // LayerBlocks (lib.rs:687-698, 755-763) are built while the copy runs,
+    // one batch per entry sharing its pool allocations; their slots are
+    // inserted once the bytes are in the pool.
+    std::vector<std::shared_ptr<LayerBlockBatch>> built(planned.size());
+    bool same_hashes = true;
     for (size_t k = 0; k < planned.size(); ++k) {
       Planned& p = planned[k];
       const uint64_t block_size = p.reg.bytes_per_block * p.reg.segments;
-      std::vector<LayerBlockPtr>& blocks = built[k];
-      blocks.resize(p.ids.size());
+      auto batch = std::make_shared<LayerBlockBatch>();
+      batch->k_alloc = p.k_alloc;
+      batch->v_alloc = p.v_alloc;
+      batch->blocks.resize(p.ids.size());
       for (size_t i = 0; i < p.ids.size(); ++i) {
-        auto lb = std::make_shared<LayerBlock>();
+        LayerBlock& lb = batch->blocks[i];
         if (p.split) {
-          lb->k_ptr = p.k_alloc->ptr + i * p.reg.bytes_per_block;
-          lb->v_ptr = p.v_alloc->ptr + i * p.reg.bytes_per_block;
-          lb->v_alloc = p.v_alloc;
+          lb.k_ptr = p.k_alloc->ptr + i * p.reg.bytes_per_block;
+          lb.v_ptr = p.v_alloc->ptr + i * p.reg.bytes_per_block;
         } else {
-          lb->k_ptr = p.k_alloc->ptr + i * block_size;
-          lb->v_ptr = nullptr;
+          lb.k_ptr = p.k_alloc->ptr + i * block_size;
+          lb.v_ptr = nullptr;
         }
-        lb->size = block_size;
-        lb->k_alloc = p.k_alloc;
-        blocks[i] = std::move(lb);
+        lb.size = block_size;
       }
+      built[k] = std::move(batch);
+      if (k > 0 && same_hashes) same_hashes = p.hashes == planned[0].hashes || *p.hashes == *planned[0].hashes;
     }
     cuda_check(cudaStreamSynchronize(ex.own_stream()), "cudaStreamSynchronize(save)");
     const auto t_xfer = Clock::now();
 
-    // insert_slot (lib.rs:700-705, 765-770), one entry at a time.
-    for (size_t k = 0; k < planned.size(); ++k) {
-      Planned& p = planned[k];
-      storage_->insert_slots(ns, p.hashes, p.slot, built[k], p.total_slots);
+    // insert_slot (lib.rs:700-705, 765-770): entry by entry, or in one
+    // hash-major pass with the same outcome when every entry has the same list.
+    auto count = [this](const Planned& p) {
       counters_.save_bytes.fetch_add(p.reg.bytes_per_block * p.reg.segments * p.ids.size());
       counters_.save_calls.fetch_add(1);
+    };
+    if (same_hashes && planned.size() > 1) {
+      std::vector<SlotFill> fills(planned.size());
+      for (size_t k = 0; k < planned.size(); ++k) fills[k] = SlotFill{planned[k].slot, built[k]};
+      storage_->insert_slots_multi(ns, *planned[0].hashes, fills, planned[0].total_slots);
+      for (const Planned& p : planned) count(p);
+    } else {
+      for (size_t k = 0; k < planned.size(); ++k) {
+        Planned& p = planned[k];
+        std::vector<LayerBlockPtr> blocks(p.ids.size());
+        for (size_t i = 0; i < blocks.size(); ++i) blocks[i] = layer_block_at(built[k], i);
+        storage_->insert_slots(ns, *p.hashes, p.slot, blocks, p.total_slots);
+        count(p);
+      }
     }
     std::lock_guard<std::mutex> g(counters_.ms_mu);
     counters_.save_ms += ms_since(t0);
@@ -540,7 +575,7 @@ void Engine::batch_load_inner(const std::string& instance_id, uint64_t tp_rank, 
   auto inst = get_instance(instance_id);
   auto gpu = get_gpu(*inst, device_id);
   if (!gpu) throw worker_missing(instance_id, device_id);
-  const std::vector<SealedBlockPtr> cache = storage_->cache_lookup_many(inst->ns, hashes);
+  std::vector<SealedBlockPtr> cache = storage_->cache_lookup_many(inst->ns, hashes);
 
   LoadTask task;
   task.shm = shm;
@@ -558,11 +593,13 @@ void Engine::batch_load_inner(const std::string& instance_id, uint64_t tp_rank, 
     L.name = name;
     L.reg = reg;
     const size_t n = std::min(block_ids.size(), cache.size());  // zip
+    L.ids.reserve(n);
+    L.blocks.reserve(n);
     for (size_t k = 0; k < n; ++k) {
       if (block_ids[k] < 0) continue;
       if (slot >= cache[k]->slots.size()) continue;
       L.ids.push_back(block_ids[k]);
-      L.blocks.push_back(cache[k]->slots[slot]);
+      L.blocks.push_back(cache[k]->slots[slot].get());
     }
     // Layers without blocks stay in the task (as empty entries) so per-layer
     // completion words line up with layer_names; the executor raises them at once.
@@ -581,6 +618,7 @@ void Engine::batch_load_inner(const std::string& instance_id, uint64_t tp_rank, 
     return;
   }
   if (!gpu->worker) throw cuda_init("engine pool is plain host memory; transfers need a pinned pool");
+  task.hold = std::move(cache);
   gpu->worker->submit_load(std::move(task));
 }
 

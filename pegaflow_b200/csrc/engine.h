@@ -44,11 +44,12 @@ struct LoadLayer {
   std::string name;
   pf_layer_desc reg;
   std::vector<int64_t> ids;
-  std::vector<LayerBlockPtr> blocks;
+  std::vector<const LayerBlock*> blocks;  // kept alive by LoadTask::hold
 };
 struct LoadTask {
   std::vector<LoadLayer> layers;
   std::string shm;
+  std::vector<SealedBlockPtr> hold;  // the sealed blocks read by the task
 };
 
 // Per-device worker: the executor plus the load thread of GpuWorkerPool
@@ -105,7 +106,8 @@ class Engine {
   struct SaveEntry {
     std::string layer_name;
     std::vector<int32_t> block_ids;
-    std::vector<std::string> hashes;
+    // Entries of one call that pass the same hash array share one list.
+    std::shared_ptr<const std::vector<std::string>> hashes;
   };
   void batch_save(const std::string& instance_id, uint64_t tp_rank, int device_id,
                   const std::vector<SaveEntry>& saves);

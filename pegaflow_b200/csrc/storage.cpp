@@ -252,28 +252,6 @@ bool Storage::inflight_has_slot(const std::string& ns, const std::string& hash, 
   return slot < it->second.slots.size() && it->second.slots[slot] != nullptr;
 }
 
-std::vector<char> Storage::needs_save(const std::string& ns, const std::vector<std::string>& hashes,
-                                      const std::vector<size_t>& idx, uint64_t slot) {
-  std::vector<char> out(idx.size(), 1);
-  BlockKey key{ns, std::string()};
-  {
-    std::lock_guard<std::mutex> g(cache_mu_);
-    for (size_t j = 0; j < idx.size(); ++j) {
-      key.hash = hashes[idx[j]];
-      if (index_.count(key)) out[j] = 0;
-    }
-  }
-  std::lock_guard<std::mutex> g(inflight_mu_);
-  if (inflight_.empty()) return out;
-  for (size_t j = 0; j < idx.size(); ++j) {
-    if (!out[j]) continue;
-    key.hash = hashes[idx[j]];
-    auto it = inflight_.find(key);
-    if (it != inflight_.end() && slot < it->second.slots.size() && it->second.slots[slot]) out[j] = 0;
-  }
-  return out;
-}
-
 void Storage::insert_slots(const std::string& ns, const std::vector<std::string>& hashes, uint64_t slot,
                            std::vector<LayerBlockPtr>& blocks, uint64_t total_slots) {
   // Same per-block steps as insert_slot (storage.rs:457-514), with the locks
@@ -333,6 +311,156 @@ void Storage::insert_slots(const std::string& ns, const std::vector<std::string>
       } else {
         counters_.admission_rejections.fetch_add(1);
       }
+    }
+  }
+}
+
+void Storage::probe_save(const std::string& ns, const std::vector<std::string>& hashes, SaveProbe* out) {
+  const size_t n = hashes.size();
+  out->cached.assign(n, 0);
+  out->filled.assign(n, std::vector<char>());
+  BlockKey key{ns, std::string()};
+  {
+    std::lock_guard<std::mutex> g(cache_mu_);
+    for (size_t i = 0; i < n; ++i) {
+      key.hash = hashes[i];
+      if (index_.count(key)) out->cached[i] = 1;
+    }
+  }
+  std::lock_guard<std::mutex> g(inflight_mu_);
+  if (inflight_.empty()) return;
+  for (size_t i = 0; i < n; ++i) {
+    if (out->cached[i]) continue;
+    key.hash = hashes[i];
+    auto it = inflight_.find(key);
+    if (it == inflight_.end()) continue;
+    const std::vector<LayerBlockPtr>& slots = it->second.slots;
+    std::vector<char>& f = out->filled[i];
+    f.resize(slots.size());
+    for (size_t s = 0; s < slots.size(); ++s) f[s] = slots[s] ? 1 : 0;
+  }
+}
+
+void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::string>& hashes,
+                                 const std::vector<SlotFill>& fills, uint64_t total_slots) {
+  // Hash-major form of calling insert_slots once per fill (fill-major). Per
+  // hash the fills are applied in order until the block seals; the sealed
+  // blocks then enter the cache in fill-major order (by the fill that sealed
+  // them, then by position), so LRU order and TinyLFU decisions match. A
+  // block that admission refuses is gone from the cache and from inflight,
+  // so fill-major would start a new inflight block from the later fills: the
+  // second pass below does that. That new block cannot seal in this call: it
+  // gets at most fills-1 < total_slots slots.
+  const size_t n = hashes.size();
+  if (fills.empty() || n == 0) return;
+  auto per_fill = [&] {
+    for (const SlotFill& f : fills) {
+      std::vector<LayerBlockPtr> blocks(n);
+      for (size_t i = 0; i < n; ++i) blocks[i] = layer_block_at(f.batch, i);
+      insert_slots(ns, hashes, f.slot, blocks, total_slots);
+    }
+  };
+  {
+    std::vector<char> seen(total_slots, 0);
+    for (const SlotFill& f : fills) {
+      if (f.slot >= total_slots || f.batch->blocks.size() != n || seen[f.slot]) return per_fill();
+      seen[f.slot] = 1;
+    }
+  }
+  std::vector<char> cached(n, 0);
+  BlockKey key{ns, std::string()};
+  {
+    std::lock_guard<std::mutex> g(cache_mu_);
+    for (size_t i = 0; i < n; ++i) {
+      key.hash = hashes[i];
+      cached[i] = index_.count(key) ? 1 : 0;
+    }
+  }
+  struct Seal {
+    size_t fill;
+    size_t index;
+    BlockKey key;
+    SealedBlockPtr block;
+  };
+  std::vector<Seal> seals;
+  {
+    std::unique_lock<std::mutex> gi(inflight_mu_);
+    // An inflight block with another slot count makes fill-major throw part
+    // way through its first fill; let it do exactly that.
+    if (!inflight_.empty()) {
+      for (size_t i = 0; i < n; ++i) {
+        if (cached[i]) continue;
+        key.hash = hashes[i];
+        auto it = inflight_.find(key);
+        if (it != inflight_.end() && it->second.total_slots != total_slots) {
+          gi.unlock();
+          return per_fill();
+        }
+      }
+    }
+    std::unordered_map<std::string, bool> sealed_here;  // a repeated hash finds its block sealed
+    for (size_t i = 0; i < n; ++i) {
+      if (cached[i]) continue;
+      if (!sealed_here.empty() && sealed_here.count(hashes[i])) continue;
+      key.hash = hashes[i];
+      auto it = inflight_.find(key);
+      if (it == inflight_.end()) {
+        Inflight fresh;
+        fresh.slots.assign(total_slots, nullptr);
+        fresh.remaining = total_slots;
+        fresh.total_slots = total_slots;
+        it = inflight_.emplace(key, std::move(fresh)).first;
+      }
+      Inflight& ib = it->second;
+      for (size_t f = 0; f < fills.size(); ++f) {
+        const uint64_t slot = fills[f].slot;
+        if (ib.slots[slot]) continue;
+        ib.footprint += fills[f].batch->blocks[i].size;
+        ib.slots[slot] = layer_block_at(fills[f].batch, i);
+        if (--ib.remaining == 0) {
+          auto sb = std::make_shared<SealedBlock>();
+          sb->slots = std::move(ib.slots);
+          sb->footprint = ib.footprint;
+          inflight_.erase(it);
+          sealed_here[hashes[i]] = true;
+          seals.push_back({f, i, key, std::move(sb)});
+          break;
+        }
+      }
+    }
+  }
+  if (seals.empty()) return;
+  std::stable_sort(seals.begin(), seals.end(), [](const Seal& a, const Seal& b) { return a.fill < b.fill; });
+  std::vector<const Seal*> refused;
+  {
+    std::lock_guard<std::mutex> g(cache_mu_);
+    for (Seal& s : seals) {
+      if (cache_insert_locked(s.key, std::move(s.block))) {
+        counters_.insertions.fetch_add(1);
+      } else {
+        counters_.admission_rejections.fetch_add(1);
+        if (s.fill + 1 < fills.size()) refused.push_back(&s);
+      }
+    }
+  }
+  if (refused.empty()) return;
+  std::lock_guard<std::mutex> gi(inflight_mu_);
+  for (const Seal* s : refused) {
+    auto it = inflight_.find(s->key);
+    if (it == inflight_.end()) {
+      Inflight fresh;
+      fresh.slots.assign(total_slots, nullptr);
+      fresh.remaining = total_slots;
+      fresh.total_slots = total_slots;
+      it = inflight_.emplace(s->key, std::move(fresh)).first;
+    }
+    Inflight& ib = it->second;
+    for (size_t f = s->fill + 1; f < fills.size(); ++f) {
+      const uint64_t slot = fills[f].slot;
+      if (ib.slots[slot]) continue;
+      ib.footprint += fills[f].batch->blocks[s->index].size;
+      ib.slots[slot] = layer_block_at(fills[f].batch, s->index);
+      --ib.remaining;
     }
   }
 }
@@ -441,6 +569,31 @@ uint64_t Storage::inflight_count() {
 uint64_t Storage::cached_count() {
   std::lock_guard<std::mutex> g(cache_mu_);
   return lru_.size();
+}
+
+namespace {
+std::vector<const LayerBlock*> slot_addresses(const std::vector<LayerBlockPtr>& slots) {
+  std::vector<const LayerBlock*> out(slots.size());
+  for (size_t s = 0; s < slots.size(); ++s) out[s] = slots[s].get();
+  return out;
+}
+}  // namespace
+
+Storage::BlockView Storage::cache_view() {
+  std::lock_guard<std::mutex> g(cache_mu_);
+  BlockView out;
+  out.reserve(lru_.size());
+  for (const auto& kv : lru_) out.emplace_back(kv.first.ns + '\0' + kv.first.hash, slot_addresses(kv.second->slots));
+  return out;
+}
+
+Storage::BlockView Storage::inflight_view() {
+  std::lock_guard<std::mutex> g(inflight_mu_);
+  BlockView out;
+  out.reserve(inflight_.size());
+  for (const auto& kv : inflight_) out.emplace_back(kv.first.ns + '\0' + kv.first.hash, slot_addresses(kv.second.slots));
+  std::sort(out.begin(), out.end());
+  return out;
 }
 
 }  // namespace pf

@@ -60,10 +60,39 @@ struct LayerBlock {
   uint8_t* k_ptr;
   uint8_t* v_ptr;  // null for contiguous blocks
   uint64_t size;   // block_size_bytes (memory_footprint)
+};
+// The blocks one save call wrote for one layer. They share the call's K (and
+// V) pool allocations, which go back to the pool when the last block of the
+// batch is dropped: the lifetime the reference gets from one
+// Arc<PinnedAllocation> per block (storage.rs:249-261), with one heap object
+// per (call, layer) instead of one per block.
+struct LayerBlockBatch {
+  std::vector<LayerBlock> blocks;
   std::shared_ptr<PoolAllocation> k_alloc;
   std::shared_ptr<PoolAllocation> v_alloc;
 };
+// Points at one block of a batch and keeps the whole batch alive.
 using LayerBlockPtr = std::shared_ptr<LayerBlock>;
+inline LayerBlockPtr layer_block_at(const std::shared_ptr<LayerBlockBatch>& batch, size_t i) {
+  return LayerBlockPtr(batch, &batch->blocks[i]);
+}
+
+// One layer's share of a multi-slot insert: block i of `batch` goes into
+// `slot` of hash i.
+struct SlotFill {
+  uint64_t slot;
+  std::shared_ptr<LayerBlockBatch> batch;
+};
+
+// Cache and inflight state of one hash list, for the save-side dedup of
+// several slots at once (lib.rs:613-616 per (hash, slot)).
+struct SaveProbe {
+  std::vector<char> cached;              // per hash: sealed in the cache
+  std::vector<std::vector<char>> filled; // per hash: filled slots (empty when not inflight)
+  bool needs(size_t i, uint64_t slot) const {
+    return !cached[i] && !(slot < filled[i].size() && filled[i][slot]);
+  }
+};
 
 struct SealedBlock {
   std::vector<LayerBlockPtr> slots;
@@ -121,14 +150,20 @@ class Storage {
   // allocator reports a large enough free region.
   std::shared_ptr<PoolAllocation> allocate(uint64_t size);
   bool inflight_has_slot(const std::string& ns, const std::string& hash, uint64_t slot);
-  // For each hash: !cache_contains && !inflight_has_slot, checked under one
-  // acquisition of each lock (the reference checks each block separately,
-  // lib.rs:613-616; the answers are the same).
-  std::vector<char> needs_save(const std::string& ns, const std::vector<std::string>& hashes,
-                               const std::vector<size_t>& idx, uint64_t slot);
+  // The save-side dedup answer, !cache_contains && !inflight_has_slot, for
+  // every (hash, slot) of one hash list, from one cache and one inflight
+  // lookup per hash under one acquisition of each lock (the reference checks
+  // each block separately, lib.rs:613-616; the answers are the same).
+  void probe_save(const std::string& ns, const std::vector<std::string>& hashes, SaveProbe* out);
   // insert_slot for many (hash, block) pairs of one slot, in order.
   void insert_slots(const std::string& ns, const std::vector<std::string>& hashes, uint64_t slot,
                     std::vector<LayerBlockPtr>& blocks, uint64_t total_slots);
+  // The same end state, cache order and admission decisions as calling
+  // insert_slots(ns, hashes, f.slot, <the blocks of f.batch>, total_slots)
+  // for each fill in order, with one inflight lookup per hash instead of one
+  // per (hash, fill).
+  void insert_slots_multi(const std::string& ns, const std::vector<std::string>& hashes,
+                          const std::vector<SlotFill>& fills, uint64_t total_slots);
   // StorageEngine::insert_slot (storage.rs:457-514). Throws pf::Error(Storage)
   // on SlotOutOfBounds / SlotCountMismatch.
   bool insert_slot(const std::string& ns, const std::string& hash, uint64_t slot, LayerBlockPtr block,
@@ -141,6 +176,11 @@ class Storage {
 
   uint64_t inflight_count();
   uint64_t cached_count();
+  // Read-only views (hash, slot block addresses; null = empty slot): the
+  // cache from least to most recently used, and inflight blocks by hash.
+  using BlockView = std::vector<std::pair<std::string, std::vector<const LayerBlock*>>>;
+  BlockView cache_view();
+  BlockView inflight_view();
   StorageCounters& counters() { return counters_; }
   PinnedPool& pool() { return *pool_; }
 

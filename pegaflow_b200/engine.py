@@ -160,9 +160,12 @@ class PegaEngine:
         entries = (N.SaveEntry * max(1, len(saves)))()
         keep = []
         converted = {}  # the same hash list object is often shared by every layer
+        converted_ids = {}  # and so is the block id list
         for i, (layer, ids, hashes) in enumerate(saves):
             name = layer.encode()
-            id_ptr, id_keep = N.int32_array(ids)
+            if id(ids) not in converted_ids:
+                converted_ids[id(ids)] = (ids, *N.int32_array(ids))
+            _, id_ptr, id_keep = converted_ids[id(ids)]
             if id(hashes) not in converted:
                 converted[id(hashes)] = (hashes, *N.bytes_array(hashes))
             _, h_ptr, hk = converted[id(hashes)]
