@@ -12,9 +12,10 @@ Three independent restatements of the reference (xiaguan/pegaflow) algorithm:
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import
 this module; the product library never does.
 
-Parity status: the reference publishes no golden vectors for KV bytes and its
-Rust sources cannot be built here (no Rust toolchain), so parity of the byte
-path is defined by copy identity and pinned against the reference's own tests
+Parity status: KV-byte parity unpinned. The reference publishes no golden
+vectors for KV bytes and its Rust sources cannot be built here (no Rust
+toolchain), so parity of the byte path is defined by copy identity and pinned
+against the reference's own tests
 where they exist (LoadState header, allocator arithmetic) and against fixtures
 generated from the reference's Python caller (tests/golden/). See the oracle
 header in pf_oracle.c.

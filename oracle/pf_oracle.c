@@ -7,7 +7,8 @@
  *
  * The "GPU memory" of a layer is a host byte array here; copies are memcpy.
  * Every function names the reference code it restates (paths relative to
- * the xiaguan/pegaflow tree). Parity status: the reference ships no golden
+ * the xiaguan/pegaflow tree). Parity status: KV-byte parity unpinned. The
+ * reference ships no golden
  * vectors for KV bytes (its 13 unit tests cover LoadState headers, allocator
  * arithmetic and size parsing only), and its Rust sources cannot be built
  * here, so byte-level parity of this restatement is pinned by copy identity

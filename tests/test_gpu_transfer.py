@@ -165,6 +165,23 @@ def test_many_chunks_and_mixed_layouts(cuda, oracle, mode, chunk, first):
     load_and_check(torch, oracle, ex, layers, regions, dst)
 
 
+@pytest.mark.parametrize("mode", MODES)
+def test_first_and_last_blocks_of_the_cache(cuda, oracle, mode):
+    """Block ids 0 and num_blocks-1 on both sides, so the last block's bytes
+    end exactly at the end of the registered tensor (split, blocks-first and
+    4-byte scale layouts)."""
+    torch = cuda
+    from pegaflow_b200 import Executor, PinnedBuffer
+
+    ex = Executor(0, save_mode=mode, load_mode=mode)
+    layers = [kv(torch, (2, 64, 16, 8, 128), torch.bfloat16, 1), kv(torch, (64, 2, 16, 4, 64), torch.float16, 2),
+              kv(torch, (64,), torch.float32, 3)]
+    src, dst = np.array([63, 0, 5, 62]), np.array([0, 63, 1, 62])
+    pool = PinnedBuffer(1 << 20)
+    regions = save_and_check(torch, oracle, ex, [(t, src) for t in layers], pool)
+    load_and_check(torch, oracle, ex, layers, regions, [dst] * 3)
+
+
 def test_empty_and_single_block_layers(cuda, oracle):
     torch = cuda
     from pegaflow_b200 import Executor, PinnedBuffer
