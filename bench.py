@@ -708,6 +708,8 @@ def main() -> int:
     e2e_value = world * 2 * payload * e2e_steps / e2e_wall / 1e9
     e2e_load_p50 = max_over_ranks(statistics.median([b for _, b in e2e_times]) * 1e3)
     eng_metrics = eng.metrics()
+    eng_ex = eng.executor(local).stats()
+    eng_metrics["executor_host_ms_per_call"] = eng_ex["host_ms"] / max(1, 2 * (e2e_steps + args.warmup))
     eng.close()
 
     # ---- the reference's copy strategy on the same GPU ------------------------
@@ -765,7 +767,7 @@ def main() -> int:
             "engine_metrics": {k: (round(eng_metrics[k], 2) if isinstance(eng_metrics[k], float) else eng_metrics[k])
                                for k in ("save_bytes", "load_bytes", "load_failures", "cache_block_evictions",
                                          "save_plan_ms", "save_transfer_ms", "save_insert_ms", "save_ms",
-                                         "load_ms")},
+                                         "load_ms", "executor_host_ms_per_call")},
         }
         print(json.dumps(line), flush=True)
     ranks.close()

@@ -212,6 +212,7 @@ typedef struct pf_executor_stats {
   double kernel_ms;
   uint64_t timed_launches;
   uint64_t bytes_p2p;       /* payload moved by pf_p2p_transfer */
+  double host_ms;           /* calling-thread time inside save/load/p2p: checks, plan, enqueue */
 } pf_executor_stats;
 int pf_executor_stats_get(pf_executor* exec, pf_executor_stats* out);
 int pf_executor_stats_reset(pf_executor* exec);

@@ -103,6 +103,7 @@ class ExecutorStats(Structure):
         ("kernel_ms", c_double),
         ("timed_launches", c_uint64),
         ("bytes_p2p", c_uint64),
+        ("host_ms", c_double),
     ]
 
 

@@ -9,6 +9,7 @@
 #include "executor.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <string>
 
@@ -104,6 +105,26 @@ constexpr uint64_t kMaxUnitBytes = 1ull << 31;
 uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
 bool aligned16(uint64_t v) { return (v & 15u) == 0; }
+
+// Plan offsets are 32-bit in PlanLayer and the kernel adds them in 32-bit
+// arithmetic, so every array end (not only each start) must fit.
+uint32_t plan_offset(uint64_t v) {
+  if (v > 0xffffffffull) throw invalid_argument("transfer too large for one plan (more than 2^32 units)");
+  return static_cast<uint32_t>(v);
+}
+void check_plan_ends(const std::vector<uint32_t>& ids, const std::vector<uint64_t>& side_base, uint64_t units) {
+  plan_offset(ids.size());
+  plan_offset(side_base.size());
+  plan_offset(units);
+}
+
+// Adds the calling thread's time in a save/load/p2p call to stats.host_ms
+// (constructed after the executor lock, so it is destroyed while held).
+struct HostTimer {
+  double* acc;
+  std::chrono::steady_clock::time_point t0 = std::chrono::steady_clock::now();
+  ~HostTimer() { *acc += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count(); }
+};
 
 // The copy of unit (b, u) must stay inside the registration. This is stricter
 // than segment_offset for non-split loads, where the reference copies
@@ -220,7 +241,7 @@ Executor::~Executor() {
 
 void Executor::build_save(const pf_save_layer* layers, uint64_t n_layers, bool staged, Built* b) {
   uint64_t dense = 0;
-  uint32_t unit_base = 0;
+  uint64_t unit_base = 0;
   for (uint64_t li = 0; li < n_layers; ++li) {
     const pf_save_layer& s = layers[li];
     const pf_layer_desc& l = s.layer;
@@ -286,9 +307,9 @@ void Executor::build_save(const pf_save_layer* layers, uint64_t n_layers, bool s
     p.tile_start = b->total_tiles;
     p.tile_count = static_cast<uint64_t>(g.units) * s.n * p.tiles_per_unit;
     if (p.tile_count > 0xffffffffull) throw invalid_argument("layer transfer too large for one plan");
-    p.ids_off = static_cast<uint32_t>(b->ids.size());
-    p.side_off = static_cast<uint32_t>(b->side_base.size());
-    p.unit_off = unit_base;
+    p.ids_off = plan_offset(b->ids.size());
+    p.side_off = plan_offset(b->side_base.size());
+    p.unit_off = plan_offset(unit_base);
     p.done_index = static_cast<uint32_t>(li);
     bool vec = aligned16(l.data_ptr) && aligned16(l.bytes_per_block) && aligned16(g.unit_stride) &&
                aligned16(g.unit_bytes);
@@ -326,14 +347,15 @@ void Executor::build_save(const pf_save_layer* layers, uint64_t n_layers, bool s
     dense = dense_layer + static_cast<uint64_t>(g.units) * s.n * g.unit_bytes;
     b->total_tiles += p.tile_count;
     b->total_bytes += static_cast<uint64_t>(g.units) * s.n * g.unit_bytes;
-    unit_base += g.units * static_cast<uint32_t>(s.n);
+    unit_base += static_cast<uint64_t>(g.units) * s.n;
+    check_plan_ends(b->ids, b->side_base, unit_base);
     b->layers.push_back(p);
   }
 }
 
 void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool staged, Built* b) {
   uint64_t dense = 0;
-  uint32_t unit_base = 0;
+  uint64_t unit_base = 0;
   for (uint64_t li = 0; li < n_layers; ++li) {
     const pf_load_layer& s = layers[li];
     const pf_layer_desc& l = s.layer;
@@ -424,9 +446,9 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
     p.tile_start = b->total_tiles;
     p.tile_count = static_cast<uint64_t>(g.units) * n * p.tiles_per_unit;
     if (p.tile_count > 0xffffffffull) throw invalid_argument("layer transfer too large for one plan");
-    p.ids_off = static_cast<uint32_t>(b->ids.size());
-    p.side_off = static_cast<uint32_t>(b->side_base.size());
-    p.unit_off = unit_base;
+    p.ids_off = plan_offset(b->ids.size());
+    p.side_off = plan_offset(b->side_base.size());
+    p.unit_off = plan_offset(unit_base);
     p.done_index = static_cast<uint32_t>(li);
     bool vec = aligned16(l.data_ptr) && aligned16(l.bytes_per_block) && aligned16(g.unit_stride) &&
                aligned16(g.unit_bytes);
@@ -465,13 +487,14 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
     dense = dense_layer + static_cast<uint64_t>(g.units) * n * g.unit_bytes;
     b->total_tiles += p.tile_count;
     b->total_bytes += static_cast<uint64_t>(g.units) * n * g.unit_bytes;
-    unit_base += g.units * static_cast<uint32_t>(n);
+    unit_base += static_cast<uint64_t>(g.units) * n;
+    check_plan_ends(b->ids, b->side_base, unit_base);
     b->layers.push_back(p);
   }
 }
 
 void Executor::build_p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push, Built* b) {
-  uint32_t unit_base = 0;
+  uint64_t unit_base = 0;
   for (uint64_t li = 0; li < n_layers; ++li) {
     const pf_p2p_layer& s = layers[li];
     const std::string lname = "#" + std::to_string(li);
@@ -524,6 +547,47 @@ void Executor::build_p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer
     std::reverse(keep.begin(), keep.end());
     const uint64_t n = keep.size();
 
+    // Warps write destination units in no order, so the destination layout
+    // must give every block its own bytes (the load path sends layouts that
+    // share bytes through ordered copy-engine copies instead).
+    uint64_t dst_k_region = 0;
+    const bool dst_owns_bytes =
+        is_split_layout(s.dst)
+            ? !mul_ovf(s.dst.num_blocks, s.dst.bytes_per_block, &dst_k_region) && s.dst.kv_stride_bytes >= dst_k_region
+            : s.dst.segments == 1;
+    if (!dst_owns_bytes) {
+      throw invalid_argument("peer transfer needs a destination layout whose blocks do not share bytes (layer " +
+                             lname + ")");
+    }
+    // One device on both sides with overlapping tensors: a byte read by one
+    // pair must not be written by another, or the result depends on timing.
+    if (peer == device_ && s.src.data_ptr < s.dst.data_ptr + s.dst.size_bytes &&
+        s.dst.data_ptr < s.src.data_ptr + s.src.size_bytes) {
+      const UnitGeometry gs = save_geometry(s.src), gd = save_geometry(s.dst);
+      std::vector<std::pair<uint64_t, uint64_t>> reads, writes;
+      for (uint64_t j = 0; j < n; ++j) {
+        const uint64_t sb = static_cast<uint64_t>(s.src_idx[keep[j]]);
+        const uint64_t db = static_cast<uint64_t>(s.dst_idx[keep[j]]);
+        for (uint32_t u = 0; u < gs.units; ++u) {
+          const uint64_t r = s.src.data_ptr + sb * s.src.bytes_per_block + u * gs.unit_stride;
+          const uint64_t w = s.dst.data_ptr + db * s.dst.bytes_per_block + u * gd.unit_stride;
+          reads.emplace_back(r, r + gs.unit_bytes);
+          writes.emplace_back(w, w + gd.unit_bytes);
+        }
+      }
+      std::sort(reads.begin(), reads.end());
+      std::sort(writes.begin(), writes.end());
+      for (size_t i = 0, k = 0; i < reads.size() && k < writes.size();) {
+        if (reads[i].second <= writes[k].first) {
+          ++i;
+        } else if (writes[k].second <= reads[i].first) {
+          ++k;
+        } else {
+          throw invalid_argument("source and destination blocks overlap in layer " + lname);
+        }
+      }
+    }
+
     PlanLayer p{};
     p.cache_base = local.data_ptr;
     p.block_pitch = local.bytes_per_block;
@@ -535,9 +599,9 @@ void Executor::build_p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer
     p.tile_start = b->total_tiles;
     p.tile_count = static_cast<uint64_t>(gl.units) * n * p.tiles_per_unit;
     if (p.tile_count > 0xffffffffull) throw invalid_argument("layer transfer too large for one plan");
-    p.ids_off = static_cast<uint32_t>(b->ids.size());
-    p.side_off = static_cast<uint32_t>(b->side_base.size());
-    p.unit_off = unit_base;
+    p.ids_off = plan_offset(b->ids.size());
+    p.side_off = plan_offset(b->side_base.size());
+    p.unit_off = plan_offset(unit_base);
     p.done_index = static_cast<uint32_t>(li);
     p.side_pitch = gl.unit_bytes;
     bool vec = aligned16(local.data_ptr) && aligned16(local.bytes_per_block) && aligned16(gl.unit_stride) &&
@@ -553,7 +617,8 @@ void Executor::build_p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer
     p.flags = vec ? kFlagVector : 0u;
     b->total_tiles += p.tile_count;
     b->total_bytes += static_cast<uint64_t>(gl.units) * n * gl.unit_bytes;
-    unit_base += gl.units * static_cast<uint32_t>(n);
+    unit_base += static_cast<uint64_t>(gl.units) * n;
+    check_plan_ends(b->ids, b->side_base, unit_base);
     b->layers.push_back(p);
   }
 }
@@ -577,6 +642,7 @@ void Executor::enable_peer(int peer) {
 
 void Executor::p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push, cudaStream_t caller) {
   std::lock_guard<std::mutex> g(mu_);
+  HostTimer timer{&stats_.host_ms};
   cuda_check(cudaSetDevice(device_), "cudaSetDevice");
   enable_peer(peer);
   Built b;
@@ -772,8 +838,35 @@ void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_
   if (timing_) {
     cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
     timed_.emplace_back(e0, e1);
+    // A caller that times without reading stats must not grow this list
+    // without bound: spans that have finished are folded in as we go.
+    if (timed_.size() >= 1024) fold_timings(false);
   }
   stats_.kernel_launches += 1;
+}
+
+void Executor::fold_timings(bool wait) {
+  size_t k = 0;
+  for (; k < timed_.size(); ++k) {
+    const auto& p = timed_[k];
+    if (wait) {
+      cuda_check(cudaEventSynchronize(p.second), "cudaEventSynchronize");
+    } else {
+      const cudaError_t q = cudaEventQuery(p.second);
+      if (q == cudaErrorNotReady) {
+        cudaGetLastError();
+        break;
+      }
+      cuda_check(q, "cudaEventQuery");
+    }
+    float ms = 0.f;
+    cuda_check(cudaEventElapsedTime(&ms, p.first, p.second), "cudaEventElapsedTime");
+    stats_.kernel_ms += ms;
+    stats_.timed_launches += 1;
+    event_pool_.push_back(p.first);
+    event_pool_.push_back(p.second);
+  }
+  timed_.erase(timed_.begin(), timed_.begin() + static_cast<std::ptrdiff_t>(k));
 }
 
 void Executor::copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h, cudaStream_t s) {
@@ -801,6 +894,7 @@ void Executor::copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h
 
 void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t caller) {
   std::lock_guard<std::mutex> g(mu_);
+  HostTimer timer{&stats_.host_ms};
   cuda_check(cudaSetDevice(device_), "cudaSetDevice");
   const bool staged = cfg_.save_mode != PF_MODE_DIRECT;
   Built b;
@@ -854,6 +948,7 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
 
 void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t caller, int64_t* layer_done) {
   std::lock_guard<std::mutex> g(mu_);
+  HostTimer timer{&stats_.host_ms};
   cuda_check(cudaSetDevice(device_), "cudaSetDevice");
   const bool staged = cfg_.load_mode != PF_MODE_DIRECT;
   Built b;
@@ -942,16 +1037,7 @@ void Executor::load_sync(const pf_load_layer* layers, uint64_t n_layers, int64_t
 
 void Executor::stats(pf_executor_stats* out) {
   std::lock_guard<std::mutex> g(mu_);
-  for (auto& p : timed_) {
-    cuda_check(cudaEventSynchronize(p.second), "cudaEventSynchronize");
-    float ms = 0.f;
-    cuda_check(cudaEventElapsedTime(&ms, p.first, p.second), "cudaEventElapsedTime");
-    stats_.kernel_ms += ms;
-    stats_.timed_launches += 1;
-    event_pool_.push_back(p.first);
-    event_pool_.push_back(p.second);
-  }
-  timed_.clear();
+  fold_timings(true);
   *out = stats_;
 }
 

@@ -130,6 +130,8 @@ class Executor {
   std::vector<int> peers_enabled_;
   bool timing_ = false;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed_;  // pending kernel spans
+  // Adds finished spans of timed_ to stats_ (all of them, waiting, when wait).
+  void fold_timings(bool wait);
   std::vector<cudaEvent_t> event_pool_;
   pf_executor_stats stats_{};
 };

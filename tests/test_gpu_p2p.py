@@ -62,6 +62,27 @@ def test_two_gpu_handoff(cuda, push):
     run_handoff(cuda, 1, 0, push, dup=True)
 
 
+def test_copies_inside_one_tensor_need_disjoint_blocks(cuda):
+    """Source and destination in the same tensor: a block that one pair reads
+    and another writes would race between warps, so it is refused before any
+    launch; disjoint blocks copy normally."""
+    torch = cuda
+    from pegaflow_b200 import Executor, Layout, P2PSpec
+
+    a = kv(torch, (2, 32, 16, 8, 128), 3, "cuda:0")
+    lay = Layout.from_tensor(a)
+    before = a.clone()
+    with pytest.raises(RuntimeError, match="overlap"):
+        Executor(0).p2p([P2PSpec(lay, lay, np.array([1, 2, 3]), np.array([3, 4, 5]))], 0)
+    torch.cuda.synchronize()
+    assert torch.equal(a, before)
+    Executor(0).p2p([P2PSpec(lay, lay, np.array([1, 2, 3]), np.array([10, 11, 31]))], 0)
+    torch.cuda.synchronize()
+    expect = before.clone()
+    expect[:, [10, 11, 31]] = before[:, [1, 2, 3]]
+    assert torch.equal(a, expect)
+
+
 def test_mismatched_layouts_are_refused(cuda):
     torch = cuda
     from pegaflow_b200 import Executor, Layout, P2PSpec
