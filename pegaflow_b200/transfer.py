@@ -41,6 +41,19 @@ class Layout:
             return Layout(t.data_ptr(), t.numel() * elt, shape[1], stride[1] * elt, stride[0] * elt, 2)
         return Layout(t.data_ptr(), t.numel() * elt, shape[0], stride[0] * elt, 0, 1)
 
+    @staticmethod
+    def from_token_major(t, page_size: int) -> "Layout":
+        """Layout of a token-major K or V buffer ``[slots, heads, head_dim]``
+        whose pages of ``page_size`` tokens are the blocks, registered as one
+        segments=1 layer, as the SGLang adapter derives it
+        (python/pegaflow/sglang/peagflow_radix_cache.py:203-222)."""
+        if page_size <= 0:
+            raise ValueError("page_size must be > 0")
+        slots, elt = t.shape[0], t.element_size()
+        if slots % page_size:
+            raise ValueError(f"KV slots ({slots}) must be divisible by page_size ({page_size})")
+        return Layout(t.data_ptr(), t.numel() * elt, slots // page_size, t.stride(0) * elt * page_size, 0, 1)
+
     def c(self) -> N.LayerDesc:
         return N.LayerDesc(
             self.data_ptr, self.size_bytes, self.num_blocks, self.bytes_per_block, self.kv_stride_bytes, self.segments

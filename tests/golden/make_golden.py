@@ -9,7 +9,12 @@ replaced by recording stubs, and records what it sends to the engine:
   * save_batches.json — the (layer, block_ids, block_hashes) list one save
     RPC carries for a batch of per-layer save tasks (worker.py:372-427);
   * load_requests.json — the load RPC arguments of start_load_kv
-    (worker.py:217-286).
+    (worker.py:217-286);
+  * tracker_traces.json, namespace.json — request-tracker traces and the
+    namespace hash (connector/common.py);
+  * sglang_registration.json — register_context arguments of the SGLang
+    adapter for token-major K/V buffers (sglang/peagflow_radix_cache.py:
+    160-250), with sglang's own modules stubbed.
 
 Usage (needs the reference tree; not run by the test suite):
     python tests/golden/make_golden.py /path/to/pegaflow
@@ -248,6 +253,37 @@ def main(argv: list[str]) -> int:
                       "num_kv_heads": 8, "head_size": 128, "num_hidden_layers": 32, "cache_dtype": "auto"},
           "namespace": derive_namespace(cfg, 2)}
     (OUT / "namespace.json").write_text(json.dumps(ns, indent=1) + "\n")
+
+    # ---- SGLang adapter registration (peagflow_radix_cache.py:160-250) ----------
+    # configs[0] registers separate K and V tensors as segments=1 layers, as
+    # the SGLang adapter does. sglang is not installed: stub the names the
+    # adapter module imports (its registration code uses none of them).
+    stubs = {"sglang": [], "sglang.srt": [], "sglang.srt.mem_cache": [],
+             "sglang.srt.mem_cache.base_prefix_cache": ["MatchResult"],
+             "sglang.srt.mem_cache.hicache_storage": ["get_hash_str"],
+             "sglang.srt.mem_cache.radix_cache": ["RadixCache", "RadixKey", "TreeNode"]}
+    for mod, names in stubs.items():
+        m = types.ModuleType(mod)
+        for n in names:
+            setattr(m, n, type(n, (), {}))
+        sys.modules[mod] = m
+    from pegaflow.sglang.peagflow_radix_cache import PeagflowRadixCache
+
+    sg_out = []
+    for name, shape, dtype, page in [("gpt2_k_token_major", (4096, 12, 64), torch.float16, 16),
+                                     ("llama8b_k_token_major", (131072, 8, 128), torch.bfloat16, 16),
+                                     ("page_size_1", (256, 4, 64), torch.float16, 1),
+                                     ("page_size_64", (8192, 2, 128), torch.bfloat16, 64)]:
+        fake_self = types.SimpleNamespace(page_size=page, engine_client=FakeEngineRpcClient(), instance_id="inst",
+                                          namespace="ns", tp_rank=0, tp_size=1, device_id=0)
+        t = torch.empty(shape, dtype=dtype, device="meta")
+        _Recorder.calls = []
+        PeagflowRadixCache._register_single_layer(fake_self, tensor=t, layer_name=name, total_layers=24)
+        (_, args), = _Recorder.calls
+        sg_out.append({"case": name, "shape": list(shape), "element_size": t.element_size(), "page_size": page,
+                       "num_layers": args[5], "num_blocks": args[8], "bytes_per_block": args[9],
+                       "kv_stride_bytes": args[10], "segments": args[11]})
+    (OUT / "sglang_registration.json").write_text(json.dumps(sg_out, indent=1) + "\n")
     print("wrote", [p.name for p in sorted(OUT.glob("*.json"))])
     return 0
 

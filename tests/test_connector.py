@@ -113,6 +113,28 @@ def test_registration_arguments_match_reference():
         assert args[:7] == ("inst", "ns", 0, 1, 0, 1, case["case"])
 
 
+def test_token_major_registration_matches_reference_sglang_adapter():
+    """configs[0] registers separate K and V buffers as segments=1 layers, as
+    the reference's SGLang adapter does; its registration arguments for
+    token-major buffers were recorded by make_golden.py."""
+    import torch
+
+    from pegaflow_b200 import Layout
+
+    dtypes = {2: torch.float16, 4: torch.float32}
+    for case in json.loads((GOLDEN / "sglang_registration.json").read_text()):
+        t = torch.empty(case["shape"], dtype=dtypes[case["element_size"]], device="meta")
+        lay = Layout.from_token_major(t, case["page_size"])
+        assert (lay.num_blocks, lay.bytes_per_block, lay.kv_stride_bytes, lay.segments) == (
+            case["num_blocks"], case["bytes_per_block"], case["kv_stride_bytes"], case["segments"]), case["case"]
+        assert case["num_layers"] == 24
+    # The same memory seen as vLLM-style blocks [blocks, page, heads, dim]
+    # registers identically (the GPT-2 shape of configs[0]).
+    t = torch.empty((4096, 12, 64), dtype=torch.float16, device="meta")
+    a, b = Layout.from_token_major(t, 16), Layout.from_tensor(t.view(256, 16, 12, 64))
+    assert (a.num_blocks, a.bytes_per_block, a.segments) == (b.num_blocks, b.bytes_per_block, b.segments)
+
+
 def _meta(intents):
     from pegaflow_b200.connector import PegaConnectorMetadata, SaveIntent
 
