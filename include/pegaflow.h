@@ -318,6 +318,15 @@ typedef struct pf_engine_config {
   uint64_t pre_evict_target_bytes;
   uint64_t pre_evict_interval_ms;
   pf_executor_config executor;    /* used for every device the engine opens */
+  /* Packed-file tier: sealed blocks are written through to packed files and
+   * read back on a query miss (the reference's DFS offload, seal_offload.rs,
+   * file format unchanged; the per-block metadata it keeps in Redis lives in
+   * a sidecar file beside each packed file). NULL or "" = off. */
+  const char* dfs_root;
+  uint64_t dfs_quota_bytes;       /* 0 = 50 GiB (server --dfs-quota default) */
+  uint64_t dfs_scan_interval_ms;  /* 0 = 100 */
+  uint32_t dfs_max_pack_size;     /* blocks per packed file, 0 = 64 */
+  uint32_t reserved1;
 } pf_engine_config;
 
 void pf_engine_config_default(pf_engine_config* cfg);
@@ -370,6 +379,45 @@ int pf_engine_save_kv_blocks(pf_engine* e, const char* instance_id,
 int pf_engine_count_prefix_hit_blocks(pf_engine* e, const char* instance_id,
                                       const pf_bytes* block_hashes, uint64_t n,
                                       uint64_t* out_hits);
+
+/* PrefetchStatus (seal_offload.rs:584-601) as engine.proto's QueryResponse
+ * carries it (service.rs:283-297). */
+typedef enum pf_prefetch_state {
+  PF_PREFETCH_READY = 0,        /* hit_blocks are in the pool */
+  PF_PREFETCH_LOADING = 1,      /* loading_blocks are being read back from packed files */
+  PF_PREFETCH_PARTIAL_MISS = 2  /* missing_blocks are in neither */
+} pf_prefetch_state;
+typedef struct pf_prefetch_status {
+  uint32_t state; /* pf_prefetch_state */
+  uint32_t reserved;
+  uint64_t hit_blocks;
+  uint64_t loading_blocks;
+  uint64_t missing_blocks;
+} pf_prefetch_status;
+/* PegaEngine::count_prefix_hit_blocks_async (lib.rs:855-942): with the
+ * packed-file tier on, a miss that the tier holds starts a background read
+ * of the rest of the prefix and reports LOADING (ask again later); with the
+ * tier off it is count_prefix_hit_blocks reported as READY. */
+int pf_engine_query_prefetch(pf_engine* e, const char* instance_id, const pf_bytes* block_hashes,
+                             uint64_t n, pf_prefetch_status* out);
+
+typedef struct pf_dfs_stats {
+  uint64_t files;             /* packed files indexed */
+  uint64_t blocks;            /* blocks indexed */
+  uint64_t usage_bytes;       /* bytes in indexed packed files */
+  uint64_t written_files;
+  uint64_t written_blocks;
+  uint64_t write_failures;
+  uint64_t prefetched_blocks; /* blocks read back into the pool */
+  uint64_t prefetch_failures;
+  uint64_t evicted_files;     /* removed by the quota */
+} pf_dfs_stats;
+/* Tier counters (PF_ERR_INVALID_ARGUMENT when the tier is off). */
+int pf_engine_dfs_stats(pf_engine* e, pf_dfs_stats* out);
+/* Waits up to timeout_s for queued writes and reads; *out_idle = 1 if done. */
+int pf_engine_dfs_flush(pf_engine* e, double timeout_s, int* out_idle);
+/* Runs the quota check now (it also runs every dfs_scan_interval_ms). */
+int pf_engine_dfs_check_quota(pf_engine* e);
 
 /* PegaEngine::batch_load_kv_blocks_multi_layer (lib.rs:957-1069).
  * Returns after the task is queued; completion is written to the LoadState

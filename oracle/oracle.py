@@ -7,7 +7,9 @@ Three independent restatements of the reference (xiaguan/pegaflow) algorithm:
   * numpy twins (``np_save_layer`` / ``np_load_layer``) of the same copies;
   * ``EngineModel``: the engine's host logic (lib.rs:373-1069, storage.rs)
     — registration checks, dedup, slot/seal, prefix hits, load selection —
-    over host byte arrays.
+    over host byte arrays;
+  * ``dfs_pack`` / ``dfs_file_meta``: the packed-file tier's file bytes and
+    metadata records (seal_offload.rs:79-105, 379-448).
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import
 this module; the product library never does.
@@ -426,3 +428,37 @@ def mt_transfer(layers: Sequence[tuple[Layout, np.ndarray, np.ndarray, np.ndarra
         arr[i].k_pool = _ptr(kp)
         arr[i].v_pool = _ptr(vp) if vp is not None else None
     return lib().or_mt_transfer(arr, len(layers), 1 if save else 0, threads)
+
+
+# ----------------------------------------------------------------------------
+# Packed-file tier (seal_offload.rs)
+# ----------------------------------------------------------------------------
+
+def dfs_pack(blocks, file_name: str):
+    """write_packed_file (seal_offload.rs:379-448) restated. ``blocks`` is a
+    list of sealed blocks, each a list of slots ``(k_bytes, v_bytes or None)``
+    with a slot's size = len(k) + len(v). Returns the packed file's bytes and
+    each block's BlockMeta record as serde_json writes it (compact, fields in
+    declaration order: file, offset, slots[is_split, size], total_slots)."""
+    import json
+
+    total_slots = len(blocks[0]) if blocks else 0
+    data, metas, offset = bytearray(), [], 0
+    for slots in blocks:
+        slot_meta = []
+        for k, v in slots:
+            data += bytes(k)
+            if v is not None:
+                data += bytes(v)
+            slot_meta.append({"is_split": v is not None, "size": len(k) + (len(v) if v is not None else 0)})
+        metas.append(json.dumps({"file": file_name, "offset": offset, "slots": slot_meta,
+                                 "total_slots": total_slots}, separators=(",", ":")))
+        offset += sum(s["size"] for s in slot_meta)
+    return bytes(data), metas
+
+
+def dfs_file_meta(hashes, size: int) -> str:
+    """FileMeta (seal_offload.rs:100-105) as serde_json writes it."""
+    import json
+
+    return json.dumps({"blocks": [bytes(h).hex() for h in hashes], "size": size}, separators=(",", ":"))

@@ -131,11 +131,32 @@ class EngineConfig(Structure):
         ("pre_evict_target_bytes", c_uint64),
         ("pre_evict_interval_ms", c_uint64),
         ("executor", ExecutorConfig),
+        ("dfs_root", c_char_p),
+        ("dfs_quota_bytes", c_uint64),
+        ("dfs_scan_interval_ms", c_uint64),
+        ("dfs_max_pack_size", c_uint32),
+        ("reserved1", c_uint32),
     ]
 
 
 class Bytes(Structure):
     _fields_ = [("data", POINTER(c_uint8)), ("len", c_uint64)]
+
+
+class PrefetchStatus(Structure):
+    _fields_ = [
+        ("state", c_uint32),
+        ("reserved", c_uint32),
+        ("hit_blocks", c_uint64),
+        ("loading_blocks", c_uint64),
+        ("missing_blocks", c_uint64),
+    ]
+
+
+class DfsStats(Structure):
+    _fields_ = [(name, c_uint64) for name in (
+        "files", "blocks", "usage_bytes", "written_files", "written_blocks", "write_failures",
+        "prefetched_blocks", "prefetch_failures", "evicted_files")]
 
 
 class SaveEntry(Structure):
@@ -228,6 +249,10 @@ _SIGNATURES = {
         [c_void_p, c_char_p, c_uint64, c_int32, c_char_p, POINTER(c_int32), POINTER(Bytes), c_uint64],
     ),
     "pf_engine_count_prefix_hit_blocks": (c_int, [c_void_p, c_char_p, POINTER(Bytes), c_uint64, POINTER(c_uint64)]),
+    "pf_engine_query_prefetch": (c_int, [c_void_p, c_char_p, POINTER(Bytes), c_uint64, POINTER(PrefetchStatus)]),
+    "pf_engine_dfs_stats": (c_int, [c_void_p, POINTER(DfsStats)]),
+    "pf_engine_dfs_flush": (c_int, [c_void_p, c_double, POINTER(c_int)]),
+    "pf_engine_dfs_check_quota": (c_int, [c_void_p]),
     "pf_engine_batch_load_kv_blocks": (
         c_int,
         [

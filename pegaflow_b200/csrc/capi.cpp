@@ -376,6 +376,49 @@ int pf_engine_count_prefix_hit_blocks(pf_engine* e, const char* instance_id, con
   });
 }
 
+int pf_engine_query_prefetch(pf_engine* e, const char* instance_id, const pf_bytes* block_hashes, uint64_t n,
+                             pf_prefetch_status* out) {
+  if (!e || !out || (!block_hashes && n)) return null_arg("argument");
+  return guarded([&] {
+    std::vector<std::string> hashes;
+    hashes.reserve(n);
+    for (uint64_t k = 0; k < n; ++k) hashes.push_back(bytes_str(block_hashes[k]));
+    const pf::PrefetchStatus s = e->impl->query_prefetch(str(instance_id), hashes);
+    *out = pf_prefetch_status{};
+    out->state = static_cast<uint32_t>(s.state);
+    out->hit_blocks = s.hit_blocks;
+    out->loading_blocks = s.loading_blocks;
+    out->missing_blocks = s.missing_blocks;
+  });
+}
+
+namespace {
+pf::DfsTier* dfs_or_throw(pf_engine* e) {
+  pf::DfsTier* t = e->impl->dfs();
+  if (!t) throw pf::invalid_argument("the packed-file tier is off (no dfs_root)");
+  return t;
+}
+}  // namespace
+
+int pf_engine_dfs_stats(pf_engine* e, pf_dfs_stats* out) {
+  if (!e || !out) return null_arg("argument");
+  return guarded([&] {
+    const pf::DfsStats s = dfs_or_throw(e)->stats();
+    *out = pf_dfs_stats{s.files,          s.blocks,           s.usage_bytes,       s.written_files, s.written_blocks,
+                        s.write_failures, s.prefetched_blocks, s.prefetch_failures, s.evicted_files};
+  });
+}
+
+int pf_engine_dfs_flush(pf_engine* e, double timeout_s, int* out_idle) {
+  if (!e || !out_idle) return null_arg("argument");
+  return guarded([&] { *out_idle = dfs_or_throw(e)->flush(timeout_s) ? 1 : 0; });
+}
+
+int pf_engine_dfs_check_quota(pf_engine* e) {
+  if (!e) return null_arg("engine");
+  return guarded([&] { dfs_or_throw(e)->check_quota(); });
+}
+
 int pf_engine_batch_load_kv_blocks(pf_engine* e, const char* instance_id, uint64_t tp_rank, int32_t device_id,
                                    const char* load_state_shm, const char* const* layer_names, uint64_t n_layers,
                                    const int32_t* block_ids, const pf_bytes* block_hashes, uint64_t n_blocks) {

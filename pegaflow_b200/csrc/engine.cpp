@@ -185,6 +185,17 @@ Engine::Engine(const pf_engine_config& cfg) : cfg_(cfg) {
   if (cfg_.pre_evict_target_bytes) sc.pre_evict_target_bytes = cfg_.pre_evict_target_bytes;
   if (cfg_.pre_evict_interval_ms) sc.pre_evict_interval_ms = cfg_.pre_evict_interval_ms;
   storage_ = std::make_unique<Storage>(pool_, sc);
+  if (cfg_.dfs_root && cfg_.dfs_root[0]) {
+    DfsConfig dc;
+    dc.root = cfg_.dfs_root;
+    if (cfg_.dfs_quota_bytes) dc.quota_bytes = cfg_.dfs_quota_bytes;
+    if (cfg_.dfs_scan_interval_ms) dc.scan_interval_ms = cfg_.dfs_scan_interval_ms;
+    if (cfg_.dfs_max_pack_size) dc.max_pack_size = cfg_.dfs_max_pack_size;
+    dfs_ = std::make_unique<DfsTier>(storage_.get(), dc);
+    DfsTier* tier = dfs_.get();
+    storage_->set_seal_listener([tier](const BlockKey& k, const SealedBlockPtr& b) { tier->on_seal(k, b); });
+  }
+  cfg_.dfs_root = nullptr;  // the caller's string is not kept
 }
 
 Engine::~Engine() {
@@ -200,6 +211,10 @@ Engine::~Engine() {
     instances_.clear();
   }
   devs.clear();
+  if (dfs_) {
+    storage_->set_seal_listener(nullptr);
+    dfs_.reset();  // stops its threads before the storage they use goes
+  }
   storage_.reset();
   pool_.reset();
 }
@@ -550,6 +565,17 @@ uint64_t Engine::count_prefix_hit_blocks(const std::string& instance_id, const s
   }
   if (hit) counters_.hits.fetch_add(hit);
   return hit;
+}
+
+PrefetchStatus Engine::query_prefetch(const std::string& instance_id, const std::vector<std::string>& hashes) {
+  if (!dfs_) {
+    // The server's query without the DFS tier (service.rs:307-319).
+    PrefetchStatus st;
+    st.hit_blocks = count_prefix_hit_blocks(instance_id, hashes);
+    return st;
+  }
+  auto inst = get_instance(instance_id);
+  return dfs_->query(inst->ns, hashes);
 }
 
 void Engine::batch_load(const std::string& instance_id, uint64_t tp_rank, int device_id, const std::string& shm,

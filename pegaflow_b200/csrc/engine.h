@@ -13,6 +13,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "dfs_tier.h"
 #include "executor.h"
 #include "pegaflow.h"
 #include "storage.h"
@@ -112,6 +113,10 @@ class Engine {
   void batch_save(const std::string& instance_id, uint64_t tp_rank, int device_id,
                   const std::vector<SaveEntry>& saves);
   uint64_t count_prefix_hit_blocks(const std::string& instance_id, const std::vector<std::string>& hashes);
+  // count_prefix_hit_blocks_async (lib.rs:855-942) over the packed-file tier;
+  // READY with the plain prefix count when the tier is off.
+  PrefetchStatus query_prefetch(const std::string& instance_id, const std::vector<std::string>& hashes);
+  DfsTier* dfs() { return dfs_.get(); }
   void batch_load(const std::string& instance_id, uint64_t tp_rank, int device_id, const std::string& shm,
                   const std::vector<std::string>& layer_names, const std::vector<int32_t>& block_ids,
                   const std::vector<std::string>& hashes);
@@ -133,6 +138,7 @@ class Engine {
   pf_engine_config cfg_;
   std::shared_ptr<PinnedPool> pool_;
   std::unique_ptr<Storage> storage_;
+  std::unique_ptr<DfsTier> dfs_;  // null when the packed-file tier is off
   std::shared_mutex inst_mu_;
   std::unordered_map<std::string, std::shared_ptr<InstanceContext>> instances_;
   std::mutex dev_mu_;

@@ -304,6 +304,7 @@ void Storage::insert_slots(const std::string& ns, const std::vector<std::string>
     }
   }
   if (!sealed.empty()) {
+    for (const auto& kv : sealed) notify_sealed(kv.first, kv.second);
     std::lock_guard<std::mutex> g(cache_mu_);
     for (auto& kv : sealed) {
       if (cache_insert_locked(kv.first, std::move(kv.second))) {
@@ -431,6 +432,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
   }
   if (seals.empty()) return;
   std::stable_sort(seals.begin(), seals.end(), [](const Seal& a, const Seal& b) { return a.fill < b.fill; });
+  for (const Seal& s : seals) notify_sealed(s.key, s.block);
   std::vector<const Seal*> refused;
   {
     std::lock_guard<std::mutex> g(cache_mu_);
@@ -522,6 +524,7 @@ bool Storage::insert_slot(const std::string& ns, const std::string& hash, uint64
     }
   }
   if (sealed) {
+    notify_sealed(key, sealed);
     std::lock_guard<std::mutex> g(cache_mu_);
     if (cache_insert_locked(key, std::move(sealed))) {
       counters_.insertions.fetch_add(1);
@@ -530,6 +533,31 @@ bool Storage::insert_slot(const std::string& ns, const std::string& hash, uint64
     }
   }
   return true;
+}
+
+void Storage::set_seal_listener(SealListener fn) {
+  std::lock_guard<std::mutex> g(listener_mu_);
+  seal_listener_ = std::move(fn);
+}
+
+void Storage::notify_sealed(const BlockKey& key, const SealedBlockPtr& block) {
+  SealListener fn;
+  {
+    std::lock_guard<std::mutex> g(listener_mu_);
+    fn = seal_listener_;
+  }
+  if (fn) fn(key, block);
+}
+
+bool Storage::cache_insert(const std::string& ns, const std::string& hash, SealedBlockPtr block) {
+  std::lock_guard<std::mutex> g(cache_mu_);
+  const bool ok = cache_insert_locked(BlockKey{ns, hash}, std::move(block));
+  if (ok) {
+    counters_.insertions.fetch_add(1);
+  } else {
+    counters_.admission_rejections.fetch_add(1);
+  }
+  return ok;
 }
 
 bool Storage::cache_contains(const std::string& ns, const std::string& hash) {

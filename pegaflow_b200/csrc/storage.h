@@ -11,6 +11,7 @@
 #include <atomic>
 #include <condition_variable>
 #include <cstdint>
+#include <functional>
 #include <list>
 #include <memory>
 #include <mutex>
@@ -169,6 +170,14 @@ class Storage {
   bool insert_slot(const std::string& ns, const std::string& hash, uint64_t slot, LayerBlockPtr block,
                    uint64_t total_slots);
   bool cache_contains(const std::string& ns, const std::string& hash);
+  // Inserts a block that was not sealed here (a block read back from the
+  // packed-file tier), with the same admission as a freshly sealed block.
+  bool cache_insert(const std::string& ns, const std::string& hash, SealedBlockPtr block);
+  // Called once for every block that seals, before it is offered to the
+  // cache (the reference's seal notification, storage.rs:494-503). It runs on
+  // the inserting thread outside the storage locks and must not block.
+  using SealListener = std::function<void(const BlockKey&, const SealedBlockPtr&)>;
+  void set_seal_listener(SealListener fn);
   // cache_lookup_many (storage.rs:529-547): bumps recency/frequency.
   std::vector<SealedBlockPtr> cache_lookup_many(const std::string& ns, const std::vector<std::string>& hashes);
   // Read-only peek (no LRU/frequency update), for introspection.
@@ -206,6 +215,10 @@ class Storage {
   std::unordered_map<BlockKey, LruList::iterator, BlockKeyHash> index_;
   std::unique_ptr<TinyLfu> lfu_;
   StorageCounters counters_;
+
+  void notify_sealed(const BlockKey& key, const SealedBlockPtr& block);
+  std::mutex listener_mu_;
+  SealListener seal_listener_;
 
   std::thread pre_evict_;
   std::mutex stop_mu_;

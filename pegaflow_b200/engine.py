@@ -39,7 +39,14 @@ class PegaEngine:
         pre_evict: Optional[tuple[int, int, int]] = None,
         pool_kind: str = "pinned",
         executor: Optional[dict] = None,
+        dfs_root: Optional[str] = None,
+        dfs_quota: int = 0,
+        dfs_scan_interval_ms: int = 0,
+        dfs_max_pack_size: int = 0,
     ):
+        """``dfs_root`` turns on the packed-file tier: sealed blocks are
+        written through to ``{dfs_root}/{namespace}/{uuid}.bin`` and read
+        back when ``query_prefetch`` finds them missing from the pool."""
         cfg = N.EngineConfig()
         N.lib.pf_engine_config_default(byref(cfg))
         cfg.pool_bytes = pool_size
@@ -55,6 +62,11 @@ class PegaEngine:
             modes = {"auto": N.PF_MODE_AUTO, "staged": N.PF_MODE_STAGED, "direct": N.PF_MODE_DIRECT}
             for k, v in executor.items():
                 setattr(cfg.executor, k, modes[v] if k.endswith("_mode") else v)
+        root = dfs_root.encode() if dfs_root else None  # kept alive across the create call
+        cfg.dfs_root = root
+        cfg.dfs_quota_bytes = dfs_quota
+        cfg.dfs_scan_interval_ms = dfs_scan_interval_ms
+        cfg.dfs_max_pack_size = dfs_max_pack_size
         h = c_void_p()
         N.check(N.lib.pf_engine_create(byref(cfg), byref(h)))
         self._h = h
@@ -116,6 +128,31 @@ class PegaEngine:
         N.check(N.lib.pf_engine_count_prefix_hit_blocks(self._h, instance_id.encode(), arr, len(block_hashes), byref(out)))
         del keep
         return out.value
+
+    def query_prefetch(self, instance_id: str, block_hashes: Sequence[bytes]) -> dict:
+        """count_prefix_hit_blocks_async (pegaflow-core/src/lib.rs:855-942):
+        ``prefetch_state`` is "ready", "loading" (blocks are being read back
+        from the packed-file tier: ask again) or "partial_miss"."""
+        arr, keep = N.bytes_array(block_hashes)
+        s = N.PrefetchStatus()
+        N.check(N.lib.pf_engine_query_prefetch(self._h, instance_id.encode(), arr, len(block_hashes), byref(s)))
+        del keep
+        return {"hit_blocks": s.hit_blocks, "prefetch_state": ("ready", "loading", "partial_miss")[s.state],
+                "loading_blocks": s.loading_blocks, "missing_blocks": s.missing_blocks}
+
+    def dfs_stats(self) -> dict:
+        s = N.DfsStats()
+        N.check(N.lib.pf_engine_dfs_stats(self._h, byref(s)))
+        return {f: getattr(s, f) for f, _ in N.DfsStats._fields_}
+
+    def dfs_flush(self, timeout_s: float = 30.0) -> bool:
+        """Wait for queued packed-file writes and reads; False on timeout."""
+        idle = ctypes.c_int()
+        N.check(N.lib.pf_engine_dfs_flush(self._h, timeout_s, byref(idle)))
+        return bool(idle.value)
+
+    def dfs_check_quota(self) -> None:
+        N.check(N.lib.pf_engine_dfs_check_quota(self._h))
 
     def batch_load_kv_blocks(
         self,

@@ -6,8 +6,10 @@ gRPC status mapping (service.rs:77-88), the CUDA IPC tensor registry that
 keeps the vLLM workers' KV tensors mapped in this process (registry.rs), and
 the command line (lib.rs:43-113). Run with ``python -m pegaflow_b200.server``.
 
-Not served: the DFS/Redis persistence tier and OTel export (their flags are
-accepted; --redis-url is refused).
+The DFS tier (seal_offload.rs) is served by --dfs-local-index: packed files
+under --dfs-root in the reference's format, with the block metadata in
+sidecar files, since this build has no Redis (--redis-url is refused). OTel
+export is not served (its flags are accepted).
 """
 
 from __future__ import annotations
@@ -144,10 +146,13 @@ class EngineService:
         return P.LoadResponse(status=self._ok())
 
     def Query(self, req, context):
-        hits = self._engine_call(context, self.engine.count_prefix_hit_blocks, req.instance_id,
-                                 list(req.block_hashes))
-        return P.QueryResponse(status=self._ok(), hit_blocks=hits, prefetch_state=P.PREFETCH_READY,
-                               loading_blocks=0, missing_blocks=0)
+        # service.rs:262-319: with the packed-file tier on, a prefix that the
+        # tier holds is read back in the background and reported as LOADING.
+        q = self._engine_call(context, self.engine.query_prefetch, req.instance_id, list(req.block_hashes))
+        state = {"ready": P.PREFETCH_READY, "loading": P.PREFETCH_LOADING,
+                 "partial_miss": P.PREFETCH_PARTIAL_MISS}[q["prefetch_state"]]
+        return P.QueryResponse(status=self._ok(), hit_blocks=q["hit_blocks"], prefetch_state=state,
+                               loading_blocks=q["loading_blocks"], missing_blocks=q["missing_blocks"])
 
     def UnregisterContext(self, req, context):
         dropped = self.registry.drop_instance(req.instance_id)
@@ -209,6 +214,9 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--dfs-root", default="/tmp/pega")
     ap.add_argument("--dfs-quota", type=parse_memory_size, default=parse_memory_size("50gb"))
     ap.add_argument("--dfs-scan-interval-ms", type=int, default=100)
+    ap.add_argument("--dfs-local-index", action="store_true",
+                    help="write sealed blocks through to packed files under --dfs-root and prefetch them back "
+                         "on a query miss, with the block metadata in sidecar files instead of Redis")
     return ap
 
 
@@ -217,7 +225,8 @@ def main(argv=None) -> int:
     logging.basicConfig(level=getattr(logging, args.log_level.upper(), logging.INFO),
                         format="%(asctime)s %(levelname)s %(name)s: %(message)s")
     if args.redis_url:
-        raise SystemExit("--redis-url: the DFS/Redis persistence tier is not part of this build")
+        raise SystemExit("--redis-url: block metadata is not kept in Redis by this build; "
+                         "--dfs-local-index keeps it in sidecar files under --dfs-root")
     import torch
 
     if torch.cuda.is_available():
@@ -226,8 +235,10 @@ def main(argv=None) -> int:
     from .engine import PegaEngine
 
     pre_evict = (args.pre_evict_threshold, args.pre_evict_target, args.pre_evict_interval_ms) if args.pre_evict else None
+    dfs = dict(dfs_root=args.dfs_root, dfs_quota=args.dfs_quota,
+               dfs_scan_interval_ms=args.dfs_scan_interval_ms) if args.dfs_local_index else {}
     engine = PegaEngine(args.pool_size, args.use_hugepages, enable_lfu_admission=not args.disable_lfu_admission,
-                        hint_value_size_bytes=args.hint_value_size or 0, pre_evict=pre_evict)
+                        hint_value_size_bytes=args.hint_value_size or 0, pre_evict=pre_evict, **dfs)
     server, _, port = serve(engine, args.addr)
     log.info("pegaflow_b200 engine server listening on %s (port %d)", args.addr, port)
     server.wait_for_termination()

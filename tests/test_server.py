@@ -88,6 +88,29 @@ def test_health_register_query_unregister(served):
     assert service.registry.drop_instance("inst") == 0
 
 
+def test_query_reports_packed_file_tier_states(native, tmp_path):
+    """With the packed-file tier on, Query carries the tier's state
+    (service.rs:283-305): blocks held nowhere are a partial miss."""
+    import numpy as np
+
+    from pegaflow_b200 import EngineRpcClient, PegaEngine
+    from pegaflow_b200.server import TensorRegistry, serve
+
+    engine = PegaEngine(1 << 20, pool_kind="host", dfs_root=str(tmp_path / "dfs"))
+    fake = np.zeros(2 * 16 * 4096, np.uint8)
+    server, _, port = serve(engine, "127.0.0.1:0",
+                            TensorRegistry(lambda d, w: (fake, fake.ctypes.data, fake.nbytes, d)))
+    client = EngineRpcClient(f"http://127.0.0.1:{port}", connect_timeout_s=5)
+    try:
+        client.register_context("inst", "ns", 0, 1, 0, 1, "L0", b"w", 16, 4096, 16 * 4096, 2)
+        r = client.query("inst", [b"a", b"b", b"c"])
+        assert (r["prefetch_state"], r["hit_blocks"], r["missing_blocks"]) == ("partial_miss", 0, 3)
+    finally:
+        client.close()
+        server.stop(0)
+        engine.close()
+
+
 def test_errors_become_grpc_status_codes(served):
     client, _, _ = served
     client.register_context("inst", "ns", 0, 1, 0, 2, "L0", b"wrapper", 16, 4096, 16 * 4096, 2)
