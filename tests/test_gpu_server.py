@@ -3,11 +3,7 @@
 CUDA IPC; the test drives it with EngineRpcClient and checks the restored
 bytes and the per-layer completion words."""
 
-import os
 import pickle
-import socket
-import subprocess
-import sys
 import time
 from pathlib import Path
 
@@ -19,40 +15,10 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parent.parent
 
 
-def _port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
 @pytest.fixture
-def server(cuda):
-    port = _port()
-    proc = subprocess.Popen([sys.executable, "-m", "pegaflow_b200.server", "--addr", f"127.0.0.1:{port}",
-                             "--pool-size", "512mb", "--disable-lfu-admission", "--log-level", "warning"],
-                            cwd=str(ROOT), stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
-                            env=dict(os.environ, PYTHONPATH=str(ROOT)))
-    from pegaflow_b200 import EngineRpcClient
-
-    client = None
-    deadline = time.time() + 120
-    while client is None:
-        try:
-            client = EngineRpcClient(f"http://127.0.0.1:{port}", connect_timeout_s=1.0)
-        except RuntimeError:
-            if proc.poll() is not None or time.time() > deadline:
-                out = proc.stdout.read().decode(errors="replace") if proc.stdout else ""
-                pytest.fail(f"server did not start: {out[-2000:]}")
-    yield client
-    try:
-        client.shutdown()
-    except RuntimeError:
-        pass
-    try:
-        proc.wait(timeout=30)
-    except subprocess.TimeoutExpired:
-        proc.kill()
-        proc.wait()
+def server(cuda, engine_server):
+    client, _ = engine_server()
+    return client
 
 
 def test_register_save_query_load_over_ipc(server, cuda):
