@@ -530,7 +530,8 @@ def config_block(args, wl) -> dict:
             "blocks_moved": wl["blocks"], "block_ids": args.order, "kv_dtype": "fp16" if wl.get("separate") else "bf16",
             "save_mode": args.save_mode, "load_mode": args.load_mode,
             "staging": {"slot_MiB": args.chunk_mib or 512, "slots": args.slots or 2,
-                        "first_chunk_MiB": args.first_chunk_mib or 64, "growth": "x2 per chunk"},
+                        "first_chunk_MiB": args.first_chunk_mib or 64, "growth": "x2 per chunk",
+                        "save_first_chunk": "max(first chunk, half a slot)"},
             "l2": "inputs larger than L2 (payload >= 36 MiB per layer set; KV cache >> 126 MB)",
             "parallelism": f"dp{args.gpus} (independent ranks, weak scaling)"}
 

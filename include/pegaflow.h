@@ -97,10 +97,11 @@ typedef struct pf_executor_config {
   uint32_t copy_streams;        /* 0 = default (2) */
   uint32_t cache_streaming;     /* 1 = evict-first loads/stores in the kernels */
   uint32_t reserved0;
-  /* Size limit of the first staged chunk of a call; each later chunk may be
-   * twice the previous one, up to staging_chunk_bytes. Small first chunks
-   * start the DMA (and raise the first per-layer flags) early; large later
-   * chunks keep the kernel launch count low. 0 = default (64 MiB). */
+  /* Size limit of the first staged chunk of a load; each later chunk may be
+   * twice the previous one, up to staging_chunk_bytes. A small first chunk
+   * raises the first per-layer flags early; large later chunks keep the
+   * kernel launch count low. Saves start at the larger of this and half a
+   * slot. 0 = default (64 MiB). */
   uint64_t first_chunk_bytes;
 } pf_executor_config;
 

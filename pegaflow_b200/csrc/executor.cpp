@@ -697,11 +697,11 @@ void Executor::issue_serial(const Built& b, cudaStream_t s, int64_t* layer_done)
   }
 }
 
-void Executor::make_chunks(const Built& b, std::vector<Chunk>* chunks) {
+void Executor::make_chunks(const Built& b, uint64_t first_limit, std::vector<Chunk>* chunks) {
   chunks->clear();
   if (b.total_tiles == 0) return;
   // Walk units in order; a chunk is a tile range whose dense span fits the
-  // current limit. The limit starts at first_chunk_ and doubles with each
+  // current limit. The limit starts at first_limit and doubles with each
   // chunk up to the slot size: the first copy-engine transfer (and, for a
   // load, the first layer's completion) starts after a small kernel, while
   // the bulk moves in few launches. Every launch pays a fixed latency of tens
@@ -711,7 +711,7 @@ void Executor::make_chunks(const Built& b, std::vector<Chunk>* chunks) {
   // 16-byte-aligned dense address aligned, even when the chunk starts inside
   // a layer of unaligned units.
   uint64_t cur_tb = 0, cur_db = 0, last_end = 0;
-  uint64_t limit = first_chunk_;
+  uint64_t limit = std::min(slot_bytes_, std::max<uint64_t>(first_limit, 2 * kTileBytes));
   bool first = true;
   uint64_t dense = 0;
   for (const PlanLayer& p : b.layers) {
@@ -920,8 +920,11 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
     launch(kPack, false, args, 0, b.total_tiles, 0, kstream_);
     stats_.kernel_bytes += b.total_bytes;
   } else {
+    // A save has no per-layer consumer waiting on its first chunk: starting
+    // at half a slot only delays the first D2H by one larger pack (about
+    // 0.1 ms for 256 MiB) and saves kernel launches.
     std::vector<Chunk> chunks;
-    make_chunks(b, &chunks);
+    make_chunks(b, std::max(first_chunk_, slot_bytes_ / 2), &chunks);
     for (size_t k = 0; k < chunks.size(); ++k) {
       const uint32_t si = static_cast<uint32_t>(k % slots_);
       uint8_t* slot = staging_ + static_cast<uint64_t>(si) * slot_bytes_;
@@ -996,8 +999,10 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     launch(kUnpack, true, args, 0, b.total_tiles, 0, kstream_);
     stats_.kernel_bytes += b.total_bytes;
   } else {
+    // Small first chunk: the first layers of a layer-wise restore are ready
+    // after one small DMA.
     std::vector<Chunk> chunks;
-    make_chunks(b, &chunks);
+    make_chunks(b, first_chunk_, &chunks);
     for (size_t k = 0; k < chunks.size(); ++k) {
       const uint32_t si = static_cast<uint32_t>(k % slots_);
       uint8_t* slot = staging_ + static_cast<uint64_t>(si) * slot_bytes_;

@@ -98,7 +98,8 @@ class Executor {
   void build_load(const pf_load_layer* layers, uint64_t n, bool staged, Built* b);
   void build_p2p(const pf_p2p_layer* layers, uint64_t n, int peer, bool push, Built* b);
   void enable_peer(int peer);
-  void make_chunks(const Built& b, std::vector<Chunk>* chunks);
+  // Chunks of at most `first` bytes, doubling per chunk up to the slot size.
+  void make_chunks(const Built& b, uint64_t first, std::vector<Chunk>* chunks);
   CopyArgs upload(const Built& b, bool with_counters, cudaStream_t s);
   void launch(Dir dir, bool table, const CopyArgs& args, uint64_t tile_begin,
               uint64_t tile_end, int64_t shift, cudaStream_t s);
