@@ -86,8 +86,7 @@ void DeviceWorker::process(LoadTask& task) {
   bool ok = true;
   uint64_t bytes = 0;
   // A LoadState with a per-layer extension covering every requested layer
-  // gets its words raised by the kernels as layers land: its page is pinned
-  // and mapped for the device for the duration of the task.
+  // gets its words raised as layers land (load_with_layer_words).
   pf_load_state* ls = nullptr;
   try {
     ls = load_state_attach(task.shm);
@@ -95,19 +94,8 @@ void DeviceWorker::process(LoadTask& task) {
     fprintf(stderr, "pegaflow_b200: failed to attach LoadState %s: %s\n", task.shm.c_str(), e.what());
   }
   int64_t* words = nullptr;
-  void* pinned_base = nullptr;
   if (ls && load_state_layers(ls) >= task.layers.size() && !task.layers.empty()) {
-    size_t len = 0;
-    void* base = load_state_base(ls, &len);
-    const size_t page = 4096;
-    len = (len + page - 1) / page * page;
-    if (cudaHostRegister(base, len, cudaHostRegisterPortable | cudaHostRegisterMapped) == cudaSuccess) {
-      pinned_register(base, len);
-      pinned_base = base;
-      words = load_state_layer_words(ls);
-    } else {
-      cudaGetLastError();  // per-layer words are then raised together at the end
-    }
+    words = load_state_layer_words(ls);
   }
   try {
     std::vector<pf_load_layer> layers;
@@ -130,24 +118,19 @@ void DeviceWorker::process(LoadTask& task) {
       layers.push_back(pl);
       bytes += load_geometry(L.reg).unit_bytes * load_geometry(L.reg).units * L.ids.size();
     }
-    exec_->load_sync(layers.data(), layers.size(), words);
+    if (words) {
+      load_with_layer_words(layers.data(), layers.size(), words);
+    } else {
+      exec_->load_sync(layers.data(), layers.size(), nullptr);
+    }
   } catch (const std::exception& e) {
     ok = false;
     fprintf(stderr, "pegaflow_b200: load task failed: %s\n", e.what());
-  }
-  if (pinned_base) {
-    pinned_unregister(pinned_base);
-    if (cudaHostUnregister(pinned_base) != cudaSuccess) cudaGetLastError();
   }
   if (!ls) {
     counters_->load_failures.fetch_add(1);
   } else {
     if (ok) {
-      const uint32_t n = load_state_layers(ls);
-      if (n >= task.layers.size() && !words) {
-        int64_t* w = load_state_layer_words(ls);
-        for (size_t l = 0; l < task.layers.size(); ++l) reinterpret_cast<volatile int64_t*>(w)[l] = 1;
-      }
       load_state_set(ls, PF_LOAD_STATE_SUCCESS);
     } else {
       counters_->load_failures.fetch_add(1);
@@ -160,6 +143,48 @@ void DeviceWorker::process(LoadTask& task) {
     counters_->load_calls.fetch_add(1);
     std::lock_guard<std::mutex> g(counters_->ms_mu);
     counters_->load_ms += ms_since(t0);
+  }
+}
+
+void DeviceWorker::load_with_layer_words(const pf_load_layer* layers, size_t n, int64_t* words) {
+  // Registering the LoadState page with CUDA for every task would cost a
+  // driver round trip on each side of every load (and unregistering can stall
+  // other work), so the kernels raise flags in one mapped pinned array this
+  // worker keeps, and this thread copies each newly raised flag into the
+  // LoadState while the load runs.
+  const size_t need = n * sizeof(int64_t);
+  if (!flags_mem_ || flags_mem_->size() < need) {
+    flags_mem_.reset();
+    flags_mem_ = std::make_unique<PinnedMemory>(std::max<size_t>(need, 4096 * sizeof(int64_t)),
+                                                PinKind::kCudaHostAlloc, /*write_combined=*/false);
+  }
+  volatile int64_t* flags = reinterpret_cast<volatile int64_t*>(flags_mem_->data());
+  for (size_t l = 0; l < n; ++l) flags[l] = 0;
+  cudaStream_t s = exec_->own_stream();
+  exec_->load(layers, n, s, const_cast<int64_t*>(flags));
+  std::vector<char> copied(n, 0);
+  size_t left = n;
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(s);
+    for (size_t l = 0; l < n && left; ++l) {
+      if (!copied[l] && flags[l] == 1) {
+        // The kernel fenced at system scope before raising the flag, so the
+        // layer's bytes are visible to whoever sees the word.
+        __atomic_store_n(&words[l], int64_t{1}, __ATOMIC_RELEASE);
+        copied[l] = 1;
+        --left;
+      }
+    }
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) {
+      cudaGetLastError();
+      cuda_check(q, "load stream");
+    }
+    std::this_thread::yield();
+  }
+  // Every layer is in place once the stream is done.
+  for (size_t l = 0; l < n; ++l) {
+    if (!copied[l]) __atomic_store_n(&words[l], int64_t{1}, __ATOMIC_RELEASE);
   }
 }
 

@@ -67,7 +67,13 @@ class DeviceWorker {
  private:
   void load_loop();
   void process(LoadTask& task);
+  // Loads `layers`, raising `words[l]` (a LoadState's per-layer words) as
+  // layer l lands: the kernels raise flags in this worker's own mapped
+  // pinned array, and this thread copies each new one into `words` while the
+  // load runs. The LoadState page itself is never registered with CUDA.
+  void load_with_layer_words(const pf_load_layer* layers, size_t n, int64_t* words);
   std::unique_ptr<Executor> exec_;
+  std::unique_ptr<PinnedMemory> flags_mem_;  // per-layer flags the kernels raise (grown on demand)
   EngineCounters* counters_;
   std::mutex mu_;
   std::condition_variable cv_, idle_cv_;
