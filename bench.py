@@ -430,8 +430,13 @@ def run_fp8_evict(args) -> None:
     kv = [torch.randint(0, 256, (2, nb, 16, 8, 128), generator=g, device="cuda:0", dtype=torch.uint8)
           for _ in range(layers)]
     sc = [torch.rand((nb,), generator=g, device="cuda:0", dtype=torch.float32) for _ in range(layers)]
-    names = [f"model.layers.{i}.attn" for i in range(layers)] + [f"model.layers.{i}.attn.scale" for i in range(layers)]
-    tensors = kv + sc
+    # Forward order, each layer's KV next to its scales: a load restores its
+    # layers in the order the request lists them, so layer i is usable once
+    # entries 2i and 2i+1 are in place.
+    names, tensors = [], []
+    for i in range(layers):
+        names += [f"model.layers.{i}.attn", f"model.layers.{i}.attn.scale"]
+        tensors += [kv[i], sc[i]]
     pool = args.fp8_pool_gb << 30
     per_block = layers * (2 * 16 * 8 * 128 + 4)
 
@@ -475,7 +480,7 @@ def run_fp8_evict(args) -> None:
             state.set_completed()
         for li in range(layers):
             if hit and overlap:
-                if not (state.wait_layer(li, 60) and state.wait_layer(layers + li, 60)):
+                if not (state.wait_layer(2 * li, 60) and state.wait_layer(2 * li + 1, 60)):
                     raise RuntimeError("layer load failed")
             elif hit and li == 0:
                 wait_ready(state)
