@@ -82,8 +82,6 @@ class _WrapperUnpickler(pickle.Unpickler):
             obj = getattr(torch, name, None)
             if name == "Size" or isinstance(obj, torch.dtype):
                 return obj
-        if module == "torch._utils" and name == "_rebuild_device_tensor_from_numpy":
-            pass
         raise pickle.UnpicklingError(f"wrapper bytes may not reference {module}.{name}")
 
 

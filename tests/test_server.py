@@ -193,3 +193,15 @@ def test_wrapper_unpickling_refuses_other_globals():
         loads_wrapper(evil)
     with pytest.raises(pickle.UnpicklingError, match="not a CudaIPCWrapper"):
         loads_wrapper(pickle.dumps({"a": 1}))
+    # A call smuggled in as a reduce of an allowed-looking name is refused too.
+    with pytest.raises(pickle.UnpicklingError, match="may not reference os.system"):
+        loads_wrapper(b"cos\nsystem\n(S'true'\ntR.")
+    # Old pickle protocols rebuild objects through copyreg, which is not allowed.
+    import torch
+
+    from pegaflow_b200.ipc import CudaIPCWrapper
+
+    w = CudaIPCWrapper.__new__(CudaIPCWrapper)
+    w.handle, w.dtype, w.shape, w.device_uuid = (0,), torch.float16, torch.Size([1]), "GPU-x"
+    with pytest.raises(pickle.UnpicklingError, match="_reconstructor"):
+        loads_wrapper(pickle.dumps(w, protocol=0))
