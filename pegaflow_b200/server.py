@@ -27,6 +27,7 @@ from . import proto as P
 log = logging.getLogger("pegaflow_b200.server")
 
 DEFAULT_ADDR = "127.0.0.1:50055"
+DRAIN_TIMEOUT_S = 60.0  # how long teardown waits for copies that use mapped tensors
 
 
 def parse_memory_size(s: str) -> int:
@@ -76,6 +77,15 @@ class TensorRegistry:
             ctx["tensors"][layer_name] = keep
         return data_ptr, size_bytes, device
 
+    def devices_of(self, instance_id: str) -> set:
+        prefix = f"{instance_id}:"
+        with self._lock:
+            return {c["device"] for k, c in self._contexts.items() if k.startswith(prefix)}
+
+    def all_devices(self) -> set:
+        with self._lock:
+            return {c["device"] for c in self._contexts.values()}
+
     def drop_instance(self, instance_id: str) -> int:
         prefix = f"{instance_id}:"
         with self._lock:
@@ -109,6 +119,35 @@ class EngineService:
         self.engine = engine
         self.registry = registry or TensorRegistry()
         self.on_shutdown = on_shutdown
+        self._busy: dict[str, int] = {}  # instance -> Save/Load RPCs running
+        self._busy_cv = threading.Condition()
+
+    def _tracked(self, instance_id: str, context, fn, *args):
+        """An engine call that reads or writes the instance's mapped tensors."""
+        with self._busy_cv:
+            self._busy[instance_id] = self._busy.get(instance_id, 0) + 1
+        try:
+            return self._engine_call(context, fn, *args)
+        finally:
+            with self._busy_cv:
+                self._busy[instance_id] -= 1
+                if not self._busy[instance_id]:
+                    del self._busy[instance_id]
+                self._busy_cv.notify_all()
+
+    def _drain(self, instance_id: Optional[str], devices) -> None:
+        """Wait for running Save/Load RPCs (of one instance, or all) and for
+        the loads queued on `devices`, so the tensors can be unmapped."""
+        with self._busy_cv:
+            done = self._busy_cv.wait_for(
+                lambda: (instance_id not in self._busy) if instance_id else not self._busy, timeout=DRAIN_TIMEOUT_S)
+        if not done:
+            log.warning("RPCs still running after %.0f s; unmapping anyway", DRAIN_TIMEOUT_S)
+        for d in sorted(devices):
+            try:
+                self.engine.wait_loads(d, DRAIN_TIMEOUT_S)
+            except Exception as e:
+                log.warning("loads on device %d did not finish: %s", d, e)
 
     @staticmethod
     def _ok():
@@ -136,13 +175,14 @@ class EngineService:
 
     def Save(self, req, context):
         saves = [(s.layer_name, list(s.block_ids), list(s.block_hashes)) for s in req.saves]
-        self._engine_call(context, self.engine.batch_save_kv_blocks, req.instance_id, req.tp_rank, req.device_id,
-                          saves)
+        self._tracked(req.instance_id, context, self.engine.batch_save_kv_blocks, req.instance_id, req.tp_rank,
+                      req.device_id, saves)
         return P.SaveResponse(status=self._ok())
 
     def Load(self, req, context):
-        self._engine_call(context, self.engine.batch_load_kv_blocks, req.instance_id, req.tp_rank, req.device_id,
-                          req.load_state_shm, list(req.layer_names), list(req.block_ids), list(req.block_hashes))
+        self._tracked(req.instance_id, context, self.engine.batch_load_kv_blocks, req.instance_id, req.tp_rank,
+                      req.device_id, req.load_state_shm, list(req.layer_names), list(req.block_ids),
+                      list(req.block_hashes))
         return P.LoadResponse(status=self._ok())
 
     def Query(self, req, context):
@@ -155,13 +195,28 @@ class EngineService:
                                loading_blocks=q["loading_blocks"], missing_blocks=q["missing_blocks"])
 
     def UnregisterContext(self, req, context):
+        # The reference drops the mapped KV tensors first (service.rs:340-353).
+        # Here the engine forgets the instance first, so no new copy starts.
+        # Then RPCs already running for it and loads queued on its devices
+        # finish, and only then are the tensors unmapped: a copy never touches
+        # a closed mapping. The engine's error, if any, is still returned.
+        from ._native import PegaError
+
+        err = None
+        try:
+            self.engine.unregister_instance(req.instance_id)
+        except PegaError as e:
+            err = e
+        self._drain(req.instance_id, self.registry.devices_of(req.instance_id))
         dropped = self.registry.drop_instance(req.instance_id)
         if dropped:
             log.info("Dropped %d CUDA tensors for instance %s", dropped, req.instance_id)
-        self._engine_call(context, self.engine.unregister_instance, req.instance_id)
+        if err is not None:
+            context.abort(_status_code(err), str(err))
         return P.UnregisterResponse(status=self._ok())
 
     def Shutdown(self, req, context):
+        self._drain(None, self.registry.all_devices())
         self.registry.clear()
         log.warning("Shutdown requested via RPC")
         if self.on_shutdown:

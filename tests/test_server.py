@@ -111,6 +111,60 @@ def test_query_reports_packed_file_tier_states(native, tmp_path):
         engine.close()
 
 
+def test_unregister_unmaps_tensors_only_after_copies_that_use_them():
+    """A Save RPC still copying from an instance's KV tensors, and loads
+    queued on its devices, finish before UnregisterContext unmaps them."""
+    import threading
+    import time
+
+    from pegaflow_b200.server import EngineService, TensorRegistry
+
+    events, in_save, release = [], threading.Event(), threading.Event()
+
+    class Engine:
+        def register_context_layer(self, *a):
+            events.append("register")
+
+        def batch_save_kv_blocks(self, *a):
+            in_save.set()
+            release.wait(10)
+            events.append("save done")
+
+        def unregister_instance(self, instance_id):
+            events.append("unregister")
+
+        def wait_loads(self, device_id, timeout_s):
+            events.append(f"wait_loads {device_id}")
+
+    class Registry(TensorRegistry):
+        def drop_instance(self, instance_id):
+            events.append("drop")
+            return super().drop_instance(instance_id)
+
+    svc = EngineService(Engine(), Registry(lambda d, w: (object(), 0x1000, 4096, d)))
+
+    def abort(code, msg):
+        raise RuntimeError(msg)
+
+    ctx = types.SimpleNamespace(abort=abort)
+    svc.RegisterContext(types.SimpleNamespace(instance_id="i", tp_rank=0, device_id=3, layer_name="L0",
+                                              wrapper_bytes=b"w", namespace="ns", num_blocks=1,
+                                              bytes_per_block=4096, kv_stride_bytes=0, segments=1, tp_size=1,
+                                              num_layers=1), ctx)
+    save = threading.Thread(target=svc.Save,
+                            args=(types.SimpleNamespace(instance_id="i", tp_rank=0, device_id=3, saves=[]), ctx))
+    save.start()
+    assert in_save.wait(5)
+    unreg = threading.Thread(target=svc.UnregisterContext, args=(types.SimpleNamespace(instance_id="i"), ctx))
+    unreg.start()
+    time.sleep(0.2)
+    assert "drop" not in events  # waiting for the save that reads the tensors
+    release.set()
+    save.join(5)
+    unreg.join(5)
+    assert events == ["register", "unregister", "save done", "wait_loads 3", "drop"]
+
+
 def test_errors_become_grpc_status_codes(served):
     client, _, _ = served
     client.register_context("inst", "ns", 0, 1, 0, 2, "L0", b"wrapper", 16, 4096, 16 * 4096, 2)
