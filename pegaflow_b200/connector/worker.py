@@ -65,9 +65,11 @@ class WorkerSide:
     # ------------------------------------------------------------------ lifecycle
 
     def shutdown(self) -> None:
-        self.unregister_context()
+        # Saves already queued go out before the instance is unregistered (the
+        # reference unregisters first, worker.py:60-63, and those saves fail).
         self._save_q.put(None)
         self._save_thread.join()
+        self.unregister_context()
 
     def unregister_context(self) -> None:
         if not self._layers:

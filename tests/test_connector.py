@@ -185,6 +185,33 @@ def test_load_rpc_matches_reference():
     assert [h.hex() for h in args[6]] == want["block_hashes"]
 
 
+def test_shutdown_sends_queued_saves_before_unregistering():
+    import threading
+
+    from pegaflow_b200.connector import WorkerSide
+
+    release, entered = threading.Event(), threading.Event()
+
+    class SlowSaves(Recorder):
+        def save(self, *a):
+            entered.set()
+            release.wait(10)
+            return super().save(*a)
+
+    rec = SlowSaves()
+    w = WorkerSide(ctx(rec, num_layers=1), wrapper_factory=lambda t: b"w")
+    w._layers = ["L0"]  # registered
+    meta = _meta({"r1": {"block_ids": [1, 2], "block_hashes": ["aa", "bb"]}})
+    w.save_kv_layer(meta, "L0", None, types.SimpleNamespace(block_table=object()))
+    assert entered.wait(10)  # the save is in flight
+    stopper = threading.Thread(target=w.shutdown)
+    stopper.start()
+    stopper.join(0.2)  # shutdown must wait for it, not unregister meanwhile
+    release.set()
+    stopper.join(10)
+    assert [name for name, _ in rec.calls] == ["save", "unregister_context"]
+
+
 def test_scheduler_flow_async_and_layerwise():
     from pegaflow_b200.connector import SchedulerSide
 
