@@ -517,7 +517,7 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
     }
     const auto t_plan = Clock::now();
     Executor& ex = worker->executor();
-    ex.save(layers.data(), layers.size(), ex.own_stream());
+    ex.save(layers.data(), layers.size(), ex.save_stream());
 
     // LayerBlocks (lib.rs:687-698, 755-763) are built while the copy runs,
     // one batch per entry sharing its pool allocations; their slots are
@@ -545,7 +545,7 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
       built[k] = std::move(batch);
       if (k > 0 && same_hashes) same_hashes = p.hashes == planned[0].hashes || *p.hashes == *planned[0].hashes;
     }
-    cuda_check(cudaStreamSynchronize(ex.own_stream()), "cudaStreamSynchronize(save)");
+    cuda_check(cudaStreamSynchronize(ex.save_stream()), "cudaStreamSynchronize(save)");
     const auto t_xfer = Clock::now();
 
     // insert_slot (lib.rs:700-705, 765-770): entry by entry, or in one

@@ -188,28 +188,56 @@ Executor::Executor(int device, const pf_executor_config& cfg) : device_(device),
   first_chunk_ = std::min(slot_bytes_, std::max<uint64_t>(cfg_.first_chunk_bytes, 2 * kTileBytes));
 
   cuda_check(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
-  cuda_check(cudaStreamCreateWithFlags(&kstream_, cudaStreamNonBlocking), "cudaStreamCreate");
-  cstreams_.resize(cfg_.copy_streams);
-  ev_copy_done_.resize(cfg_.copy_streams);
+  cuda_check(cudaStreamCreateWithFlags(&save_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  init_lane(save_lane_);
+  init_lane(load_lane_);
+}
+
+void Executor::init_lane(Lane& l) {
+  cuda_check(cudaStreamCreateWithFlags(&l.kstream, cudaStreamNonBlocking), "cudaStreamCreate");
+  l.cstreams.resize(cfg_.copy_streams);
+  l.ev_copy_done.resize(cfg_.copy_streams);
   for (uint32_t i = 0; i < cfg_.copy_streams; ++i) {
-    cuda_check(cudaStreamCreateWithFlags(&cstreams_[i], cudaStreamNonBlocking), "cudaStreamCreate");
-    cuda_check(cudaEventCreateWithFlags(&ev_copy_done_[i], cudaEventDisableTiming), "cudaEventCreate");
+    cuda_check(cudaStreamCreateWithFlags(&l.cstreams[i], cudaStreamNonBlocking), "cudaStreamCreate");
+    cuda_check(cudaEventCreateWithFlags(&l.ev_copy_done[i], cudaEventDisableTiming), "cudaEventCreate");
   }
-  ev_filled_.resize(slots_);
-  ev_drained_.resize(slots_);
+  l.ev_filled.resize(slots_);
+  l.ev_drained.resize(slots_);
   for (uint32_t i = 0; i < slots_; ++i) {
-    cuda_check(cudaEventCreateWithFlags(&ev_filled_[i], cudaEventDisableTiming), "cudaEventCreate");
-    cuda_check(cudaEventCreateWithFlags(&ev_drained_[i], cudaEventDisableTiming), "cudaEventCreate");
+    cuda_check(cudaEventCreateWithFlags(&l.ev_filled[i], cudaEventDisableTiming), "cudaEventCreate");
+    cuda_check(cudaEventCreateWithFlags(&l.ev_drained[i], cudaEventDisableTiming), "cudaEventCreate");
   }
-  cuda_check(cudaEventCreateWithFlags(&ev_start_, cudaEventDisableTiming), "cudaEventCreate");
-  cuda_check(cudaEventCreateWithFlags(&ev_plan_, cudaEventDisableTiming), "cudaEventCreate");
-  cuda_check(cudaEventCreateWithFlags(&ev_done_, cudaEventDisableTiming), "cudaEventCreate");
-  cuda_check(cudaMalloc(reinterpret_cast<void**>(&staging_), slot_bytes_ * slots_), "cudaMalloc(staging)");
+  cuda_check(cudaEventCreateWithFlags(&l.ev_start, cudaEventDisableTiming), "cudaEventCreate");
+  cuda_check(cudaEventCreateWithFlags(&l.ev_plan, cudaEventDisableTiming), "cudaEventCreate");
+  cuda_check(cudaEventCreateWithFlags(&l.ev_done, cudaEventDisableTiming), "cudaEventCreate");
   // Nothing is in flight yet: record the "previous call finished" events once.
-  cuda_check(cudaEventRecord(ev_done_, kstream_), "cudaEventRecord");
+  cuda_check(cudaEventRecord(l.ev_done, l.kstream), "cudaEventRecord");
   for (uint32_t i = 0; i < cfg_.copy_streams; ++i) {
-    cuda_check(cudaEventRecord(ev_copy_done_[i], cstreams_[i]), "cudaEventRecord");
+    cuda_check(cudaEventRecord(l.ev_copy_done[i], l.cstreams[i]), "cudaEventRecord");
   }
+}
+
+uint8_t* Executor::lane_staging(Lane& l) {
+  // Allocated on first use: a lane that only moves zero-copy transfers never
+  // needs it, and a save-only caller holds one lane's worth.
+  if (!l.staging) {
+    cuda_check(cudaMalloc(reinterpret_cast<void**>(&l.staging), slot_bytes_ * slots_), "cudaMalloc(staging)");
+  }
+  return l.staging;
+}
+
+void Executor::destroy_lane(Lane& l) {
+  for (auto e : l.ev_filled) cudaEventDestroy(e);
+  for (auto e : l.ev_drained) cudaEventDestroy(e);
+  for (auto e : l.ev_copy_done) cudaEventDestroy(e);
+  if (l.ev_start) cudaEventDestroy(l.ev_start);
+  if (l.ev_plan) cudaEventDestroy(l.ev_plan);
+  if (l.ev_done) cudaEventDestroy(l.ev_done);
+  for (auto s : l.cstreams) cudaStreamDestroy(s);
+  if (l.kstream) cudaStreamDestroy(l.kstream);
+  cudaFree(l.staging);
+  cudaFree(l.d_plan);
+  if (l.h_plan) cudaFreeHost(l.h_plan);
 }
 
 Executor::~Executor() {
@@ -220,18 +248,10 @@ Executor::~Executor() {
     cudaEventDestroy(p.second);
   }
   for (auto e : event_pool_) cudaEventDestroy(e);
-  for (auto e : ev_filled_) cudaEventDestroy(e);
-  for (auto e : ev_drained_) cudaEventDestroy(e);
-  for (auto e : ev_copy_done_) cudaEventDestroy(e);
-  cudaEventDestroy(ev_start_);
-  cudaEventDestroy(ev_plan_);
-  cudaEventDestroy(ev_done_);
-  for (auto s : cstreams_) cudaStreamDestroy(s);
-  cudaStreamDestroy(kstream_);
+  destroy_lane(save_lane_);
+  destroy_lane(load_lane_);
   cudaStreamDestroy(own_stream_);
-  cudaFree(staging_);
-  cudaFree(d_plan_);
-  if (h_plan_) cudaFreeHost(h_plan_);
+  cudaStreamDestroy(save_stream_);
   cudaGetLastError();
 }
 
@@ -648,12 +668,13 @@ void Executor::p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool
   Built b;
   build_p2p(layers, n_layers, peer, push, &b);
   if (b.total_tiles == 0) return;
-  cuda_check(cudaEventRecord(ev_start_, caller), "cudaEventRecord");
-  cuda_check(cudaStreamWaitEvent(kstream_, ev_start_, 0), "cudaStreamWaitEvent");
-  const CopyArgs args = upload(b, false, kstream_);
-  launch(push ? kPack : kUnpack, true, args, 0, b.total_tiles, 0, kstream_);
-  cuda_check(cudaEventRecord(ev_done_, kstream_), "cudaEventRecord");
-  cuda_check(cudaStreamWaitEvent(caller, ev_done_, 0), "cudaStreamWaitEvent");
+  Lane& L = load_lane_;
+  cuda_check(cudaEventRecord(L.ev_start, caller), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_start, 0), "cudaStreamWaitEvent");
+  const CopyArgs args = upload(L, b, false);
+  launch(push ? kPack : kUnpack, true, args, 0, b.total_tiles, 0, L.kstream);
+  cuda_check(cudaEventRecord(L.ev_done, L.kstream), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(caller, L.ev_done, 0), "cudaStreamWaitEvent");
   stats_.kernel_bytes += b.total_bytes;  // local HBM side; the other side crosses NVLink
   stats_.bytes_p2p += b.total_bytes;
 }
@@ -747,7 +768,10 @@ void Executor::make_chunks(const Built& b, uint64_t first_limit, std::vector<Chu
   chunks->push_back({cur_tb, b.total_tiles, cur_db, last_end});
 }
 
-CopyArgs Executor::upload(const Built& b, bool with_counters, cudaStream_t s) {
+CopyArgs Executor::upload(Lane& l, const Built& b, bool with_counters) {
+  // The plan is copied on the lane's kernel stream, after the lane's
+  // previous kernels (which read the previous plan) and before its own.
+  const cudaStream_t s = l.kstream;
   auto a16 = [](size_t v) { return (v + 15) & ~size_t(15); };
   const size_t sz_layers = a16(b.layers.size() * sizeof(PlanLayer));
   const size_t sz_ids = a16(b.ids.size() * sizeof(uint32_t));
@@ -757,25 +781,25 @@ CopyArgs Executor::upload(const Built& b, bool with_counters, cudaStream_t s) {
   const size_t total = sz_layers + sz_ids + sz_base + sz_ptrs + sz_cnt;
 
   // The pinned staging of the previous plan may still be in flight.
-  if (plan_pending_) cuda_check(cudaEventSynchronize(ev_plan_), "cudaEventSynchronize(plan)");
-  if (total > h_plan_cap_) {
-    if (h_plan_) cudaFreeHost(h_plan_);
-    h_plan_ = nullptr;
-    h_plan_cap_ = 0;
+  if (l.plan_pending) cuda_check(cudaEventSynchronize(l.ev_plan), "cudaEventSynchronize(plan)");
+  if (total > l.h_plan_cap) {
+    if (l.h_plan) cudaFreeHost(l.h_plan);
+    l.h_plan = nullptr;
+    l.h_plan_cap = 0;
     const size_t cap = std::max<size_t>(total * 2, 1 << 16);
-    cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&h_plan_), cap, cudaHostAllocDefault), "cudaHostAlloc(plan)");
-    h_plan_cap_ = cap;
+    cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&l.h_plan), cap, cudaHostAllocDefault), "cudaHostAlloc(plan)");
+    l.h_plan_cap = cap;
   }
-  if (total > d_plan_cap_) {
-    cuda_check(cudaStreamSynchronize(kstream_), "cudaStreamSynchronize");
-    if (d_plan_) cudaFree(d_plan_);
-    d_plan_ = nullptr;
-    d_plan_cap_ = 0;
+  if (total > l.d_plan_cap) {
+    cuda_check(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    if (l.d_plan) cudaFree(l.d_plan);
+    l.d_plan = nullptr;
+    l.d_plan_cap = 0;
     const size_t cap = std::max<size_t>(total * 2, 1 << 16);
-    cuda_check(cudaMalloc(reinterpret_cast<void**>(&d_plan_), cap), "cudaMalloc(plan)");
-    d_plan_cap_ = cap;
+    cuda_check(cudaMalloc(reinterpret_cast<void**>(&l.d_plan), cap), "cudaMalloc(plan)");
+    l.d_plan_cap = cap;
   }
-  uint8_t* h = h_plan_;
+  uint8_t* h = l.h_plan;
   size_t off = 0;
   std::memcpy(h + off, b.layers.data(), b.layers.size() * sizeof(PlanLayer));
   off += sz_layers;
@@ -786,21 +810,22 @@ CopyArgs Executor::upload(const Built& b, bool with_counters, cudaStream_t s) {
   if (!b.side_ptrs.empty()) std::memcpy(h + off, b.side_ptrs.data(), b.side_ptrs.size() * sizeof(uint64_t));
   off += sz_ptrs;
   if (sz_cnt) std::memset(h + off, 0, sz_cnt);
-  cuda_check(cudaMemcpyAsync(d_plan_, h_plan_, total, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync(plan)");
-  cuda_check(cudaEventRecord(ev_plan_, s), "cudaEventRecord(plan)");
-  plan_pending_ = true;
+  cuda_check(cudaMemcpyAsync(l.d_plan, l.h_plan, total, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync(plan)");
+  cuda_check(cudaEventRecord(l.ev_plan, s), "cudaEventRecord(plan)");
+  l.plan_pending = true;
 
+  uint8_t* d = l.d_plan;
   CopyArgs a{};
   off = 0;
-  a.layers = reinterpret_cast<const PlanLayer*>(d_plan_ + off);
+  a.layers = reinterpret_cast<const PlanLayer*>(d + off);
   off += sz_layers;
-  a.ids = reinterpret_cast<const uint32_t*>(d_plan_ + off);
+  a.ids = reinterpret_cast<const uint32_t*>(d + off);
   off += sz_ids;
-  a.side_base = reinterpret_cast<const uint64_t*>(d_plan_ + off);
+  a.side_base = reinterpret_cast<const uint64_t*>(d + off);
   off += sz_base;
-  a.side_ptrs = reinterpret_cast<const uint64_t*>(d_plan_ + off);
+  a.side_ptrs = reinterpret_cast<const uint64_t*>(d + off);
   off += sz_ptrs;
-  a.layer_tiles_done = sz_cnt ? reinterpret_cast<unsigned long long*>(d_plan_ + off) : nullptr;
+  a.layer_tiles_done = sz_cnt ? reinterpret_cast<unsigned long long*>(d + off) : nullptr;
   a.n_layers = static_cast<uint32_t>(b.layers.size());
   return a;
 }
@@ -907,17 +932,19 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
       }
     }
   }
-  // Order after the caller's work and after this executor's previous call.
-  cuda_check(cudaEventRecord(ev_start_, caller), "cudaEventRecord");
-  cuda_check(cudaStreamWaitEvent(kstream_, ev_start_, 0), "cudaStreamWaitEvent");
-  for (auto e : ev_copy_done_) cuda_check(cudaStreamWaitEvent(kstream_, e, 0), "cudaStreamWaitEvent");
-  for (auto cs : cstreams_) {
-    cuda_check(cudaStreamWaitEvent(cs, ev_start_, 0), "cudaStreamWaitEvent");
-    cuda_check(cudaStreamWaitEvent(cs, ev_done_, 0), "cudaStreamWaitEvent");
+  // Order after the caller's work and after the save lane's previous call.
+  Lane& L = save_lane_;
+  cuda_check(cudaEventRecord(L.ev_start, caller), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_start, 0), "cudaStreamWaitEvent");
+  for (auto e : L.ev_copy_done) cuda_check(cudaStreamWaitEvent(L.kstream, e, 0), "cudaStreamWaitEvent");
+  for (auto cs : L.cstreams) {
+    cuda_check(cudaStreamWaitEvent(cs, L.ev_start, 0), "cudaStreamWaitEvent");
+    cuda_check(cudaStreamWaitEvent(cs, L.ev_done, 0), "cudaStreamWaitEvent");
   }
-  const CopyArgs args = upload(b, false, kstream_);
+  uint8_t* staging = staged ? lane_staging(L) : nullptr;
+  const CopyArgs args = upload(L, b, false);
   if (!staged) {
-    launch(kPack, false, args, 0, b.total_tiles, 0, kstream_);
+    launch(kPack, false, args, 0, b.total_tiles, 0, L.kstream);
     stats_.kernel_bytes += b.total_bytes;
   } else {
     // A save has no per-layer consumer waiting on its first chunk: starting
@@ -927,24 +954,24 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
     make_chunks(b, std::max(first_chunk_, slot_bytes_ / 2), &chunks);
     for (size_t k = 0; k < chunks.size(); ++k) {
       const uint32_t si = static_cast<uint32_t>(k % slots_);
-      uint8_t* slot = staging_ + static_cast<uint64_t>(si) * slot_bytes_;
-      if (k >= slots_) cuda_check(cudaStreamWaitEvent(kstream_, ev_drained_[si], 0), "cudaStreamWaitEvent");
+      uint8_t* slot = staging + static_cast<uint64_t>(si) * slot_bytes_;
+      if (k >= slots_) cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_drained[si], 0), "cudaStreamWaitEvent");
       const int64_t shift = static_cast<int64_t>(reinterpret_cast<uint64_t>(slot)) -
                             static_cast<int64_t>(chunks[k].dense_begin);
-      launch(kPack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, kstream_);
-      cuda_check(cudaEventRecord(ev_filled_[si], kstream_), "cudaEventRecord");
-      cudaStream_t cs = cstreams_[k % cstreams_.size()];
-      cuda_check(cudaStreamWaitEvent(cs, ev_filled_[si], 0), "cudaStreamWaitEvent");
+      launch(kPack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, L.kstream);
+      cuda_check(cudaEventRecord(L.ev_filled[si], L.kstream), "cudaEventRecord");
+      cudaStream_t cs = L.cstreams[k % L.cstreams.size()];
+      cuda_check(cudaStreamWaitEvent(cs, L.ev_filled[si], 0), "cudaStreamWaitEvent");
       copy_runs(b, chunks[k], slot, true, cs);
-      cuda_check(cudaEventRecord(ev_drained_[si], cs), "cudaEventRecord");
+      cuda_check(cudaEventRecord(L.ev_drained[si], cs), "cudaEventRecord");
     }
     stats_.kernel_bytes += 2 * b.total_bytes;
   }
-  cuda_check(cudaEventRecord(ev_done_, kstream_), "cudaEventRecord");
-  cuda_check(cudaStreamWaitEvent(caller, ev_done_, 0), "cudaStreamWaitEvent");
-  for (size_t j = 0; j < cstreams_.size(); ++j) {
-    cuda_check(cudaEventRecord(ev_copy_done_[j], cstreams_[j]), "cudaEventRecord");
-    cuda_check(cudaStreamWaitEvent(caller, ev_copy_done_[j], 0), "cudaStreamWaitEvent");
+  cuda_check(cudaEventRecord(L.ev_done, L.kstream), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(caller, L.ev_done, 0), "cudaStreamWaitEvent");
+  for (size_t j = 0; j < L.cstreams.size(); ++j) {
+    cuda_check(cudaEventRecord(L.ev_copy_done[j], L.cstreams[j]), "cudaEventRecord");
+    cuda_check(cudaStreamWaitEvent(caller, L.ev_copy_done[j], 0), "cudaStreamWaitEvent");
   }
   stats_.bytes_saved += b.total_bytes;
 }
@@ -976,16 +1003,18 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
       }
     }
   }
-  cuda_check(cudaEventRecord(ev_start_, caller), "cudaEventRecord");
-  cuda_check(cudaStreamWaitEvent(kstream_, ev_start_, 0), "cudaStreamWaitEvent");
-  for (auto e : ev_copy_done_) cuda_check(cudaStreamWaitEvent(kstream_, e, 0), "cudaStreamWaitEvent");
-  for (auto cs : cstreams_) {
-    cuda_check(cudaStreamWaitEvent(cs, ev_start_, 0), "cudaStreamWaitEvent");
-    cuda_check(cudaStreamWaitEvent(cs, ev_done_, 0), "cudaStreamWaitEvent");
+  Lane& L = load_lane_;
+  cuda_check(cudaEventRecord(L.ev_start, caller), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_start, 0), "cudaStreamWaitEvent");
+  for (auto e : L.ev_copy_done) cuda_check(cudaStreamWaitEvent(L.kstream, e, 0), "cudaStreamWaitEvent");
+  for (auto cs : L.cstreams) {
+    cuda_check(cudaStreamWaitEvent(cs, L.ev_start, 0), "cudaStreamWaitEvent");
+    cuda_check(cudaStreamWaitEvent(cs, L.ev_done, 0), "cudaStreamWaitEvent");
   }
+  uint8_t* staging = (staged && b.total_tiles > 0) ? lane_staging(L) : nullptr;
   CopyArgs args{};
   if (b.total_tiles > 0) {
-    args = upload(b, layer_done != nullptr, kstream_);
+    args = upload(L, b, layer_done != nullptr);
     if (layer_done) {
       // The kernel writes through the device view of the pinned words.
       void* dev = nullptr;
@@ -996,7 +1025,7 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
   if (b.total_tiles == 0) {
     // only ordered copies below
   } else if (!staged) {
-    launch(kUnpack, true, args, 0, b.total_tiles, 0, kstream_);
+    launch(kUnpack, true, args, 0, b.total_tiles, 0, L.kstream);
     stats_.kernel_bytes += b.total_bytes;
   } else {
     // Small first chunk: the first layers of a layer-wise restore are ready
@@ -1005,24 +1034,24 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     make_chunks(b, first_chunk_, &chunks);
     for (size_t k = 0; k < chunks.size(); ++k) {
       const uint32_t si = static_cast<uint32_t>(k % slots_);
-      uint8_t* slot = staging_ + static_cast<uint64_t>(si) * slot_bytes_;
-      cudaStream_t cs = cstreams_[k % cstreams_.size()];
-      if (k >= slots_) cuda_check(cudaStreamWaitEvent(cs, ev_drained_[si], 0), "cudaStreamWaitEvent");
+      uint8_t* slot = staging + static_cast<uint64_t>(si) * slot_bytes_;
+      cudaStream_t cs = L.cstreams[k % L.cstreams.size()];
+      if (k >= slots_) cuda_check(cudaStreamWaitEvent(cs, L.ev_drained[si], 0), "cudaStreamWaitEvent");
       copy_runs(b, chunks[k], slot, false, cs);
-      cuda_check(cudaEventRecord(ev_filled_[si], cs), "cudaEventRecord");
-      cuda_check(cudaStreamWaitEvent(kstream_, ev_filled_[si], 0), "cudaStreamWaitEvent");
+      cuda_check(cudaEventRecord(L.ev_filled[si], cs), "cudaEventRecord");
+      cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_filled[si], 0), "cudaStreamWaitEvent");
       const int64_t shift = static_cast<int64_t>(reinterpret_cast<uint64_t>(slot)) -
                             static_cast<int64_t>(chunks[k].dense_begin);
-      launch(kUnpack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, kstream_);
-      cuda_check(cudaEventRecord(ev_drained_[si], kstream_), "cudaEventRecord");
+      launch(kUnpack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, L.kstream);
+      cuda_check(cudaEventRecord(L.ev_drained[si], L.kstream), "cudaEventRecord");
     }
     stats_.kernel_bytes += 2 * b.total_bytes;
   }
-  issue_serial(b, kstream_, layer_done);
-  cuda_check(cudaEventRecord(ev_done_, kstream_), "cudaEventRecord");
-  cuda_check(cudaStreamWaitEvent(caller, ev_done_, 0), "cudaStreamWaitEvent");
-  for (size_t j = 0; j < cstreams_.size(); ++j) {
-    cuda_check(cudaEventRecord(ev_copy_done_[j], cstreams_[j]), "cudaEventRecord");
+  issue_serial(b, L.kstream, layer_done);
+  cuda_check(cudaEventRecord(L.ev_done, L.kstream), "cudaEventRecord");
+  cuda_check(cudaStreamWaitEvent(caller, L.ev_done, 0), "cudaStreamWaitEvent");
+  for (size_t j = 0; j < L.cstreams.size(); ++j) {
+    cuda_check(cudaEventRecord(L.ev_copy_done[j], L.cstreams[j]), "cudaEventRecord");
   }
   stats_.bytes_loaded += b.total_bytes;
   for (const SerialLoad& sl : b.serial) {
@@ -1031,8 +1060,8 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
 }
 
 void Executor::save_sync(const pf_save_layer* layers, uint64_t n_layers) {
-  save(layers, n_layers, own_stream_);
-  cuda_check(cudaStreamSynchronize(own_stream_), "cudaStreamSynchronize(save)");
+  save(layers, n_layers, save_stream_);
+  cuda_check(cudaStreamSynchronize(save_stream_), "cudaStreamSynchronize(save)");
 }
 
 void Executor::load_sync(const pf_load_layer* layers, uint64_t n_layers, int64_t* layer_done) {

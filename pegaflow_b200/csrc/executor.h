@@ -47,8 +47,10 @@ class Executor {
   Executor& operator=(const Executor&) = delete;
 
   int device() const { return device_; }
-  // The executor's private stream (used by the blocking wrappers).
+  // The executor's private streams, used by the blocking wrappers: one for
+  // loads and peer copies, one for saves, so the two can overlap.
   cudaStream_t own_stream() const { return own_stream_; }
+  cudaStream_t save_stream() const { return save_stream_; }
 
   // Enqueue a save/load ordered after `caller`; `caller` waits for completion.
   void save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t caller);
@@ -100,7 +102,28 @@ class Executor {
   void enable_peer(int peer);
   // Chunks of at most `first` bytes, doubling per chunk up to the slot size.
   void make_chunks(const Built& b, uint64_t first, std::vector<Chunk>* chunks);
-  CopyArgs upload(const Built& b, bool with_counters, cudaStream_t s);
+
+  // One transfer pipeline: its kernel stream, copy streams, staging slots,
+  // plan buffers and events. Saves run on the save lane, loads and peer
+  // copies on the load lane, so a save and a load on one GPU proceed at the
+  // same time (the host link is full duplex, and each direction has its own
+  // copy engine). Calls on one lane run in order.
+  struct Lane {
+    cudaStream_t kstream = nullptr;
+    std::vector<cudaStream_t> cstreams;
+    std::vector<cudaEvent_t> ev_filled, ev_drained, ev_copy_done;
+    cudaEvent_t ev_start = nullptr, ev_plan = nullptr, ev_done = nullptr;
+    uint8_t* staging = nullptr;  // allocated on the lane's first staged call
+    uint8_t* d_plan = nullptr;
+    size_t d_plan_cap = 0;
+    uint8_t* h_plan = nullptr;
+    size_t h_plan_cap = 0;
+    bool plan_pending = false;
+  };
+  void init_lane(Lane& l);
+  void destroy_lane(Lane& l);
+  uint8_t* lane_staging(Lane& l);
+  CopyArgs upload(Lane& l, const Built& b, bool with_counters);
   void launch(Dir dir, bool table, const CopyArgs& args, uint64_t tile_begin,
               uint64_t tile_end, int64_t shift, cudaStream_t s);
   int grid_for(uint64_t tiles) const;
@@ -111,21 +134,12 @@ class Executor {
   int device_;
   pf_executor_config cfg_;
   int num_sms_ = 148;
-  cudaStream_t own_stream_ = nullptr;   // for the blocking wrappers
-  cudaStream_t kstream_ = nullptr;      // pack/unpack kernels
-  std::vector<cudaStream_t> cstreams_;  // copy-engine DMA
-  uint8_t* staging_ = nullptr;
+  cudaStream_t own_stream_ = nullptr;   // blocking loads and peer copies
+  cudaStream_t save_stream_ = nullptr;  // blocking saves
   uint64_t slot_bytes_ = 0;
-  uint64_t first_chunk_ = 0;  // limit of a call's first chunk; doubles per chunk up to slot_bytes_
+  uint64_t first_chunk_ = 0;  // limit of a load's first chunk; doubles per chunk up to slot_bytes_
   uint32_t slots_ = 0;
-  std::vector<cudaEvent_t> ev_filled_, ev_drained_;
-  cudaEvent_t ev_start_ = nullptr, ev_plan_ = nullptr, ev_done_ = nullptr;
-  std::vector<cudaEvent_t> ev_copy_done_;
-  uint8_t* d_plan_ = nullptr;
-  size_t d_plan_cap_ = 0;
-  uint8_t* h_plan_ = nullptr;
-  size_t h_plan_cap_ = 0;
-  bool plan_pending_ = false;
+  Lane save_lane_, load_lane_;
 
   std::mutex mu_;
   std::vector<int> peers_enabled_;
