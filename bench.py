@@ -530,6 +530,139 @@ def run_fp8_evict(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_duplex(args) -> None:
+    """Save and load at once on one GPU (a prefill saving its KV while another
+    request's prefix is restored). Llama-3.1-8B shape (32 layers of KV-first
+    [2, 8192, 16, 8, 128] bf16); one seeded permutation gives 640 block ids to
+    save and 640 other ids to restore into, so the two transfers touch
+    disjoint blocks. Executor: the save on one stream and the load on another
+    (the executor's save and load lanes), against the same two back to back on
+    one stream. Engine: a queued batch_load_kv_blocks of the previous step's
+    hashes while batch_save_kv_blocks stores this step's."""
+    import torch
+
+    from pegaflow_b200 import Executor, Layout, PegaEngine, PinnedBuffer, PyLoadState
+
+    torch.cuda.set_device(0)
+    wl = dict(WORKLOADS["llama8b"])
+    if args.layers:
+        wl["layers"] = args.layers
+    nb, n = wl["num_blocks"], wl["blocks"]
+    gen = torch.Generator(device="cuda:0").manual_seed(1000)
+    tensors = [torch.randn((2, nb, 16, 8, 128), generator=gen, device="cuda:0", dtype=torch.float32)
+               .to(torch.bfloat16) for _ in range(wl["layers"])]
+    perm = np.random.default_rng(5).permutation(nb)
+    save_ids, load_ids = perm[:n].astype(np.int64), perm[n:2 * n].astype(np.int64)
+    payload = payload_bytes(tensors, n)
+    link = link_peaks(torch, 0)
+    pool = PinnedBuffer(2 * payload + (4 << 20), write_combined=True)
+    saves, _, off = executor_specs(tensors, save_ids, save_ids, pool.ptr)
+    _, loads, _ = executor_specs(tensors, load_ids, load_ids, pool.ptr + off)
+    ex = Executor(0, save_mode=args.save_mode, load_mode=args.load_mode, staging_chunk_bytes=args.chunk_mib << 20,
+                  staging_slots=args.slots, copy_streams=args.copy_streams, first_chunk_bytes=args.first_chunk_mib << 20)
+    a, b = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def timed(duplex):
+        e0, e1, eb = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(a)
+        if duplex:
+            b.wait_event(e0)
+            ex.save(saves, stream=a.cuda_stream)
+            ex.load(loads, stream=b.cuda_stream)
+            eb.record(b)
+            a.wait_event(eb)
+        else:
+            ex.save(saves, stream=a.cuda_stream)
+            ex.load(loads, stream=a.cuda_stream)
+        e1.record(a)
+        return e0, e1
+
+    for _ in range(args.warmup):
+        timed(True)
+        timed(False)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    res = {}
+    for mode in ("serial", "duplex"):
+        evs = [timed(mode == "duplex") for _ in range(args.steps)]
+        torch.cuda.synchronize()
+        ms = [x.elapsed_time(y) for x, y in evs]
+        res[mode] = {"ms_per_step": round(statistics.median(ms), 3),
+                     "GBps": round(2 * payload / (statistics.median(ms) / 1e3) / 1e9, 2)}
+    clocks = sampler.stop()
+
+    # Engine: this step's save runs while the previous step's blocks load.
+    eng = PegaEngine(3 * payload + (512 << 20), enable_lfu_admission=False,
+                     executor=dict(save_mode=args.save_mode, load_mode=args.load_mode,
+                                   staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
+                                   copy_streams=args.copy_streams, first_chunk_bytes=args.first_chunk_mib << 20))
+    names = [f"model.layers.{i}.self_attn" for i in range(len(tensors))]
+    for nm, t in zip(names, tensors):
+        lay = Layout.from_tensor(t)
+        eng.register_context_layer("dup", "bench", 0, nm, lay.data_ptr, lay.size_bytes, lay.num_blocks,
+                                   lay.bytes_per_block, lay.kv_stride_bytes, lay.segments, 0, 1, len(names))
+    sl, ll = save_ids.tolist(), load_ids.tolist()
+
+    def hashes(k):
+        return [f"dup-s{k}-b{i}".encode() for i in range(n)]
+
+    def wait(state):
+        deadline = time.perf_counter() + 120.0
+        while not state.is_ready():
+            if time.perf_counter() > deadline:
+                raise TimeoutError("engine load did not complete within 120 s")
+        if state.get_state() != 1:
+            raise RuntimeError("engine load failed")
+
+    def e2e_step(k, duplex):
+        t0 = time.perf_counter()
+        s = PyLoadState(len(names))
+        if duplex:
+            eng.batch_load_kv_blocks("dup", 0, 0, s.shm_name(), names, ll, hashes(k - 1))
+            eng.batch_save_kv_blocks("dup", 0, 0, [(nm, sl, hashes(k)) for nm in names])
+            wait(s)
+        else:
+            eng.batch_save_kv_blocks("dup", 0, 0, [(nm, sl, hashes(k)) for nm in names])
+            eng.batch_load_kv_blocks("dup", 0, 0, s.shm_name(), names, ll, hashes(k - 1))
+            wait(s)
+        s.close()
+        return time.perf_counter() - t0
+
+    eng.batch_save_kv_blocks("dup", 0, 0, [(nm, sl, hashes(0)) for nm in names])
+    k = 1
+    e2e = {}
+    for mode in ("serial", "duplex"):
+        for _ in range(args.warmup):
+            e2e_step(k, mode == "duplex")
+            k += 1
+        times = []
+        for _ in range(args.steps):
+            times.append(e2e_step(k, mode == "duplex"))
+            k += 1
+        e2e[mode] = {"ms_per_step": round(statistics.median(times) * 1e3, 3),
+                     "GBps": round(2 * payload * len(times) / sum(times) / 1e9, 2)}
+    m = eng.metrics()
+    eng.close()
+    line = {
+        "metric": METRIC, "value": res["duplex"]["GBps"], "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": res["duplex"]["ms_per_step"], "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded ~N(0,1) bf16 KV)",
+        "config": {"workload": "llama8b_duplex", "layers": wl["layers"], "num_blocks": nb, "blocks_saved": n,
+                   "blocks_loaded": n, "block_ids": "one seeded permutation, disjoint save and load ids",
+                   "l2": "inputs larger than L2"},
+        "executor": res, "duplex_speedup": round(res["serial"]["ms_per_step"] / res["duplex"]["ms_per_step"], 3),
+        "e2e": {"value": e2e["duplex"]["GBps"], "unit": "GB/s", "h2d_bytes_per_step": payload,
+                "d2h_bytes_per_step": payload, "serial": e2e["serial"], "duplex": e2e["duplex"],
+                "api": "batch_load_kv_blocks (queued) + batch_save_kv_blocks, then LoadState"},
+        "host_link": {"peak_h2d_GBps": link["h2d"], "peak_d2h_GBps": link["d2h"],
+                      "duplex_frac_of_sum": round(res["duplex"]["GBps"] / (link["h2d"] + link["d2h"]), 3)},
+        "engine": {k2: m[k2] for k2 in ("load_failures", "cache_block_evictions", "pool_alloc_failures")},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def config_block(args, wl) -> dict:
     return {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
             "blocks_moved": wl["blocks"], "block_ids": args.order, "kv_dtype": "fp16" if wl.get("separate") else "bf16",
@@ -550,7 +683,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["qwen3_pd", "llama8b_fp8_evict"], default="llama8b")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["qwen3_pd", "llama8b_fp8_evict", "llama8b_duplex"],
+                    default="llama8b")
     ap.add_argument("--fp8-requests", type=int, default=64)
     ap.add_argument("--fp8-pool-gb", type=int, default=30)
     ap.add_argument("--fp8-compute-ms", type=float, default=0.5)
@@ -585,6 +719,14 @@ def main() -> int:
                               "unavailable": "engine-level scenario; the reference engine cannot be built here"}))
             return 0
         run_fp8_evict(args)
+        return 0
+    if args.workload == "llama8b_duplex":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": "llama8b_duplex",
+                              "unavailable": "engine-level scenario; the reference engine cannot be built here"}))
+            return 0
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_duplex(args)
         return 0
     wl = dict(WORKLOADS[args.workload])
     if args.layers:

@@ -345,3 +345,48 @@ def test_stream_ordered_save_and_stats(cuda):
     assert st["kernel_ms"] > 0 and st["bytes_saved"] == 200 * 65536
     ref = t[0, :200].contiguous().view(torch.uint8).cpu().numpy().reshape(-1)
     np.testing.assert_array_equal(pool.numpy()[: ref.size], ref)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_save_and_load_run_at_once_on_two_streams(cuda, oracle, mode):
+    """A save and a load issued back to back on two caller streams go to the
+    executor's two lanes and overlap. They touch disjoint blocks of one KV
+    cache; each moves exactly its own bytes, over several staging chunks per
+    lane. A second save, ordered after the load by an event on the caller
+    side, sees the restored blocks."""
+    torch = cuda
+    from pegaflow_b200 import Executor, Layout, LoadSpec, PinnedBuffer, SaveSpec
+
+    bpb, n = 32768, 96
+    cache = kv(torch, (2, 256, 16, 8, 128), torch.bfloat16, 11)
+    lay = Layout.from_tensor(cache)
+    perm = torch.randperm(256, generator=torch.Generator().manual_seed(13)).numpy()
+    save_ids, load_ids = perm[:n], perm[n:2 * n]
+    pool = PinnedBuffer(3 * 2 * n * bpb)
+    view = pool.numpy()
+    # Region 1 receives the save; region 2 holds seeded blocks to restore.
+    region2 = pool.ptr + 2 * n * bpb
+    blocks = np.random.default_rng(14).integers(0, 256, 2 * n * bpb, dtype=np.uint8)
+    view[2 * n * bpb:4 * n * bpb] = blocks
+    ks = np.array([region2 + i * bpb for i in range(n)], np.uint64)
+    vs = ks + n * bpb
+    want_save = oracle.np_save_layer(olayout(oracle, lay), host_bytes(cache), save_ids)
+    want_load = host_bytes(cache)
+    oracle.load_layer(olayout(oracle, lay), want_load, load_ids, [int(x) for x in ks], [int(x) for x in vs])
+
+    ex = Executor(0, save_mode=mode, load_mode=mode, staging_chunk_bytes=1 << 20, staging_slots=2,
+                  first_chunk_bytes=256 << 10)
+    s_save, s_load = torch.cuda.Stream(), torch.cuda.Stream()
+    ex.save([SaveSpec(lay, save_ids, pool.ptr, pool.ptr + n * bpb)], stream=s_save.cuda_stream)
+    ex.load([LoadSpec(lay, load_ids, ks, vs)], stream=s_load.cuda_stream)
+    loaded = torch.cuda.Event()
+    loaded.record(s_load)
+    s_save.wait_event(loaded)
+    region3 = pool.ptr + 4 * n * bpb
+    ex.save([SaveSpec(lay, load_ids, region3, region3 + n * bpb)], stream=s_save.cuda_stream)
+    torch.cuda.synchronize()
+
+    np.testing.assert_array_equal(view[:n * bpb], want_save[0])
+    np.testing.assert_array_equal(view[n * bpb:2 * n * bpb], want_save[1])
+    np.testing.assert_array_equal(host_bytes(cache), want_load)
+    np.testing.assert_array_equal(view[4 * n * bpb:6 * n * bpb], blocks)
