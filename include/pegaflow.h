@@ -89,8 +89,10 @@ typedef enum pf_transfer_mode {
 } pf_transfer_mode;
 
 typedef struct pf_executor_config {
+  /* Saves and loads each have their own staging slots (allocated on first
+   * use), so a save and a load on two streams run at the same time. */
   uint64_t staging_chunk_bytes; /* slot size, 0 = default (512 MiB) */
-  uint32_t staging_slots;       /* 0 = default (2) */
+  uint32_t staging_slots;       /* slots per direction, 0 = default (2) */
   uint32_t save_mode;           /* pf_transfer_mode */
   uint32_t load_mode;           /* pf_transfer_mode */
   uint32_t ctas_per_sm;         /* 0 = default */
