@@ -616,20 +616,22 @@ def run_duplex(args) -> None:
             raise RuntimeError("engine load failed")
 
     def e2e_step(k, duplex):
+        new, old = hashes(k), hashes(k - 1)  # one list per request, shared by its layers
         t0 = time.perf_counter()
         s = PyLoadState(len(names))
         if duplex:
-            eng.batch_load_kv_blocks("dup", 0, 0, s.shm_name(), names, ll, hashes(k - 1))
-            eng.batch_save_kv_blocks("dup", 0, 0, [(nm, sl, hashes(k)) for nm in names])
+            eng.batch_load_kv_blocks("dup", 0, 0, s.shm_name(), names, ll, old)
+            eng.batch_save_kv_blocks("dup", 0, 0, [(nm, sl, new) for nm in names])
             wait(s)
         else:
-            eng.batch_save_kv_blocks("dup", 0, 0, [(nm, sl, hashes(k)) for nm in names])
-            eng.batch_load_kv_blocks("dup", 0, 0, s.shm_name(), names, ll, hashes(k - 1))
+            eng.batch_save_kv_blocks("dup", 0, 0, [(nm, sl, new) for nm in names])
+            eng.batch_load_kv_blocks("dup", 0, 0, s.shm_name(), names, ll, old)
             wait(s)
         s.close()
         return time.perf_counter() - t0
 
-    eng.batch_save_kv_blocks("dup", 0, 0, [(nm, sl, hashes(0)) for nm in names])
+    first = hashes(0)
+    eng.batch_save_kv_blocks("dup", 0, 0, [(nm, sl, first) for nm in names])
     k = 1
     e2e = {}
     for mode in ("serial", "duplex"):
@@ -657,7 +659,10 @@ def run_duplex(args) -> None:
                 "api": "batch_load_kv_blocks (queued) + batch_save_kv_blocks, then LoadState"},
         "host_link": {"peak_h2d_GBps": link["h2d"], "peak_d2h_GBps": link["d2h"],
                       "duplex_frac_of_sum": round(res["duplex"]["GBps"] / (link["h2d"] + link["d2h"]), 3)},
-        "engine": {k2: m[k2] for k2 in ("load_failures", "cache_block_evictions", "pool_alloc_failures")},
+        "engine": {k2: (round(m[k2], 2) if isinstance(m[k2], float) else m[k2])
+                   for k2 in ("load_failures", "cache_block_evictions", "pool_alloc_failures", "save_plan_ms",
+                              "save_transfer_ms", "save_insert_ms", "save_ms", "load_ms")},
+        "engine_calls": {"saves": 1 + 2 * (args.warmup + args.steps), "loads": 2 * (args.warmup + args.steps)},
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

@@ -226,3 +226,30 @@ def test_lru_eviction_makes_room(cuda, oracle):
     assert e.metrics()["cache_block_evictions"] >= 16
     with pytest.raises(RuntimeError, match="pinned pool exhausted"):
         e.save_kv_blocks("i", 0, 0, "L", list(range(64)), hashes_for("big", 64))
+
+
+def test_save_while_a_load_runs(cuda, oracle):
+    """A save issued while a queued load is still moving (the save on the
+    calling thread, the load on the device's load thread, on separate lanes)
+    gives the same pool and cache bytes as the two run one after the other.
+    The load's destination blocks and the save's source blocks are disjoint."""
+    torch = cuda
+    from pegaflow_b200 import PyLoadState
+
+    p = Pair(torch, oracle)
+    names = [f"model.layers.{i}.self_attn" for i in range(4)]
+    for i, n in enumerate(names):
+        p.register(n, kv(torch, (2, 1024, 16, 8, 128), torch.bfloat16, 50 + i), num_layers=4)
+    perm = np.random.default_rng(7).permutation(1024)
+    a_src, load_dst, b_src = perm[:300].tolist(), perm[300:600].tolist(), perm[600:900].tolist()
+    ha, hb = hashes_for("dup-a", 300), hashes_for("dup-b", 300)
+    p.save([(n, a_src, ha) for n in names])
+    s = PyLoadState(len(names))
+    p.e.batch_load_kv_blocks("inst", 0, 0, s.shm_name(), names, load_dst, ha)
+    p.e.batch_save_kv_blocks("inst", 0, 0, [(n, b_src, hb) for n in names])
+    assert wait_state(s) == 1
+    assert p.m.batch_load("inst", 0, 0, names, load_dst, ha) == (1, None)
+    p.m.batch_save("inst", 0, 0, [(n, b_src, hb) for n in names])
+    assert p.e.count_prefix_hit_blocks("inst", hb) == 300
+    p.check_slots(hb[:50] + hb[-50:], range(4))
+    p.check_caches()
