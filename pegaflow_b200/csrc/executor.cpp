@@ -118,12 +118,17 @@ void check_plan_ends(const std::vector<uint32_t>& ids, const std::vector<uint64_
   plan_offset(units);
 }
 
-// Adds the calling thread's time in a save/load/p2p call to stats.host_ms
-// (constructed after the executor lock, so it is destroyed while held).
+// Adds the calling thread's time in a save/load/p2p call to stats.host_ms,
+// under the stats mutex, when the call returns or throws.
 struct HostTimer {
   double* acc;
+  std::mutex* mu;
   std::chrono::steady_clock::time_point t0 = std::chrono::steady_clock::now();
-  ~HostTimer() { *acc += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count(); }
+  ~HostTimer() {
+    const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    std::lock_guard<std::mutex> g(*mu);
+    *acc += ms;
+  }
 };
 
 // The copy of unit (b, u) must stay inside the registration. This is stricter
@@ -661,22 +666,22 @@ void Executor::enable_peer(int peer) {
 }
 
 void Executor::p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push, cudaStream_t caller) {
-  std::lock_guard<std::mutex> g(mu_);
-  HostTimer timer{&stats_.host_ms};
+  HostTimer timer{&stats_.host_ms, &stats_mu_};
   cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  Lane& L = load_lane_;
+  std::lock_guard<std::mutex> g(L.mu);
   enable_peer(peer);
   Built b;
   build_p2p(layers, n_layers, peer, push, &b);
   if (b.total_tiles == 0) return;
-  Lane& L = load_lane_;
   cuda_check(cudaEventRecord(L.ev_start, caller), "cudaEventRecord");
   cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_start, 0), "cudaStreamWaitEvent");
   const CopyArgs args = upload(L, b, false);
   launch(push ? kPack : kUnpack, true, args, 0, b.total_tiles, 0, L.kstream);
   cuda_check(cudaEventRecord(L.ev_done, L.kstream), "cudaEventRecord");
   cuda_check(cudaStreamWaitEvent(caller, L.ev_done, 0), "cudaStreamWaitEvent");
-  stats_.kernel_bytes += b.total_bytes;  // local HBM side; the other side crosses NVLink
-  stats_.bytes_p2p += b.total_bytes;
+  // kernel bytes: the local HBM side; the other side crosses NVLink
+  account(b.total_bytes, 0, 0, 0, b.total_bytes);
 }
 
 void Executor::p2p_sync(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push) {
@@ -688,10 +693,11 @@ namespace {
 void CUDART_CB raise_flag(void* p) { *static_cast<volatile int64_t*>(p) = 1; }
 }  // namespace
 
-void Executor::issue_serial(const Built& b, cudaStream_t s, int64_t* layer_done) {
+uint64_t Executor::issue_serial(const Built& b, cudaStream_t s, int64_t* layer_done) {
   // Copies in list order, merged into runs, exactly as batch_copy_segments_to_gpu
   // (transfer.rs:116-198): K list then V list for the split layout, one
   // block_size_bytes list otherwise.
+  uint64_t copies = 0;
   for (const SerialLoad& sl : b.serial) {
     const pf_layer_desc& l = sl.layer;
     const bool split = is_split_layout(l);
@@ -710,12 +716,13 @@ void Executor::issue_serial(const Built& b, cudaStream_t s, int64_t* layer_done)
         cuda_check(cudaMemcpyAsync(reinterpret_cast<void*>(l.data_ptr + g0), reinterpret_cast<void*>(host[i]),
                                    c * unit, cudaMemcpyHostToDevice, s),
                    "cudaMemcpyAsync H2D (ordered)");
-        stats_.copy_calls += 1;
+        copies += 1;
         i += c;
       }
     }
     if (layer_done) cuda_check(cudaLaunchHostFunc(s, raise_flag, layer_done + sl.done_index), "cudaLaunchHostFunc");
   }
+  return copies;
 }
 
 void Executor::make_chunks(const Built& b, uint64_t first_limit, std::vector<Chunk>* chunks) {
@@ -843,47 +850,47 @@ void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_
   a.tile_end = tile_end;
   a.side_shift = shift;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
-  if (timing_) {
-    auto take = [this]() {
-      if (!event_pool_.empty()) {
-        cudaEvent_t e = event_pool_.back();
-        event_pool_.pop_back();
+  {
+    std::lock_guard<std::mutex> g(stats_mu_);
+    stats_.kernel_launches += 1;
+    if (timing_) {
+      auto take = [this]() {
+        if (!event_pool_.empty()) {
+          cudaEvent_t e = event_pool_.back();
+          event_pool_.pop_back();
+          return e;
+        }
+        cudaEvent_t e;
+        cuda_check(cudaEventCreate(&e), "cudaEventCreate");
         return e;
-      }
-      cudaEvent_t e;
-      cuda_check(cudaEventCreate(&e), "cudaEventCreate");
-      return e;
-    };
-    e0 = take();
-    e1 = take();
-    cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
+      };
+      e0 = take();
+      e1 = take();
+    }
   }
+  if (e0) cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
   cuda_check(launch_copy(dir, table, a, grid_for(tile_end - tile_begin), s, cfg_.cache_streaming != 0),
              "kernel launch");
-  if (timing_) {
+  if (e1) {
     cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
+    std::lock_guard<std::mutex> g(stats_mu_);
     timed_.emplace_back(e0, e1);
     // A caller that times without reading stats must not grow this list
     // without bound: spans that have finished are folded in as we go.
-    if (timed_.size() >= 1024) fold_timings(false);
+    if (timed_.size() >= 1024) fold_finished_timings();
   }
-  stats_.kernel_launches += 1;
 }
 
-void Executor::fold_timings(bool wait) {
+void Executor::fold_finished_timings() {
   size_t k = 0;
   for (; k < timed_.size(); ++k) {
     const auto& p = timed_[k];
-    if (wait) {
-      cuda_check(cudaEventSynchronize(p.second), "cudaEventSynchronize");
-    } else {
-      const cudaError_t q = cudaEventQuery(p.second);
-      if (q == cudaErrorNotReady) {
-        cudaGetLastError();
-        break;
-      }
-      cuda_check(q, "cudaEventQuery");
+    const cudaError_t q = cudaEventQuery(p.second);
+    if (q == cudaErrorNotReady) {
+      cudaGetLastError();
+      break;
     }
+    cuda_check(q, "cudaEventQuery");
     float ms = 0.f;
     cuda_check(cudaEventElapsedTime(&ms, p.first, p.second), "cudaEventElapsedTime");
     stats_.kernel_ms += ms;
@@ -894,10 +901,20 @@ void Executor::fold_timings(bool wait) {
   timed_.erase(timed_.begin(), timed_.begin() + static_cast<std::ptrdiff_t>(k));
 }
 
-void Executor::copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h, cudaStream_t s) {
+void Executor::account(uint64_t kernel_bytes, uint64_t copies, uint64_t saved, uint64_t loaded, uint64_t p2p) {
+  std::lock_guard<std::mutex> g(stats_mu_);
+  stats_.kernel_bytes += kernel_bytes;
+  stats_.copy_calls += copies;
+  stats_.bytes_saved += saved;
+  stats_.bytes_loaded += loaded;
+  stats_.bytes_p2p += p2p;
+}
+
+uint64_t Executor::copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h, cudaStream_t s) {
   // First run ending after the chunk start.
   auto it = std::upper_bound(b.runs.begin(), b.runs.end(), c.dense_begin,
                              [](uint64_t v, const Run& r) { return v < r.dense + r.bytes; });
+  uint64_t copies = 0;
   for (; it != b.runs.end() && it->dense < c.dense_end; ++it) {
     const uint64_t lo = std::max(it->dense, c.dense_begin);
     const uint64_t hi = std::min(it->dense + it->bytes, c.dense_end);
@@ -909,8 +926,9 @@ void Executor::copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h
     } else {
       cuda_check(cudaMemcpyAsync(dev, host, hi - lo, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync H2D");
     }
-    stats_.copy_calls += 1;
+    copies += 1;
   }
+  return copies;
 }
 
 // ---------------------------------------------------------------------------
@@ -918,8 +936,7 @@ void Executor::copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h
 // ---------------------------------------------------------------------------
 
 void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t caller) {
-  std::lock_guard<std::mutex> g(mu_);
-  HostTimer timer{&stats_.host_ms};
+  HostTimer timer{&stats_.host_ms, &stats_mu_};
   cuda_check(cudaSetDevice(device_), "cudaSetDevice");
   const bool staged = cfg_.save_mode != PF_MODE_DIRECT;
   Built b;
@@ -934,6 +951,8 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
   }
   // Order after the caller's work and after the save lane's previous call.
   Lane& L = save_lane_;
+  std::lock_guard<std::mutex> g(L.mu);
+  uint64_t kernel_bytes = b.total_bytes, copies = 0;
   cuda_check(cudaEventRecord(L.ev_start, caller), "cudaEventRecord");
   cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_start, 0), "cudaStreamWaitEvent");
   for (auto e : L.ev_copy_done) cuda_check(cudaStreamWaitEvent(L.kstream, e, 0), "cudaStreamWaitEvent");
@@ -945,7 +964,6 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
   const CopyArgs args = upload(L, b, false);
   if (!staged) {
     launch(kPack, false, args, 0, b.total_tiles, 0, L.kstream);
-    stats_.kernel_bytes += b.total_bytes;
   } else {
     // A save has no per-layer consumer waiting on its first chunk: starting
     // at half a slot only delays the first D2H by one larger pack (about
@@ -962,10 +980,10 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
       cuda_check(cudaEventRecord(L.ev_filled[si], L.kstream), "cudaEventRecord");
       cudaStream_t cs = L.cstreams[k % L.cstreams.size()];
       cuda_check(cudaStreamWaitEvent(cs, L.ev_filled[si], 0), "cudaStreamWaitEvent");
-      copy_runs(b, chunks[k], slot, true, cs);
+      copies += copy_runs(b, chunks[k], slot, true, cs);
       cuda_check(cudaEventRecord(L.ev_drained[si], cs), "cudaEventRecord");
     }
-    stats_.kernel_bytes += 2 * b.total_bytes;
+    kernel_bytes = 2 * b.total_bytes;  // into the slot, then out of it
   }
   cuda_check(cudaEventRecord(L.ev_done, L.kstream), "cudaEventRecord");
   cuda_check(cudaStreamWaitEvent(caller, L.ev_done, 0), "cudaStreamWaitEvent");
@@ -973,12 +991,11 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
     cuda_check(cudaEventRecord(L.ev_copy_done[j], L.cstreams[j]), "cudaEventRecord");
     cuda_check(cudaStreamWaitEvent(caller, L.ev_copy_done[j], 0), "cudaStreamWaitEvent");
   }
-  stats_.bytes_saved += b.total_bytes;
+  account(kernel_bytes, copies, b.total_bytes, 0, 0);
 }
 
 void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t caller, int64_t* layer_done) {
-  std::lock_guard<std::mutex> g(mu_);
-  HostTimer timer{&stats_.host_ms};
+  HostTimer timer{&stats_.host_ms, &stats_mu_};
   cuda_check(cudaSetDevice(device_), "cudaSetDevice");
   const bool staged = cfg_.load_mode != PF_MODE_DIRECT;
   Built b;
@@ -1004,6 +1021,8 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     }
   }
   Lane& L = load_lane_;
+  std::lock_guard<std::mutex> g(L.mu);
+  uint64_t kernel_bytes = 0, copies = 0;
   cuda_check(cudaEventRecord(L.ev_start, caller), "cudaEventRecord");
   cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_start, 0), "cudaStreamWaitEvent");
   for (auto e : L.ev_copy_done) cuda_check(cudaStreamWaitEvent(L.kstream, e, 0), "cudaStreamWaitEvent");
@@ -1026,7 +1045,7 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     // only ordered copies below
   } else if (!staged) {
     launch(kUnpack, true, args, 0, b.total_tiles, 0, L.kstream);
-    stats_.kernel_bytes += b.total_bytes;
+    kernel_bytes = b.total_bytes;
   } else {
     // Small first chunk: the first layers of a layer-wise restore are ready
     // after one small DMA.
@@ -1037,7 +1056,7 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
       uint8_t* slot = staging + static_cast<uint64_t>(si) * slot_bytes_;
       cudaStream_t cs = L.cstreams[k % L.cstreams.size()];
       if (k >= slots_) cuda_check(cudaStreamWaitEvent(cs, L.ev_drained[si], 0), "cudaStreamWaitEvent");
-      copy_runs(b, chunks[k], slot, false, cs);
+      copies += copy_runs(b, chunks[k], slot, false, cs);
       cuda_check(cudaEventRecord(L.ev_filled[si], cs), "cudaEventRecord");
       cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_filled[si], 0), "cudaStreamWaitEvent");
       const int64_t shift = static_cast<int64_t>(reinterpret_cast<uint64_t>(slot)) -
@@ -1045,18 +1064,19 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
       launch(kUnpack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, L.kstream);
       cuda_check(cudaEventRecord(L.ev_drained[si], L.kstream), "cudaEventRecord");
     }
-    stats_.kernel_bytes += 2 * b.total_bytes;
+    kernel_bytes = 2 * b.total_bytes;  // into the slot, then out of it
   }
-  issue_serial(b, L.kstream, layer_done);
+  copies += issue_serial(b, L.kstream, layer_done);
   cuda_check(cudaEventRecord(L.ev_done, L.kstream), "cudaEventRecord");
   cuda_check(cudaStreamWaitEvent(caller, L.ev_done, 0), "cudaStreamWaitEvent");
   for (size_t j = 0; j < L.cstreams.size(); ++j) {
     cuda_check(cudaEventRecord(L.ev_copy_done[j], L.cstreams[j]), "cudaEventRecord");
   }
-  stats_.bytes_loaded += b.total_bytes;
+  uint64_t loaded = b.total_bytes;
   for (const SerialLoad& sl : b.serial) {
-    stats_.bytes_loaded += sl.ids.size() * load_geometry(sl.layer).unit_bytes * load_geometry(sl.layer).units;
+    loaded += sl.ids.size() * load_geometry(sl.layer).unit_bytes * load_geometry(sl.layer).units;
   }
+  account(kernel_bytes, copies, 0, loaded, 0);
 }
 
 void Executor::save_sync(const pf_save_layer* layers, uint64_t n_layers) {
@@ -1070,20 +1090,39 @@ void Executor::load_sync(const pf_load_layer* layers, uint64_t n_layers, int64_t
 }
 
 void Executor::stats(pf_executor_stats* out) {
-  std::lock_guard<std::mutex> g(mu_);
-  fold_timings(true);
+  // Wait for the spans issued so far without holding the mutex, so that
+  // calls on either lane keep launching meanwhile.
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
+  {
+    std::lock_guard<std::mutex> g(stats_mu_);
+    pending.swap(timed_);
+  }
+  double ms_sum = 0.0;
+  for (const auto& p : pending) {
+    cuda_check(cudaEventSynchronize(p.second), "cudaEventSynchronize");
+    float ms = 0.f;
+    cuda_check(cudaEventElapsedTime(&ms, p.first, p.second), "cudaEventElapsedTime");
+    ms_sum += ms;
+  }
+  std::lock_guard<std::mutex> g(stats_mu_);
+  stats_.kernel_ms += ms_sum;
+  stats_.timed_launches += pending.size();
+  for (const auto& p : pending) {
+    event_pool_.push_back(p.first);
+    event_pool_.push_back(p.second);
+  }
   *out = stats_;
 }
 
 void Executor::reset_stats() {
   pf_executor_stats tmp;
   stats(&tmp);
-  std::lock_guard<std::mutex> g(mu_);
+  std::lock_guard<std::mutex> g(stats_mu_);
   stats_ = pf_executor_stats{};
 }
 
 void Executor::set_timing(bool on) {
-  std::lock_guard<std::mutex> g(mu_);
+  std::lock_guard<std::mutex> g(stats_mu_);
   timing_ = on;
 }
 

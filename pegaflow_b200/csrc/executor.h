@@ -107,8 +107,11 @@ class Executor {
   // plan buffers and events. Saves run on the save lane, loads and peer
   // copies on the load lane, so a save and a load on one GPU proceed at the
   // same time (the host link is full duplex, and each direction has its own
-  // copy engine). Calls on one lane run in order.
+  // copy engine). Calls on one lane run in order; `mu` serialises them on
+  // the host, so a call on one lane never waits for the other lane's host
+  // work. Plans are built before the lane is taken.
   struct Lane {
+    std::mutex mu;
     cudaStream_t kstream = nullptr;
     std::vector<cudaStream_t> cstreams;
     std::vector<cudaEvent_t> ev_filled, ev_drained, ev_copy_done;
@@ -127,9 +130,12 @@ class Executor {
   void launch(Dir dir, bool table, const CopyArgs& args, uint64_t tile_begin,
               uint64_t tile_end, int64_t shift, cudaStream_t s);
   int grid_for(uint64_t tiles) const;
-  void copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h,
-                 cudaStream_t s);
-  void issue_serial(const Built& b, cudaStream_t s, int64_t* layer_done);
+  // Both return the number of copy-engine copies issued.
+  uint64_t copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h,
+                     cudaStream_t s);
+  uint64_t issue_serial(const Built& b, cudaStream_t s, int64_t* layer_done);
+  // Adds one call's counters to stats_.
+  void account(uint64_t kernel_bytes, uint64_t copies, uint64_t saved, uint64_t loaded, uint64_t p2p);
 
   int device_;
   pf_executor_config cfg_;
@@ -141,12 +147,14 @@ class Executor {
   uint32_t slots_ = 0;
   Lane save_lane_, load_lane_;
 
-  std::mutex mu_;
-  std::vector<int> peers_enabled_;
+  std::vector<int> peers_enabled_;  // touched only by peer copies, under load_lane_.mu
+
+  // Counters and kernel timing, shared by both lanes.
+  std::mutex stats_mu_;
   bool timing_ = false;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed_;  // pending kernel spans
-  // Adds finished spans of timed_ to stats_ (all of them, waiting, when wait).
-  void fold_timings(bool wait);
+  // Adds the finished spans at the front of timed_ to stats_ (stats_mu_ held).
+  void fold_finished_timings();
   std::vector<cudaEvent_t> event_pool_;
   pf_executor_stats stats_{};
 };

@@ -390,3 +390,59 @@ def test_save_and_load_run_at_once_on_two_streams(cuda, oracle, mode):
     np.testing.assert_array_equal(view[n * bpb:2 * n * bpb], want_save[1])
     np.testing.assert_array_equal(host_bytes(cache), want_load)
     np.testing.assert_array_equal(view[4 * n * bpb:6 * n * bpb], blocks)
+
+
+def test_saves_and_loads_from_two_threads(cuda, oracle):
+    """One executor driven by a saving thread and a loading thread at once
+    (each lane serialises its own calls; the counters are shared): every
+    transfer moves its own bytes, and the counters add up."""
+    import threading
+
+    torch = cuda
+    from pegaflow_b200 import Executor, Layout, LoadSpec, PinnedBuffer, SaveSpec
+
+    bpb, n, reps = 32768, 64, 12
+    cache = kv(torch, (2, 512, 16, 8, 128), torch.bfloat16, 21)
+    lay = Layout.from_tensor(cache)
+    perm = np.random.default_rng(22).permutation(512)
+    save_ids, load_ids = perm[:n], perm[n:2 * n]
+    pool = PinnedBuffer(2 * 2 * n * bpb)
+    view = pool.numpy()
+    src = pool.ptr + 2 * n * bpb
+    blocks = np.random.default_rng(23).integers(0, 256, 2 * n * bpb, dtype=np.uint8)
+    view[2 * n * bpb:] = blocks
+    ks = np.array([src + i * bpb for i in range(n)], np.uint64)
+    want_save = oracle.np_save_layer(olayout(oracle, lay), host_bytes(cache), save_ids)
+    want_load = host_bytes(cache)
+    oracle.load_layer(olayout(oracle, lay), want_load, load_ids, [int(x) for x in ks], [int(x) for x in ks + n * bpb])
+
+    ex = Executor(0, staging_chunk_bytes=1 << 20, staging_slots=2, first_chunk_bytes=128 << 10)
+    ex.set_timing(True)
+    ex.reset_stats()
+    errors = []
+
+    def run(fn):
+        try:
+            stream = torch.cuda.Stream()
+            for _ in range(reps):
+                fn(stream)
+            stream.synchronize()
+        except Exception as e:  # reported by the main thread
+            errors.append(e)
+
+    save = lambda s: ex.save([SaveSpec(lay, save_ids, pool.ptr, pool.ptr + n * bpb)], stream=s.cuda_stream)
+    load = lambda s: ex.load([LoadSpec(lay, load_ids, ks, ks + n * bpb)], stream=s.cuda_stream)
+    threads = [threading.Thread(target=run, args=(save,)), threading.Thread(target=run, args=(load,))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(120)
+    assert not errors and not any(t.is_alive() for t in threads)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(view[:n * bpb], want_save[0])
+    np.testing.assert_array_equal(view[n * bpb:2 * n * bpb], want_save[1])
+    np.testing.assert_array_equal(host_bytes(cache), want_load)
+    st = ex.stats()
+    assert st["bytes_saved"] == st["bytes_loaded"] == reps * 2 * n * bpb
+    assert st["timed_launches"] == st["kernel_launches"] > 2 * reps
+    assert st["kernel_bytes"] == 2 * 2 * reps * 2 * n * bpb
