@@ -141,8 +141,11 @@ def traffic_per_launch(kernel_bytes_per_launch: float) -> int:
     return round(payload * (TRAFFIC_READ_PER_BYTE + TRAFFIC_WRITE_PER_BYTE))
 
 
-def link_peaks(torch, device: int) -> dict:
-    """Pinned host<->device copy-engine bandwidth with 1 GiB buffers (best of 3)."""
+def link_peaks(torch, device: int, barrier=None) -> dict:
+    """Pinned host<->device copy-engine bandwidth with 1 GiB buffers (best of
+    3). With `barrier` (one process per GPU), every rank copies at the same
+    time, so the figure is this GPU's share of the host link while all GPUs
+    use it: the denominator the transfers of a multi-GPU run compete for."""
     n = 1 << 30
     host = torch.empty(n, dtype=torch.uint8, pin_memory=True)
     dev = torch.empty(n, dtype=torch.uint8, device=device)
@@ -154,6 +157,9 @@ def link_peaks(torch, device: int) -> dict:
         with torch.cuda.stream(s):
             fn()
             for _ in range(3):
+                s.synchronize()
+                if barrier:
+                    barrier()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(s)
                 fn()
@@ -163,6 +169,22 @@ def link_peaks(torch, device: int) -> dict:
         out[name] = round(best, 2)
     del host, dev
     return out
+
+
+def aligned_rates(torch, stream, fn, nbytes: int, barrier, reps: int = 3) -> float:
+    """GB/s of `fn` (work enqueued on `stream`) started on every rank at once;
+    median of `reps`, device-timed on the stream."""
+    vals = []
+    for _ in range(reps):
+        stream.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        b.synchronize()
+        vals.append(nbytes / (a.elapsed_time(b) / 1e3) / 1e9)
+    return statistics.median(vals)
 
 
 def make_workload(torch, wl: dict, device: int, rank: int, world: int, order: str):
@@ -758,7 +780,8 @@ def main() -> int:
 
     cpus = bind_to_gpu_cpus(local)
     peaks = measured_peaks()
-    link = link_peaks(torch, local)
+    link = link_peaks(torch, local, barrier if world > 1 else None)  # all ranks at once
+    link_d2h_all, link_h2d_all = ranks.gather(link["d2h"]), ranks.gather(link["h2d"])
     tensors, src, dst = make_workload(torch, wl, local, rank, world, args.order)
     n = len(src)
     payload = payload_bytes(tensors, n)
@@ -811,10 +834,21 @@ def main() -> int:
     ms_max = max_over_ranks(ms)
     steps = args.steps
     value = world * 2 * payload * steps / (ms_max / 1e3) / 1e9
-    save_gbps = min_over_ranks(payload / (statistics.median(save_ms) / 1e3) / 1e9)
-    load_gbps = min_over_ranks(payload / (statistics.median(load_ms) / 1e3) / 1e9)
+    my_save = payload / (statistics.median(save_ms) / 1e3) / 1e9
+    my_load = payload / (statistics.median(load_ms) / 1e3) / 1e9
+    save_gbps, load_gbps = min_over_ranks(my_save), min_over_ranks(my_load)
+    # Each rank against its own share of the link (measured with all ranks copying).
+    save_frac = min_over_ranks(my_save / link["d2h"])
+    load_frac = min_over_ranks(my_load / link["h2d"])
     p50_load = max_over_ranks(statistics.median(load_ms))
     kernel_gbps = st["kernel_bytes"] / (st["kernel_ms"] / 1e3) / 1e9 if st["kernel_ms"] > 0 else None
+
+    # Saves alone and loads alone, started on every rank at once: the same
+    # traffic pattern as the link peaks, so the fractions compare like with like
+    # (inside a step, ranks drift apart and one rank's saves meet another's loads).
+    al_save = aligned_rates(torch, stream, lambda: ex.save(saves, stream=sp), payload, barrier)
+    al_load = aligned_rates(torch, stream, lambda: ex.load(loads, stream=sp), payload, barrier)
+    al_save_all, al_load_all = ranks.gather(al_save), ranks.gather(al_load)
 
     # ---- e2e through the engine API (host wall clock) ------------------------
     e2e_steps = args.e2e_steps or args.steps
@@ -888,7 +922,6 @@ def main() -> int:
         cpu = CpuWorkload(wl, os.cpu_count() or 1).rate(args.cpu_seconds)
 
     if rank == 0:
-        link_dir = min(link["h2d"], link["d2h"])
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / steps, 4), "higher_is_better": True,
@@ -898,9 +931,19 @@ def main() -> int:
             "save_GBps": round(save_gbps, 3), "load_GBps": round(load_gbps, 3), "p50_load_ms": round(p50_load, 3),
             "payload_bytes_per_direction": payload,
             "host_link": {"peak_h2d_GBps": link["h2d"], "peak_d2h_GBps": link["d2h"],
-                          "save_frac": round(save_gbps / link["d2h"], 3),
-                          "load_frac": round(load_gbps / link["h2d"], 3),
-                          "how": "pinned 1 GiB cudaMemcpyAsync, best of 3, this GPU"},
+                          "save_frac": round(save_frac, 3), "load_frac": round(load_frac, 3),
+                          "per_rank_peak_d2h_GBps": [round(x, 2) for x in link_d2h_all],
+                          "per_rank_peak_h2d_GBps": [round(x, 2) for x in link_h2d_all],
+                          "aligned": {
+                              "save_GBps_per_rank": [round(x, 2) for x in al_save_all],
+                              "load_GBps_per_rank": [round(x, 2) for x in al_load_all],
+                              "save_frac_min": round(min(a / p for a, p in zip(al_save_all, link_d2h_all)), 3),
+                              "load_frac_min": round(min(a / p for a, p in zip(al_load_all, link_h2d_all)), 3),
+                              "how": "saves alone, then loads alone, started on every rank at once (median "
+                                     "of 3); each rank against its own concurrent peak"},
+                          "how": "pinned 1 GiB cudaMemcpyAsync, best of 3, every rank copying at once; "
+                                 "peak_* are rank 0's; *_frac = min over ranks of the step's save (load) rate "
+                                 "over that rank's own peak"},
             "roofline": {"bound": "hbm", "achieved": round(kernel_gbps, 1) if kernel_gbps else None,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(kernel_gbps / peaks["hbm_gbs"], 3) if kernel_gbps else None,

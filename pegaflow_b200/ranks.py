@@ -63,6 +63,19 @@ class Ranks:
     def sum(self, x: float) -> float:
         return self._reduce(x, "sum")
 
+    def gather(self, x: float) -> list[float]:
+        """Every rank's value, in rank order, on every rank."""
+        if self.world == 1:
+            return [float(x)]
+        import torch
+        import torch.distributed as dist
+
+        dev = f"cuda:{self.local}" if self.backend == "nccl" else "cpu"
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        dist.all_gather(out, t)
+        return [float(v.item()) for v in out]
+
     def barrier(self) -> None:
         if self.world > 1:
             import torch.distributed as dist

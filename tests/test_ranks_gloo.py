@@ -56,6 +56,7 @@ def _worker(rank: int, world: int, port: int, out):
         slowest = r.max(float(r.rank + 1))
         fastest = r.min(float(r.rank + 1))
         total = r.sum(float(seg))
+        assert r.gather(float(10 * r.rank + 1)) == [float(10 * i + 1) for i in range(r.world)]
         out.put((r.rank, ok, slowest, fastest, total, (lo, hi)))
     finally:
         r.close()
