@@ -250,31 +250,54 @@ def payload_bytes(tensors, n) -> int:
 class CpuWorkload:
     """Oracle port of the reference's copies (multi-threaded memcpy gather and
     scatter) on host-resident buffers with the workload's layout: a bounded
-    sample of `max_layers` layers with the workload's block lists."""
+    sample of `max_layers` layers with the workload's block lists.
 
-    def __init__(self, wl: dict, threads: int, max_layers: int = 8):
+    `pool` picks the memory the pool regions live in: "malloc" (cacheable
+    pages), "pinned" (page-locked, cacheable) or "pinned_wc" (page-locked and
+    write-combined, the reference's pool memory, pinned_mem.rs:159, which the
+    CPU reads uncached)."""
+
+    def __init__(self, wl: dict, threads: int, max_layers: int = 8, pool: str = "malloc"):
         from oracle import oracle
 
         self.oracle = oracle
         oracle.build()
         self.threads = threads
+        self._keep = []
         L = min(wl["layers"], max_layers)
         nb, bs, hd, heads = wl["num_blocks"], wl["block_size"], wl["head_dim"], wl["heads"]
         seg = bs * heads * hd * 2
         n = wl["blocks"]
         src = np.random.default_rng(3).permutation(nb)[:n]
         dst = np.random.default_rng(4).permutation(nb)[:n]
+
+        def region(nbytes):
+            if pool == "malloc":
+                return np.zeros(nbytes, np.uint8)
+            from pegaflow_b200 import PinnedBuffer
+
+            buf = PinnedBuffer(nbytes, write_combined=pool == "pinned_wc")
+            self._keep.append(buf)
+            arr = buf.numpy()
+            arr[::4096] = 0
+            return arr
+
         self.saves, self.loads = [], []
         for i in range(L):
             lay = oracle.Layout(nb * seg, nb, seg, 0, 1) if wl.get("separate") else \
                 oracle.Layout(2 * nb * seg, nb, seg, nb * seg, 2)
             cache = np.empty(lay.size_bytes, np.uint8)
             cache[::4096] = i  # fault every page in before timing
-            kp = np.zeros(n * seg, np.uint8)
-            vp = np.zeros(n * seg, np.uint8) if lay.split else None
+            kp = region(n * seg)
+            vp = region(n * seg) if lay.split else None
             self.saves.append((lay, cache, src, kp, vp))
             self.loads.append((lay, cache, dst, kp, vp))
-        self.sample = f"{L} of {wl['layers']} layers x {n} blocks (save + load), host-resident buffers"
+        self.sample = f"{L} of {wl['layers']} layers x {n} blocks (save + load), host-resident buffers, pool: {pool}"
+
+    def close(self) -> None:
+        for b in self._keep:
+            b.close()
+        self._keep.clear()
 
     def step(self) -> int:
         moved = self.oracle.mt_transfer(self.saves, True, self.threads)
@@ -920,6 +943,13 @@ def main() -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = CpuWorkload(wl, os.cpu_count() or 1).rate(args.cpu_seconds)
+        # The same copies with the pool in page-locked memory, cacheable and
+        # write-combined (shorter samples; reported beside the baseline).
+        cpu["pool_variants_GBps"] = {}
+        for kind in ("pinned", "pinned_wc"):
+            cw = CpuWorkload(wl, os.cpu_count() or 1, pool=kind)
+            cpu["pool_variants_GBps"][kind] = cw.rate(args.cpu_seconds / 4)["value"]
+            cw.close()
 
     if rank == 0:
         line = {
