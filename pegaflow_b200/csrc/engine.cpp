@@ -43,6 +43,27 @@ DeviceWorker::~DeviceWorker() {
   }
   cv_.notify_all();
   if (thread_.joinable()) thread_.join();
+  cudaSetDevice(exec_->device());
+  for (cudaStream_t s : all_save_streams_) cudaStreamDestroy(s);
+}
+
+cudaStream_t DeviceWorker::acquire_save_stream() {
+  std::lock_guard<std::mutex> g(streams_mu_);
+  if (!free_save_streams_.empty()) {
+    cudaStream_t s = free_save_streams_.back();
+    free_save_streams_.pop_back();
+    return s;
+  }
+  cuda_check(cudaSetDevice(exec_->device()), "cudaSetDevice");
+  cudaStream_t s = nullptr;
+  cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate(save)");
+  all_save_streams_.push_back(s);
+  return s;
+}
+
+void DeviceWorker::release_save_stream(cudaStream_t s) {
+  std::lock_guard<std::mutex> g(streams_mu_);
+  free_save_streams_.push_back(s);
 }
 
 void DeviceWorker::submit_load(LoadTask task) {
@@ -517,7 +538,15 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
     }
     const auto t_plan = Clock::now();
     Executor& ex = worker->executor();
-    ex.save(layers.data(), layers.size(), ex.save_stream());
+    // The call orders on a stream of its own, so concurrent saves on this
+    // device (other instances, other RPC threads) each wait only for their
+    // own copies; the executor's save lane still runs them in order.
+    struct StreamLease {
+      DeviceWorker* w;
+      cudaStream_t s;
+      ~StreamLease() { w->release_save_stream(s); }
+    } lease{worker.get(), worker->acquire_save_stream()};
+    ex.save(layers.data(), layers.size(), lease.s);
 
     // LayerBlocks (lib.rs:687-698, 755-763) are built while the copy runs,
     // one batch per entry sharing its pool allocations; their slots are
@@ -545,7 +574,7 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
       built[k] = std::move(batch);
       if (k > 0 && same_hashes) same_hashes = p.hashes == planned[0].hashes || *p.hashes == *planned[0].hashes;
     }
-    cuda_check(cudaStreamSynchronize(ex.save_stream()), "cudaStreamSynchronize(save)");
+    cuda_check(cudaStreamSynchronize(lease.s), "cudaStreamSynchronize(save)");
     const auto t_xfer = Clock::now();
 
     // insert_slot (lib.rs:700-705, 765-770): entry by entry, or in one

@@ -63,8 +63,15 @@ class DeviceWorker {
   Executor& executor() { return *exec_; }
   void submit_load(LoadTask task);
   bool wait_idle(double timeout_s);
+  // A stream for one save call to order on and wait for, so that concurrent
+  // saves on this device each wait only for their own copies. Return it with
+  // release_save_stream once synchronised.
+  cudaStream_t acquire_save_stream();
+  void release_save_stream(cudaStream_t s);
 
  private:
+  std::mutex streams_mu_;
+  std::vector<cudaStream_t> free_save_streams_, all_save_streams_;
   void load_loop();
   void process(LoadTask& task);
   // Loads `layers`, raising `words[l]` (a LoadState's per-layer words) as

@@ -253,3 +253,40 @@ def test_save_while_a_load_runs(cuda, oracle):
     assert p.e.count_prefix_hit_blocks("inst", hb) == 300
     p.check_slots(hb[:50] + hb[-50:], range(4))
     p.check_caches()
+
+
+def test_concurrent_saves_of_two_instances(cuda, oracle):
+    """Two instances on one device saving from two threads at once (each save
+    call orders on a stream of its own; the device's save lane runs them in
+    turn): every sealed block holds its own source bytes."""
+    import threading
+
+    torch = cuda
+    p = Pair(torch, oracle)
+    insts = {"i1": ("ns1", 60), "i2": ("ns2", 70)}
+    for inst, (ns, seed) in insts.items():
+        for j in range(2):
+            p.register(f"{inst}.L{j}", kv(torch, (2, 512, 16, 8, 128), torch.bfloat16, seed + j), inst=inst, ns=ns,
+                       num_layers=2)
+    work = {inst: [(np.random.default_rng(seed + k).permutation(512)[:40].tolist(), hashes_for(f"{inst}-{k}", 40))
+                   for k in range(6)] for inst, (_, seed) in insts.items()}
+    errors = []
+
+    def run(inst):
+        try:
+            for ids, hs in work[inst]:
+                p.e.batch_save_kv_blocks(inst, 0, 0, [(f"{inst}.L{j}", ids, hs) for j in range(2)])
+        except Exception as e:  # reported by the main thread
+            errors.append(e)
+
+    threads = [threading.Thread(target=run, args=(inst,)) for inst in work]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(120)
+    assert not errors and not any(t.is_alive() for t in threads)
+    for inst, (ns, _) in insts.items():
+        for ids, hs in work[inst]:
+            p.m.batch_save(inst, 0, 0, [(f"{inst}.L{j}", ids, hs) for j in range(2)])
+            assert p.e.count_prefix_hit_blocks(inst, hs) == 40
+            p.check_slots(hs[:4] + hs[-4:], range(2), ns=ns)
