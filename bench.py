@@ -407,26 +407,52 @@ def run_pd(args) -> None:
         si, di = reqs[r]
         ex0.p2p([P2PSpec(x, y, si, di) for x, y in zip(sl, dl)], 1, push=True, stream=stream.cuda_stream)
 
-    pool = PinnedBuffer(payload + layers * 4096, write_combined=True)
-    saves, loads = [], []
-    off = 0
-    for x, y in zip(sl, dl):
-        k, v = pool.ptr + off, pool.ptr + off + n * 32768
-        ks = np.arange(n, dtype=np.uint64) * 32768 + k
-        saves.append((x, k, v))
-        loads.append((y, ks, ks + n * 32768))
-        off += 2 * n * 32768 + 4096
+    # Two pool regions: the pipelined bounce saves request r+1 on GPU0 while
+    # GPU1 still loads request r.
+    region = payload + layers * 4096
+    pool = PinnedBuffer(2 * region, write_combined=True)
+    saves, loads = [[], []], [[], []]
+    for half in (0, 1):
+        off = half * region
+        for x, y in zip(sl, dl):
+            k, v = pool.ptr + off, pool.ptr + off + n * 32768
+            ks = np.arange(n, dtype=np.uint64) * 32768 + k
+            saves[half].append((x, k, v))
+            loads[half].append((y, ks, ks + n * 32768))
+            off += 2 * n * 32768 + 4096
 
     def bounce(r, stream):
         si, di = reqs[r]
         go = torch.cuda.Event()
         go.record(stream)  # the save starts after the request's start event
         s0.wait_event(go)
-        ex0.save([SaveSpec(x, si, k, v) for x, k, v in saves], stream=s0.cuda_stream)
+        ex0.save([SaveSpec(x, si, k, v) for x, k, v in saves[0]], stream=s0.cuda_stream)
         ev = torch.cuda.Event()
         ev.record(s0)
         stream.wait_event(ev)
-        ex1.load([LoadSpec(y, di, ks, vs) for y, ks, vs in loads], stream=stream.cuda_stream)
+        ex1.load([LoadSpec(y, di, ks, vs) for y, ks, vs in loads[0]], stream=stream.cuda_stream)
+
+    def bounce_pipelined(reps):
+        """Saves run ahead on GPU0 (one region ahead); each load on GPU1 waits
+        for its own save. Returns ms from the first save to the last load."""
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(s1)
+        s0.wait_event(start)
+        saved, loaded = [], []
+        for r in range(reps):
+            si, di = reqs[r]
+            if r >= 2:
+                s0.wait_event(loaded[r - 2])  # its pool region is free again
+            ex0.save([SaveSpec(x, si, k, v) for x, k, v in saves[r % 2]], stream=s0.cuda_stream)
+            saved.append(torch.cuda.Event())
+            saved[-1].record(s0)
+            s1.wait_event(saved[-1])
+            ex1.load([LoadSpec(y, di, ks, vs) for y, ks, vs in loads[r % 2]], stream=s1.cuda_stream)
+            loaded.append(torch.cuda.Event())
+            loaded[-1].record(s1)
+        end.record(s1)
+        end.synchronize()
+        return start.elapsed_time(end)
 
     for fn in (pull, push, bounce):
         timed(fn, s1 if fn is not push else s0, min(3, requests))
@@ -436,6 +462,11 @@ def run_pd(args) -> None:
         ms = timed(fn, st, reps)
         res[name] = {"GBps": round(payload * reps / (sum(ms) / 1e3) / 1e9, 2),
                      "p50_request_ms": round(statistics.median(ms), 3), "requests": reps}
+    reps = min(requests, args.pd_bounce_requests)
+    bounce_pipelined(2)
+    res["host_pool"]["pipelined_GBps"] = round(payload * reps / (bounce_pipelined(reps) / 1e3) / 1e9, 2)
+    res["host_pool"]["how"] = ("GBps and p50: one request at a time (save on GPU0, then load on GPU1); "
+                               "pipelined_GBps: saves run one request ahead of loads, two pool regions")
     best = max(("p2p_pull", "p2p_push"), key=lambda k: res[k]["GBps"])
     line = {
         "metric": METRIC, "value": res[best]["GBps"], "unit": "GB/s", "n_gpus": 2, "steps": requests,
