@@ -1048,9 +1048,18 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     kernel_bytes = b.total_bytes;
   } else {
     // Small first chunk: the first layers of a layer-wise restore are ready
-    // after one small DMA.
+    // after one small DMA. When the caller waits on per-layer flags, the
+    // first chunk holds about two layers (at least 4 MiB), so layer 0's flag
+    // (and, for KV listed beside its scales, the scales') rises after the
+    // DMA of those layers alone; the chunks then double as usual.
+    uint64_t first = first_chunk_;
+    if (layer_done && !b.layers.empty()) {
+      const PlanLayer& p0 = b.layers.front();
+      const uint64_t layer0 = static_cast<uint64_t>(p0.units) * p0.n * p0.unit_bytes;
+      first = std::min(first, std::max<uint64_t>(kLayerwiseMinFirstChunk, 2 * layer0));
+    }
     std::vector<Chunk> chunks;
-    make_chunks(b, first_chunk_, &chunks);
+    make_chunks(b, first, &chunks);
     for (size_t k = 0; k < chunks.size(); ++k) {
       const uint32_t si = static_cast<uint32_t>(k % slots_);
       uint8_t* slot = staging + static_cast<uint64_t>(si) * slot_bytes_;
