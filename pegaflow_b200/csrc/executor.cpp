@@ -280,14 +280,7 @@ void Executor::build_save(const pf_save_layer* layers, uint64_t n_layers, bool s
     if (g.unit_bytes > kMaxUnitBytes) throw invalid_argument("block larger than 2 GiB");
     const uint64_t block_size = l.bytes_per_block * l.segments;
 
-    for (uint64_t i = 0; i < s.n; ++i) {
-      const int64_t bi = s.block_idx[i];
-      if (bi < 0 || static_cast<uint64_t>(bi) >= l.num_blocks) {
-        // lib.rs:597-603
-        throw invalid_argument("block " + std::to_string(bi) + " out of range for layer " + lname + " (" +
-                               std::to_string(l.num_blocks) + " blocks registered)");
-      }
-      const uint64_t blk = static_cast<uint64_t>(bi);
+    auto check_offsets = [&](uint64_t blk) {
       if (is_split_layout(l)) {
         segment_offset(l, blk, 0);
         segment_offset(l, blk, 1);
@@ -297,6 +290,35 @@ void Executor::build_save(const pf_save_layer* layers, uint64_t n_layers, bool s
         for (uint64_t sg = 0; sg < l.segments; ++sg) segment_offset(l, blk, sg);
       }
       for (uint32_t u = 0; u < g.units; ++u) check_unit_range(l, blk, u, g);
+    };
+    auto check_block = [&](uint64_t i) {
+      const int64_t bi = s.block_idx[i];
+      if (bi < 0 || static_cast<uint64_t>(bi) >= l.num_blocks) {
+        // lib.rs:597-603
+        throw invalid_argument("block " + std::to_string(bi) + " out of range for layer " + lname + " (" +
+                               std::to_string(l.num_blocks) + " blocks registered)");
+      }
+      check_offsets(static_cast<uint64_t>(bi));
+    };
+    // Every offset and copy end grows with the block index, so when all ids
+    // are in range, checking the largest id checks them all. Any failure
+    // replays the per-block checks in list order, for the same first error.
+    bool fast = true;
+    uint64_t max_blk = 0;
+    for (uint64_t i = 0; i < s.n && fast; ++i) {
+      const int64_t bi = s.block_idx[i];
+      fast = bi >= 0 && static_cast<uint64_t>(bi) < l.num_blocks;
+      if (fast) max_blk = std::max(max_blk, static_cast<uint64_t>(bi));
+    }
+    if (fast) {
+      try {
+        check_offsets(max_blk);
+      } catch (const std::exception&) {
+        fast = false;
+      }
+    }
+    if (!fast) {
+      for (uint64_t i = 0; i < s.n; ++i) check_block(i);
     }
 
     // Host destinations (SaveBlock pointers, lib.rs:671-679 and 739-747).
@@ -394,18 +416,38 @@ void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool s
     if (g.unit_bytes > kMaxUnitBytes) throw invalid_argument("block larger than 2 GiB");
     const bool split = is_split_layout(l);
 
-    uint64_t max_id = 0;
-    for (uint64_t i = 0; i < s.n; ++i) {
-      const int64_t bi = s.block_idx[i];
-      if (bi < 0) throw invalid_argument("negative block index " + std::to_string(bi));
-      const uint64_t blk = static_cast<uint64_t>(bi);
+    auto check_offsets = [&](uint64_t blk) {
       // process_load_task's checks (gpu_worker.rs:227-230, 266-267) ...
       segment_offset(l, blk, 0);
       if (split) segment_offset(l, blk, 1);
       // ... plus the copy's own end (see check_unit_range).
       for (uint32_t u = 0; u < g.units; ++u) check_unit_range(l, blk, u, g);
-      if (s.k_src[i] == nullptr) throw invalid_argument("null source pointer for block " + std::to_string(bi));
-      max_id = std::max(max_id, blk);
+    };
+    // As for saves: with no negative id and no null source, checking the
+    // largest id checks every block; otherwise the per-block checks run in
+    // list order for the same first error.
+    uint64_t max_id = 0;
+    bool fast = true;
+    for (uint64_t i = 0; i < s.n && fast; ++i) {
+      const int64_t bi = s.block_idx[i];
+      fast = bi >= 0 && s.k_src[i] != nullptr;
+      if (fast) max_id = std::max(max_id, static_cast<uint64_t>(bi));
+    }
+    if (fast) {
+      try {
+        check_offsets(max_id);
+      } catch (const std::exception&) {
+        fast = false;
+      }
+    }
+    if (!fast) {
+      for (uint64_t i = 0; i < s.n; ++i) {
+        const int64_t bi = s.block_idx[i];
+        if (bi < 0) throw invalid_argument("negative block index " + std::to_string(bi));
+        check_offsets(static_cast<uint64_t>(bi));
+        if (s.k_src[i] == nullptr) throw invalid_argument("null source pointer for block " + std::to_string(bi));
+        max_id = std::max(max_id, static_cast<uint64_t>(bi));
+      }
     }
 
     // The reference copies a layer's blocks in list order on one stream, so
@@ -754,8 +796,13 @@ void Executor::make_chunks(const Built& b, uint64_t first_limit, std::vector<Chu
         cur_db = ud / kDenseAlign * kDenseAlign;
         first = false;
       }
-      if (ue - cur_db <= limit) {  // whole unit joins the current chunk
-        last_end = ue;
+      if (ue - cur_db <= limit) {  // whole unit joins the current chunk ...
+        // ... and so do the following units that end inside the limit
+        // (units of a layer are uniform): skip to the last of them.
+        const uint64_t fit = (cur_db + limit - ud) / p.unit_bytes;  // >= 1 units starting at ul
+        const uint64_t last = std::min(nunits - 1, ul + fit - 1);
+        ul = last;
+        last_end = dense + (last + 1) * p.unit_bytes;
         continue;
       }
       for (uint32_t t = 0; t < p.tiles_per_unit; ++t) {

@@ -254,7 +254,27 @@ def test_out_of_range_ids_fail_before_any_copy(cuda):
         ex.save([SaveSpec(Layout.from_tensor(t), np.array([0, 16]), pool.ptr, pool.ptr + 4096 * 2)])
     with pytest.raises(RuntimeError, match="block -1 out of range"):
         ex.save([SaveSpec(Layout.from_tensor(t), np.array([-1]), pool.ptr, pool.ptr + 4096)])
+    # The first bad id in list order is the one reported, not the largest.
+    with pytest.raises(RuntimeError, match="block 17 out of range"):
+        ex.save([SaveSpec(Layout.from_tensor(t), np.array([3, 17, 5, 40]), pool.ptr, pool.ptr + 4096 * 4)])
     assert (pool.numpy() == 7).all()
+
+
+def test_load_past_the_registration_names_the_first_bad_block(cuda):
+    torch = cuda
+    from pegaflow_b200 import Executor, Layout, LoadSpec, PinnedBuffer
+
+    ex = Executor(0)
+    t = kv(torch, (32, 16, 128), torch.bfloat16, 2)  # blocks-first, 4 KiB blocks
+    before = host_bytes(t)
+    pool = PinnedBuffer(1 << 20)
+    ks = np.array([pool.ptr + i * 4096 for i in range(4)], np.uint64)
+    with pytest.raises(RuntimeError, match="Block 35 segment 0 exceeds registered memory"):
+        ex.load([LoadSpec(Layout.from_tensor(t), np.array([2, 35, 3, 40]), ks, None)])
+    with pytest.raises(RuntimeError, match="negative block index -2"):
+        ex.load([LoadSpec(Layout.from_tensor(t), np.array([2, -2, 3, 40]), ks, None)])
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host_bytes(t), before)  # nothing was copied
 
 
 def test_direct_mode_refuses_unregistered_host_memory(cuda):
