@@ -1022,7 +1022,6 @@ def main() -> int:
                     "p50_first_layer_ms": round(e2e_first_layer_p50, 3), "steps": e2e_steps,
                     "api": "PegaEngine.batch_save_kv_blocks + batch_load_kv_blocks + PyLoadState"},
             "gpu_launches": st["kernel_launches"],
-            "executor_host_ms_per_call": round(st["host_ms"] / max(1, 2 * steps), 3),
             "host_cpus": (f"{len(cpus)} CPUs local to the GPU (NVML affinity)" if cpus else "unbound"),
             "copy_calls": st["copy_calls"],
             "reference_copy_path": ref,
