@@ -104,7 +104,8 @@ typedef struct pf_executor_config {
    * raises the first per-layer flags early; large later chunks keep the
    * kernel launch count low. Saves start at the larger of this and half a
    * slot. A load given per-layer flags starts at the smaller of this and
-   * about two of its layers (at least 4 MiB). 0 = default (64 MiB). */
+   * its first layer plus the small layers listed right after it (at least
+   * 4 MiB). 0 = default (64 MiB). */
   uint64_t first_chunk_bytes;
 } pf_executor_config;
 

@@ -1096,14 +1096,18 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
   } else {
     // Small first chunk: the first layers of a layer-wise restore are ready
     // after one small DMA. When the caller waits on per-layer flags, the
-    // first chunk holds about two layers (at least 4 MiB), so layer 0's flag
-    // (and, for KV listed beside its scales, the scales') rises after the
-    // DMA of those layers alone; the chunks then double as usual.
+    // first chunk holds layer 0 and the small layers listed right after it
+    // (per-block scales beside their KV), at least 4 MiB, so layer 0's flags
+    // rise after the DMA of those bytes alone; the chunks then double as usual.
     uint64_t first = first_chunk_;
     if (layer_done && !b.layers.empty()) {
-      const PlanLayer& p0 = b.layers.front();
-      const uint64_t layer0 = static_cast<uint64_t>(p0.units) * p0.n * p0.unit_bytes;
-      first = std::min(first, std::max<uint64_t>(kLayerwiseMinFirstChunk, 2 * layer0));
+      auto layer_bytes = [](const PlanLayer& p) { return static_cast<uint64_t>(p.units) * p.n * p.unit_bytes; };
+      const uint64_t layer0 = layer_bytes(b.layers[0]);
+      uint64_t span = align_up(layer0, kDenseAlign);  // dense bytes, as the chunks count them
+      for (size_t i = 1; i < b.layers.size() && layer_bytes(b.layers[i]) * 8 <= layer0; ++i) {
+        span += align_up(layer_bytes(b.layers[i]), kDenseAlign);
+      }
+      first = std::min(first, std::max<uint64_t>(kLayerwiseMinFirstChunk, span));
     }
     std::vector<Chunk> chunks;
     make_chunks(b, first, &chunks);

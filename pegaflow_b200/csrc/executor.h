@@ -33,7 +33,8 @@ bool is_contiguous_layout(const pf_layer_desc& l);  // transfer.rs:50-52
 constexpr uint64_t kDefaultSlotBytes = 512ull << 20;
 constexpr uint32_t kDefaultSlots = 2;
 constexpr uint64_t kDefaultFirstChunkBytes = 64ull << 20;
-// Lower bound of a layer-wise load's first chunk (about two layers).
+// Lower bound of a layer-wise load's first chunk (which holds layer 0 and
+// the small layers listed right after it).
 constexpr uint64_t kLayerwiseMinFirstChunk = 4ull << 20;
 
 // Layout checks of register_context_layer (lib.rs:389-449).
