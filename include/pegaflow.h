@@ -103,9 +103,10 @@ typedef struct pf_executor_config {
    * twice the previous one, up to staging_chunk_bytes. A small first chunk
    * raises the first per-layer flags early; large later chunks keep the
    * kernel launch count low. Saves start at the larger of this and half a
-   * slot. A load given per-layer flags starts at the smaller of this and
-   * its first layer plus the small layers listed right after it (at least
-   * 4 MiB). 0 = default (64 MiB). */
+   * slot; loads without per-layer flags use whole slots. A load given
+   * per-layer flags starts at the smaller of this and its first layer plus
+   * the small layers listed right after it (at least 4 MiB).
+   * 0 = default (64 MiB). */
   uint64_t first_chunk_bytes;
 } pf_executor_config;
 

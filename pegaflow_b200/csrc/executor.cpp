@@ -1099,7 +1099,12 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     // first chunk holds layer 0 and the small layers listed right after it
     // (per-block scales beside their KV), at least 4 MiB, so layer 0's flags
     // rise after the DMA of those bytes alone; the chunks then double as usual.
-    uint64_t first = first_chunk_;
+    // Without per-layer flags nobody reads the first layers early, so the
+    // load uses whole slots from the start: fewer launches (each pays a fixed
+    // cost of tens of microseconds while DMA streams), and the remainder,
+    // the smallest chunk, comes last, where its unpack is the only work
+    // left after the final DMA.
+    uint64_t first = layer_done ? first_chunk_ : slot_bytes_;
     if (layer_done && !b.layers.empty()) {
       auto layer_bytes = [](const PlanLayer& p) { return static_cast<uint64_t>(p.units) * p.n * p.unit_bytes; };
       const uint64_t layer0 = layer_bytes(b.layers[0]);

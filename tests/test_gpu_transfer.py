@@ -64,8 +64,11 @@ def save_and_check(cuda, oracle, ex, layers_and_ids, pool):
     return regions
 
 
-def load_and_check(cuda, oracle, ex, dst_tensors, regions, dst_ids):
-    from pegaflow_b200 import LoadSpec
+def load_and_check(cuda, oracle, ex, dst_tensors, regions, dst_ids, layer_flags=False):
+    """Load every region into `dst_ids` and compare with the oracle. With
+    `layer_flags`, the load also raises per-layer flags (which start its chunk
+    schedule small) and every flag must be up afterwards."""
+    from pegaflow_b200 import LoadSpec, PinnedBuffer
 
     specs, expect = [], []
     for t, (k, v, lay), ids in zip(dst_tensors, regions, dst_ids):
@@ -81,10 +84,17 @@ def load_and_check(cuda, oracle, ex, dst_tensors, regions, dst_ids):
         oracle.load_layer(olayout(oracle, dlay), ref, ids, [int(x) for x in ks],
                           [int(x) for x in vs] if vs is not None else None)
         expect.append(ref)
-    ex.load(specs)
+    if layer_flags:
+        flags = PinnedBuffer(8 * len(specs))
+        flags.numpy()[:] = 0
+        ex.load(specs, layer_done=flags.ptr)
+    else:
+        ex.load(specs)
     cuda.cuda.synchronize()
     for t, ref in zip(dst_tensors, expect):
         np.testing.assert_array_equal(host_bytes(t), ref)
+    if layer_flags:
+        assert flags.numpy(np.int64).tolist() == [1] * len(specs)
 
 
 @pytest.mark.parametrize("mode", MODES)
@@ -143,7 +153,8 @@ def test_many_chunks_and_mixed_layouts(cuda, oracle, mode, chunk, first):
     """Small staging chunks split units across chunks and slots wrap many
     times; layers mix split, blocks-first, 4-byte scales and unaligned units.
     A small first chunk makes every chunk of the growth schedule differ in
-    size (8 KiB, 16 KiB, ... up to the slot)."""
+    size (8 KiB, 16 KiB, ... up to the slot): loads with per-layer flags
+    start there; saves and flagless loads start at half a slot."""
     torch = cuda
     from pegaflow_b200 import Executor, PinnedBuffer
 
@@ -163,6 +174,8 @@ def test_many_chunks_and_mixed_layouts(cuda, oracle, mode, chunk, first):
     regions = save_and_check(torch, oracle, ex, list(zip(layers, ids)), pool)
     dst = [rng.permutation(64)[:40] for _ in layers]
     load_and_check(torch, oracle, ex, layers, regions, dst)
+    dst = [rng.permutation(64)[:40] for _ in layers]
+    load_and_check(torch, oracle, ex, layers, regions, dst, layer_flags=True)
 
 
 @pytest.mark.parametrize("mode", MODES)
