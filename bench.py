@@ -748,9 +748,11 @@ def config_block(args, wl) -> dict:
     return {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
             "blocks_moved": wl["blocks"], "block_ids": args.order, "kv_dtype": "fp16" if wl.get("separate") else "bf16",
             "save_mode": args.save_mode, "load_mode": args.load_mode,
-            "staging": {"slot_MiB": args.chunk_mib or 512, "slots": args.slots or 2,
+            "staging": {"slot_MiB": args.chunk_mib or 512, "slots": args.slots or 2, "lanes": "save, load",
                         "first_chunk_MiB": args.first_chunk_mib or 64, "growth": "x2 per chunk",
-                        "save_first_chunk": "max(first chunk, half a slot)"},
+                        "save_first_chunk": "max(first chunk, half a slot)",
+                        "load_first_chunk": "a whole slot; with per-layer flags (the e2e engine loads) "
+                                            "the first layer, at most the first chunk"},
             "l2": "inputs larger than L2 (payload >= 36 MiB per layer set; KV cache >> 126 MB)",
             "parallelism": f"dp{args.gpus} (independent ranks, weak scaling)"}
 
