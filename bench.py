@@ -171,6 +171,34 @@ def link_peaks(torch, device: int, barrier=None) -> dict:
     return out
 
 
+def duplex_peak(torch, device: int) -> float:
+    """Pinned copies in both directions at once: 1 GiB D2H and 1 GiB H2D on
+    two streams from one start event to both ends (best of 3), total GB/s."""
+    n = 1 << 30
+    h_out = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    h_in = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    d_out = torch.empty(n, dtype=torch.uint8, device=device)
+    d_in = torch.empty(n, dtype=torch.uint8, device=device)
+    s1, s2 = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    best = 0.0
+    for _ in range(4):
+        torch.cuda.synchronize(device)
+        start, end, other = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        start.record(s1)
+        s2.wait_event(start)
+        with torch.cuda.stream(s1):
+            h_out.copy_(d_out, non_blocking=True)
+        with torch.cuda.stream(s2):
+            d_in.copy_(h_in, non_blocking=True)
+        other.record(s2)
+        s1.wait_event(other)
+        end.record(s1)
+        end.synchronize()
+        best = max(best, 2 * n / (start.elapsed_time(end) / 1e3) / 1e9)
+    del h_out, h_in, d_out, d_in
+    return round(best, 2)
+
+
 def aligned_rates(torch, stream, fn, nbytes: int, barrier, reps: int = 3) -> float:
     """GB/s of `fn` (work enqueued on `stream`) started on every rank at once;
     median of `reps`, device-timed on the stream."""
@@ -631,6 +659,7 @@ def run_duplex(args) -> None:
     save_ids, load_ids = perm[:n].astype(np.int64), perm[n:2 * n].astype(np.int64)
     payload = payload_bytes(tensors, n)
     link = link_peaks(torch, 0)
+    link["duplex"] = duplex_peak(torch, 0)
     pool = PinnedBuffer(2 * payload + (4 << 20), write_combined=True)
     saves, _, off = executor_specs(tensors, save_ids, save_ids, pool.ptr)
     _, loads, _ = executor_specs(tensors, load_ids, load_ids, pool.ptr + off)
@@ -734,7 +763,10 @@ def run_duplex(args) -> None:
                 "d2h_bytes_per_step": payload, "serial": e2e["serial"], "duplex": e2e["duplex"],
                 "api": "batch_load_kv_blocks (queued) + batch_save_kv_blocks, then LoadState"},
         "host_link": {"peak_h2d_GBps": link["h2d"], "peak_d2h_GBps": link["d2h"],
-                      "duplex_frac_of_sum": round(res["duplex"]["GBps"] / (link["h2d"] + link["d2h"]), 3)},
+                      "duplex_frac_of_sum": round(res["duplex"]["GBps"] / (link["h2d"] + link["d2h"]), 3),
+                      "peak_duplex_GBps": link["duplex"],
+                      "duplex_frac": round(res["duplex"]["GBps"] / link["duplex"], 3),
+                      "how": "pinned 1 GiB copies, best of 3; peak_duplex: one D2H and one H2D at once"},
         "engine": {k2: (round(m[k2], 2) if isinstance(m[k2], float) else m[k2])
                    for k2 in ("load_failures", "cache_block_evictions", "pool_alloc_failures", "save_plan_ms",
                               "save_transfer_ms", "save_insert_ms", "save_ms", "load_ms")},
