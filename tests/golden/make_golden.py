@@ -106,7 +106,10 @@ CASES = [
 
 
 def main(argv: list[str]) -> int:
-    ref_root = Path(argv[1] if len(argv) > 1 else "/root/reference")
+    if len(argv) < 2:
+        print(__doc__.split("Usage")[1].strip(), file=sys.stderr)
+        return 2
+    ref_root = Path(argv[1])
     install_stubs(ref_root / "python")
     from pegaflow.connector.common import ConnectorContext, LoadIntent, PegaConnectorMetadata, SaveIntent
     from pegaflow.connector.worker import SaveTask, WorkerConnector
