@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define PF_ABI_VERSION 2
+#define PF_ABI_VERSION 3
 
 /* ------------------------------------------------------------------------ */
 /* Status codes: one per EngineError variant (pegaflow-core/src/lib.rs:58-67) */
@@ -472,6 +472,7 @@ typedef struct pf_engine_metrics {
   double save_plan_ms;      /* dedup + pool allocation (host) */
   double save_transfer_ms;  /* pack kernels + D2H, waited on */
   double save_insert_ms;    /* slot bookkeeping after the copy (host) */
+  uint64_t inflight_dropped; /* inflight blocks released after the age limit (ABI 3) */
 } pf_engine_metrics;
 int pf_engine_metrics_get(pf_engine* e, pf_engine_metrics* out);
 

@@ -25,6 +25,7 @@ from ctypes import (
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpegaflow_b200.so"
+ABI_VERSION = 3  # PF_ABI_VERSION the structs below follow
 
 PF_OK = 0
 PF_ERR_INSTANCE_MISSING = 1
@@ -189,6 +190,7 @@ class EngineMetrics(Structure):
         ("save_plan_ms", c_double),
         ("save_transfer_ms", c_double),
         ("save_insert_ms", c_double),
+        ("inflight_dropped", c_uint64),
     ]
 
 
@@ -291,6 +293,9 @@ def _load() -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
+    if lib.pf_abi_version() != ABI_VERSION:  # the structs above would not match
+        raise ImportError(f"{LIB_PATH} has ABI {lib.pf_abi_version()}, these bindings need {ABI_VERSION}: "
+                          "rebuild it with `python -m pegaflow_b200.build`")
     return lib
 
 

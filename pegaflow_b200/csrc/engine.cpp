@@ -735,6 +735,7 @@ void Engine::metrics(pf_engine_metrics* out) {
   out->cache_block_admission_rejections = sc.admission_rejections.load();
   out->cache_block_evictions = sc.evictions.load();
   out->pool_alloc_failures = sc.pool_alloc_failures.load();
+  out->inflight_dropped = sc.inflight_dropped.load();
   out->inflight_blocks = storage_->inflight_count();
   out->cached_blocks = storage_->cached_count();
 }

@@ -256,6 +256,7 @@ void Storage::insert_slots(const std::string& ns, const std::vector<std::string>
                            std::vector<LayerBlockPtr>& blocks, uint64_t total_slots) {
   // Same per-block steps as insert_slot (storage.rs:457-514), with the locks
   // taken once for the whole list instead of once per block.
+  maybe_drop_stale_inflight();
   std::vector<std::pair<BlockKey, SealedBlockPtr>> sealed;
   {
     std::unique_lock<std::mutex> gc(cache_mu_);
@@ -354,6 +355,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
   // gets at most fills-1 < total_slots slots.
   const size_t n = hashes.size();
   if (fills.empty() || n == 0) return;
+  maybe_drop_stale_inflight();
   auto per_fill = [&] {
     for (const SlotFill& f : fills) {
       std::vector<LayerBlockPtr> blocks(n);
@@ -486,6 +488,7 @@ bool Storage::cache_insert_locked(const BlockKey& key, SealedBlockPtr block) {
 
 bool Storage::insert_slot(const std::string& ns, const std::string& hash, uint64_t slot, LayerBlockPtr block,
                           uint64_t total_slots) {
+  maybe_drop_stale_inflight();
   BlockKey key{ns, hash};
   {
     std::lock_guard<std::mutex> g(cache_mu_);
@@ -592,6 +595,38 @@ SealedBlockPtr Storage::cache_peek(const std::string& ns, const std::string& has
 uint64_t Storage::inflight_count() {
   std::lock_guard<std::mutex> g(inflight_mu_);
   return inflight_.size();
+}
+
+uint64_t Storage::drop_stale_inflight() {
+  if (cfg_.inflight_max_age_ms == 0) return 0;
+  const auto now = std::chrono::steady_clock::now();
+  const auto max_age = std::chrono::milliseconds(cfg_.inflight_max_age_ms);
+  std::vector<Inflight> dropped;  // their pool memory is released after the lock
+  {
+    std::lock_guard<std::mutex> g(inflight_mu_);
+    for (auto it = inflight_.begin(); it != inflight_.end();) {
+      if (now - it->second.created > max_age) {
+        dropped.push_back(std::move(it->second));
+        it = inflight_.erase(it);
+      } else {
+        ++it;
+      }
+    }
+  }
+  counters_.inflight_dropped.fetch_add(dropped.size());
+  return dropped.size();
+}
+
+void Storage::maybe_drop_stale_inflight() {
+  if (cfg_.inflight_max_age_ms == 0) return;
+  const int64_t now = std::chrono::duration_cast<std::chrono::nanoseconds>(
+                          std::chrono::steady_clock::now().time_since_epoch())
+                          .count();
+  const int64_t every = std::min<int64_t>(60'000'000'000ll, int64_t(cfg_.inflight_max_age_ms) * 250'000);
+  int64_t last = last_sweep_ns_.load(std::memory_order_relaxed);
+  if (now - last < every) return;
+  if (!last_sweep_ns_.compare_exchange_strong(last, now)) return;  // another save sweeps
+  drop_stale_inflight();
 }
 
 uint64_t Storage::cached_count() {

@@ -9,6 +9,7 @@
 #pragma once
 
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdint>
 #include <functional>
@@ -118,6 +119,12 @@ struct StorageConfig {
   uint64_t pre_evict_threshold_bytes = 5ull << 30;  // storage.rs:35
   uint64_t pre_evict_target_bytes = 8ull << 30;     // storage.rs:37
   uint64_t pre_evict_interval_ms = 100;             // storage.rs:39
+  // An inflight block older than this is dropped with its pool memory (0 =
+  // never). A block skipped for one layer because it was cached, then
+  // evicted before its next layer is saved, becomes an inflight block whose
+  // earlier slots never arrive (the race lib.rs:604-611 describes; the
+  // reference proposes this cleanup but has none).
+  uint64_t inflight_max_age_ms = 3600ull * 1000;
 };
 
 struct StorageCounters {
@@ -125,6 +132,7 @@ struct StorageCounters {
   std::atomic<uint64_t> admission_rejections{0};
   std::atomic<uint64_t> evictions{0};
   std::atomic<uint64_t> pool_alloc_failures{0};
+  std::atomic<uint64_t> inflight_dropped{0};  // stale inflight blocks released
 };
 
 // Count-min-sketch TinyLFU (cache.rs:99-243), deterministic hashing.
@@ -185,6 +193,9 @@ class Storage {
 
   uint64_t inflight_count();
   uint64_t cached_count();
+  // Drops every inflight block older than inflight_max_age_ms and returns
+  // how many. Saves run it on their own, at most every few seconds.
+  uint64_t drop_stale_inflight();
   // Read-only views (hash, slot block addresses; null = empty slot): the
   // cache from least to most recently used, and inflight blocks by hash.
   using BlockView = std::vector<std::pair<std::string, std::vector<const LayerBlock*>>>;
@@ -203,7 +214,12 @@ class Storage {
     uint64_t remaining;
     uint64_t total_slots;
     uint64_t footprint = 0;
+    std::chrono::steady_clock::time_point created = std::chrono::steady_clock::now();
   };
+  // Runs drop_stale_inflight when the last sweep is older than a quarter of
+  // the age limit (at most once a minute), so a save pays for it rarely.
+  void maybe_drop_stale_inflight();
+  std::atomic<int64_t> last_sweep_ns_{0};
   using LruList = std::list<std::pair<BlockKey, SealedBlockPtr>>;
 
   std::shared_ptr<PinnedPool> pool_;

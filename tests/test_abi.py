@@ -27,7 +27,7 @@ def test_binding_covers_header(native):
 
 
 def test_abi_version(native):
-    assert native.lib.pf_abi_version() == 2
+    assert native.lib.pf_abi_version() == 3
 
 
 def test_library_is_sm100a_build(native):
