@@ -1,0 +1,58 @@
+"""bench.py's JSON contract on the CPU: the reference arm's line (the oracle
+port timed on host cores) carries every key the driver reads, the metric is
+BASELINE.json's, engine-level scenarios print an `unavailable` line for the
+reference arm, and the B200 arm fails loudly without a GPU."""
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def run(*args, timeout=300):
+    return subprocess.run([sys.executable, str(ROOT / "bench.py"), *args], capture_output=True, text=True,
+                          timeout=timeout, cwd=ROOT)
+
+
+def last_json(out: str) -> dict:
+    return json.loads(out.strip().splitlines()[-1])
+
+
+def test_reference_arm_line_has_the_contract_keys():
+    p = run("--impl", "reference", "--workload", "gpt2", "--steps", "2", "--warmup", "1")
+    assert p.returncode == 0, p.stderr
+    line = last_json(p.stdout)
+    baseline = json.loads((ROOT / "BASELINE.json").read_text())
+    assert line["impl"] == "reference" and line["metric"] == baseline["metric"]
+    assert line["value"] > 0 and line["unit"] == "GB/s" and line["higher_is_better"] is True
+    assert (line["n_gpus"], line["steps"], line["warmup"]) == (1, 2, 1)
+    assert line["ms_per_step"] > 0 and line["scaling"] == "weak" and line["vs_baseline"] is None
+    assert line["dtype"] == "u8" and "synthetic" in line["data"]
+    assert line["config"]["workload"] == "gpt2"
+    cb = line["cpu_baseline"]
+    assert cb["value"] == line["value"] and cb["kind"] == "port" and cb["cores"] >= 1 and cb["sample"]
+    e2e = line["e2e"]
+    assert e2e["value"] == line["value"] and e2e["unit"] == "GB/s"
+    assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+@pytest.mark.parametrize("workload", ["qwen3_pd", "llama8b_fp8_evict", "llama8b_duplex"])
+def test_engine_scenarios_report_the_reference_arm_unavailable(workload):
+    p = run("--impl", "reference", "--workload", workload)
+    assert p.returncode == 0, p.stderr
+    line = last_json(p.stdout)
+    assert line["impl"] == "reference" and line["unavailable"]
+
+
+def test_b200_arm_fails_loudly_without_a_gpu():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    p = run("--steps", "1", "--warmup", "0", "--no-cpu", "--no-refcopy")
+    assert p.returncode != 0
+    assert not p.stdout.strip()  # no JSON line from a run that did not happen
