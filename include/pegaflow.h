@@ -15,7 +15,9 @@
  *     void*. Pinned pool memory is mapped into the unified address space, so a
  *     pool pointer is valid on every device.
  *   - Thread safety: a pf_engine may be called from many threads at once
- *     (the reference engine is Sync). A pf_executor serialises its own calls.
+ *     (the reference engine is Sync). A pf_executor may be too: it
+ *     serialises the calls of each of its two lanes (saves; loads and peer
+ *     copies) and runs the lanes side by side.
  */
 #ifndef PEGAFLOW_B200_H
 #define PEGAFLOW_B200_H
@@ -113,8 +115,13 @@ typedef struct pf_executor_config {
 /* Fill *cfg with the library defaults. */
 void pf_executor_config_default(pf_executor_config* cfg);
 
-/* One executor per device: streams, staging ring, plan buffers
- * (replaces GpuWorkerPool::spawn, gpu_worker.rs:61-93). */
+/* One executor per device (replaces GpuWorkerPool::spawn,
+ * gpu_worker.rs:61-93, which starts a load thread and a save thread per GPU).
+ * It has two lanes, each with its own streams, staging ring and plan buffers:
+ * saves use one, loads and peer copies the other. Calls on one lane run in
+ * the order they were made; a save and a load, issued from different threads
+ * or on different streams, run at the same time, one per direction of the
+ * host link. */
 int pf_executor_create(int32_t device_id, const pf_executor_config* cfg,
                        pf_executor** out);
 void pf_executor_destroy(pf_executor* exec);
