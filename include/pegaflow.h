@@ -326,7 +326,14 @@ typedef struct pf_engine_config {
   int32_t pool_kind;              /* pf_pool_kind */
   uint64_t hint_value_size_bytes; /* allocator unit hint, 0 = none (storage.rs:84) */
   int32_t pre_evict_enabled;      /* PreEvictConfig (storage.rs:43-76) */
-  int32_t reserved0;
+  /* Pool placement for an engine that drives several GPUs (no reference
+   * counterpart; the reference allocates one pool): 0 = one pool (default);
+   * 1 = one pool per NUMA node of the visible GPUs, each on its node, sized
+   * by its GPU count; 2 = one pool per GPU, on that GPU's node. A save
+   * allocates from its GPU's pool, and reclaim for a pool evicts only blocks
+   * held there. With every GPU on one node, 1 is the same as 0. Placed
+   * pools are page-locked with cudaHostRegister, so not write-combined. */
+  int32_t numa_pools;
   uint64_t pre_evict_threshold_bytes;
   uint64_t pre_evict_target_bytes;
   uint64_t pre_evict_interval_ms;
@@ -448,7 +455,8 @@ int pf_engine_batch_load_kv_blocks(pf_engine* e, const char* instance_id,
 int pf_engine_wait_loads(pf_engine* e, int32_t device_id, double timeout_s);
 
 /* Pool usage (PinnedMemoryPool::usage / largest_free_allocation,
- * pinned_pool.rs:171-185). */
+ * pinned_pool.rs:171-185); with numa_pools, used and total sum the pools and
+ * largest_free is the largest of them. */
 int pf_engine_pool_usage(pf_engine* e, uint64_t* used, uint64_t* total,
                          uint64_t* largest_free);
 

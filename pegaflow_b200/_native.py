@@ -127,7 +127,7 @@ class EngineConfig(Structure):
         ("pool_kind", c_int32),
         ("hint_value_size_bytes", c_uint64),
         ("pre_evict_enabled", c_int32),
-        ("reserved0", c_int32),
+        ("numa_pools", c_int32),
         ("pre_evict_threshold_bytes", c_uint64),
         ("pre_evict_target_bytes", c_uint64),
         ("pre_evict_interval_ms", c_uint64),

@@ -449,10 +449,10 @@ int pf_engine_pool_usage(pf_engine* e, uint64_t* used, uint64_t* total, uint64_t
   if (!e) return null_arg("engine");
   return guarded([&] {
     uint64_t u = 0, t = 0;
-    e->impl->storage().pool().usage(&u, &t);
+    e->impl->storage().usage(&u, &t);  // all pools together
     if (used) *used = u;
     if (total) *total = t;
-    if (largest_free) *largest_free = e->impl->storage().pool().largest_free();
+    if (largest_free) *largest_free = e->impl->storage().largest_free();
   });
 }
 

@@ -221,7 +221,48 @@ Engine::Engine(const pf_engine_config& cfg) : cfg_(cfg) {
   } else if (cfg_.use_hugepages) {
     kind = PinKind::kHugePagesRegistered;
   }
-  pool_ = PinnedPool::create(cfg_.pool_bytes, kind, cfg_.write_combined != 0, cfg_.hint_value_size_bytes);
+  if (cfg_.numa_pools != 0 && kind != PinKind::kPlainHost) {
+    // Group the visible GPUs by NUMA node (numa_pools 1) or one per GPU (2);
+    // each group gets a pool on its node, sized by its share of the GPUs.
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess) {
+      cudaGetLastError();
+      count = 0;
+    }
+    std::vector<int> group_node;
+    std::vector<uint64_t> group_gpus;
+    std::vector<size_t> group_of(static_cast<size_t>(count), 0);
+    for (int d = 0; d < count; ++d) {
+      const int node = device_numa_node(d);
+      size_t g = group_node.size();
+      if (cfg_.numa_pools == 1) {
+        for (size_t i = 0; i < group_node.size(); ++i) {
+          if (group_node[i] == node) g = i;
+        }
+      }
+      if (g == group_node.size()) {
+        group_node.push_back(node);
+        group_gpus.push_back(0);
+      }
+      group_gpus[g] += 1;
+      group_of[d] = g;
+    }
+    if (group_node.size() > 1) {
+      uint64_t given = 0;
+      for (size_t g = 0; g < group_node.size(); ++g) {
+        const uint64_t bytes = g + 1 == group_node.size()
+                                   ? cfg_.pool_bytes - given
+                                   : cfg_.pool_bytes / static_cast<uint64_t>(count) * group_gpus[g];
+        given += bytes;
+        pools_.push_back(PinnedPool::create(bytes, kind, cfg_.write_combined != 0, cfg_.hint_value_size_bytes,
+                                            group_node[g]));
+      }
+      device_pool_ = group_of;
+    }
+  }
+  if (pools_.empty()) {
+    pools_.push_back(PinnedPool::create(cfg_.pool_bytes, kind, cfg_.write_combined != 0, cfg_.hint_value_size_bytes));
+  }
   StorageConfig sc;
   sc.enable_lfu_admission = cfg_.enable_lfu_admission != 0;
   sc.capacity_bytes = cfg_.pool_bytes;
@@ -230,7 +271,7 @@ Engine::Engine(const pf_engine_config& cfg) : cfg_(cfg) {
   if (cfg_.pre_evict_threshold_bytes) sc.pre_evict_threshold_bytes = cfg_.pre_evict_threshold_bytes;
   if (cfg_.pre_evict_target_bytes) sc.pre_evict_target_bytes = cfg_.pre_evict_target_bytes;
   if (cfg_.pre_evict_interval_ms) sc.pre_evict_interval_ms = cfg_.pre_evict_interval_ms;
-  storage_ = std::make_unique<Storage>(pool_, sc);
+  storage_ = std::make_unique<Storage>(pools_, sc);
   if (cfg_.dfs_root && cfg_.dfs_root[0]) {
     DfsConfig dc;
     dc.root = cfg_.dfs_root;
@@ -262,14 +303,19 @@ Engine::~Engine() {
     dfs_.reset();  // stops its threads before the storage they use goes
   }
   storage_.reset();
-  pool_.reset();
+  pools_.clear();
+}
+
+size_t Engine::pool_for_device(int device_id) const {
+  if (device_id < 0 || static_cast<size_t>(device_id) >= device_pool_.size()) return 0;
+  return device_pool_[static_cast<size_t>(device_id)];
 }
 
 std::shared_ptr<DeviceWorker> Engine::device_worker(int device_id) {
   std::lock_guard<std::mutex> g(dev_mu_);
   auto it = devices_.find(device_id);
   if (it != devices_.end()) return it->second;
-  if (pool_->kind() == PinKind::kPlainHost) return nullptr;
+  if (pools_.front()->kind() == PinKind::kPlainHost) return nullptr;
   auto w = std::make_shared<DeviceWorker>(device_id, cfg_.executor, &counters_);
   devices_[device_id] = w;
   return w;
@@ -501,15 +547,16 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
         p.hashes = std::move(kept);
       }
       const uint64_t n = p.ids.size();
+      const size_t pool = pool_for_device(device_id);
       if (p.split) {
         const uint64_t bytes = reg.bytes_per_block * n;
-        p.k_alloc = storage_->allocate(bytes);
+        p.k_alloc = storage_->allocate(bytes, pool);
         if (!p.k_alloc) throw storage_error("pinned pool exhausted while allocating K segment buffer");
-        p.v_alloc = storage_->allocate(bytes);
+        p.v_alloc = storage_->allocate(bytes, pool);
         if (!p.v_alloc) throw storage_error("pinned pool exhausted while allocating V segment buffer");
       } else {
         const uint64_t bytes = reg.bytes_per_block * reg.segments * n;
-        p.k_alloc = storage_->allocate(bytes);
+        p.k_alloc = storage_->allocate(bytes, pool);
         if (!p.k_alloc) throw storage_error("pinned pool exhausted while allocating contiguous block buffer");
       }
       p.worker = gpu->worker;

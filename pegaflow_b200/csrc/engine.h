@@ -148,8 +148,12 @@ class Engine {
                         const std::vector<std::string>& layer_names, const std::vector<int32_t>& block_ids,
                         const std::vector<std::string>& hashes);
 
+  // The pool a save on `device_id` allocates from.
+  size_t pool_for_device(int device_id) const;
+
   pf_engine_config cfg_;
-  std::shared_ptr<PinnedPool> pool_;
+  std::vector<std::shared_ptr<PinnedPool>> pools_;
+  std::vector<size_t> device_pool_;  // device -> index in pools_ (empty: one pool)
   std::unique_ptr<Storage> storage_;
   std::unique_ptr<DfsTier> dfs_;  // null when the packed-file tier is off
   std::shared_mutex inst_mu_;

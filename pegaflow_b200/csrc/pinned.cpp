@@ -2,7 +2,12 @@
 
 #include <cuda_runtime.h>
 #include <sys/mman.h>
+#include <sys/syscall.h>
+#include <unistd.h>
 
+#include <algorithm>
+#include <cctype>
+#include <cerrno>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
@@ -58,8 +63,72 @@ size_t huge_page_size() {
   return 0;
 }
 
-PinnedMemory::PinnedMemory(size_t size, PinKind kind, bool write_combined) : kind_(kind) {
+namespace {
+
+// Linux memory-policy modes and flags (uapi/linux/mempolicy.h).
+constexpr int kMpolPreferred = 1;
+constexpr int kMpolFNode = 1 << 0;
+constexpr int kMpolFAddr = 1 << 1;
+constexpr int kMaxNodes = 1024;
+
+// mbind(MPOL_PREFERRED, {node}) on [p, p + bytes); false when refused.
+bool bind_to_node(void* p, size_t bytes, int node) {
+  if (node < 0 || node >= kMaxNodes) return false;
+  unsigned long mask[kMaxNodes / (8 * sizeof(unsigned long))] = {};
+  mask[node / (8 * sizeof(unsigned long))] = 1ul << (node % (8 * sizeof(unsigned long)));
+  return syscall(SYS_mbind, p, bytes, kMpolPreferred, mask, static_cast<unsigned long>(kMaxNodes), 0u) == 0;
+}
+
+}  // namespace
+
+int numa_node_of(const void* p) {
+  int node = -1;
+  if (syscall(SYS_get_mempolicy, &node, nullptr, 0ul, const_cast<void*>(p), kMpolFNode | kMpolFAddr) != 0) {
+    return -1;
+  }
+  return node;
+}
+
+int device_numa_node(int device) {
+  char bus[32] = {};
+  if (cudaDeviceGetPCIBusId(bus, sizeof(bus), device) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  std::string id(bus);
+  std::transform(id.begin(), id.end(), id.begin(), [](unsigned char c) { return std::tolower(c); });
+  std::ifstream f("/sys/bus/pci/devices/" + id + "/numa_node");
+  int node = -1;
+  if (!(f >> node)) return -1;
+  return node;
+}
+
+PinnedMemory::PinnedMemory(size_t size, PinKind kind, bool write_combined, int numa_node)
+    : kind_(kind), numa_node_(numa_node) {
   if (size == 0) throw Error(PF_ERR_INVALID_ARGUMENT, "size must be greater than zero");
+  if (numa_node >= 0 && kind != PinKind::kHugePagesRegistered) {
+    // Placement needs memory this library maps itself: mmap, bind, then pin
+    // in place (the page faults cudaHostRegister takes follow the binding).
+    const size_t aligned = (size + 4095) & ~size_t(4095);
+    void* p = mmap(nullptr, aligned, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
+    if (p == MAP_FAILED) throw cuda_init("mmap failed for a pool on NUMA node " + std::to_string(numa_node));
+    numa_bound_ = bind_to_node(p, aligned, numa_node);
+    ptr_ = static_cast<uint8_t*>(p);
+    size_ = aligned;
+    mapped_ = true;
+    if (kind == PinKind::kCudaHostAlloc) {
+      cudaError_t err = cudaHostRegister(p, aligned, cudaHostRegisterPortable | cudaHostRegisterMapped);
+      if (err != cudaSuccess) {
+        cudaGetLastError();
+        munmap(p, aligned);
+        ptr_ = nullptr;
+        throw cuda_init(std::string("cudaHostRegister failed: ") + cudaGetErrorString(err));
+      }
+      registered_ = true;
+      pinned_register(ptr_, size_);
+    }
+    return;
+  }
   switch (kind) {
     case PinKind::kCudaHostAlloc: {
       unsigned flags = cudaHostAllocPortable | cudaHostAllocMapped;
@@ -83,6 +152,7 @@ PinnedMemory::PinnedMemory(size_t size, PinKind kind, bool write_combined) : kin
       void* p = mmap(nullptr, aligned, PROT_READ | PROT_WRITE,
                      MAP_PRIVATE | MAP_ANONYMOUS | MAP_HUGETLB, -1, 0);
       if (p == MAP_FAILED) throw cuda_init("mmap failed (MAP_HUGETLB)");
+      if (numa_node >= 0) numa_bound_ = bind_to_node(p, aligned, numa_node);
       cudaError_t err = cudaHostRegister(p, aligned, cudaHostRegisterPortable | cudaHostRegisterMapped);
       if (err != cudaSuccess) {
         cudaGetLastError();
@@ -106,6 +176,14 @@ PinnedMemory::PinnedMemory(size_t size, PinKind kind, bool write_combined) : kin
 
 PinnedMemory::~PinnedMemory() {
   if (!ptr_) return;
+  if (mapped_ && kind_ != PinKind::kHugePagesRegistered) {  // placed on a NUMA node
+    if (registered_) {
+      pinned_unregister(ptr_);
+      if (cudaHostUnregister(ptr_) != cudaSuccess) cudaGetLastError();
+    }
+    munmap(ptr_, size_);
+    return;
+  }
   if (kind_ != PinKind::kPlainHost) pinned_unregister(ptr_);
   switch (kind_) {
     case PinKind::kCudaHostAlloc:

@@ -50,9 +50,9 @@ PoolAllocation::~PoolAllocation() {
 }
 
 std::shared_ptr<PinnedPool> PinnedPool::create(uint64_t bytes, PinKind kind, bool write_combined,
-                                               uint64_t unit_hint) {
+                                               uint64_t unit_hint, int numa_node) {
   if (bytes == 0) throw invalid_argument("Pinned memory pool size must be greater than zero");
-  auto mem = std::make_unique<PinnedMemory>(bytes, kind, write_combined);
+  auto mem = std::make_unique<PinnedMemory>(bytes, kind, write_combined, numa_node);
   const uint64_t actual = mem->size();
   uint64_t unit = unit_hint;
   if (unit == 0) unit = actual > 0xffffffffull ? (actual + 0xfffffffeull) / 0xffffffffull : 1;
@@ -158,7 +158,14 @@ void TinyLfu::age() {
 // Storage
 // ---------------------------------------------------------------------------
 
-Storage::Storage(std::shared_ptr<PinnedPool> pool, const StorageConfig& cfg) : pool_(std::move(pool)), cfg_(cfg) {
+Storage::Storage(std::shared_ptr<PinnedPool> pool, const StorageConfig& cfg)
+    : Storage(std::vector<std::shared_ptr<PinnedPool>>{std::move(pool)}, cfg) {}
+
+Storage::Storage(std::vector<std::shared_ptr<PinnedPool>> pools, const StorageConfig& cfg)
+    : pools_(std::move(pools)), cfg_(cfg) {
+  if (pools_.empty() || std::any_of(pools_.begin(), pools_.end(), [](const auto& p) { return !p; })) {
+    throw invalid_argument("storage needs at least one pool");
+  }
   if (cfg_.enable_lfu_admission) {
     const uint64_t per_value = cfg_.hint_value_size_bytes ? cfg_.hint_value_size_bytes : kDefaultBytesPerValue;
     const uint64_t items = std::max<uint64_t>(1, cfg_.capacity_bytes / per_value);  // cache.rs:39-42
@@ -176,70 +183,110 @@ Storage::~Storage() {
   if (pre_evict_.joinable()) pre_evict_.join();
 }
 
-std::shared_ptr<PoolAllocation> Storage::allocate(uint64_t size) {
+std::shared_ptr<PoolAllocation> Storage::allocate(uint64_t size, size_t pool) {
   // The allocator succeeds exactly when its largest-free report covers the
   // request, so the retry below is taken at most once per reclaim that freed
   // something; a retry that frees nothing ends the loop (the reference would
   // spin if the allocator ran out of nodes).
+  pool = std::min(pool, pools_.size() - 1);
+  PinnedPool& p = *pools_[pool];
   for (;;) {
-    if (auto a = pool_->allocate(size)) return a;
+    if (auto a = p.allocate(size)) return a;
     uint64_t freed = 0;
-    reclaim_until_fits(size, &freed);
-    if (pool_->largest_free() >= size && freed > 0) continue;
-    if (pool_->largest_free() >= size) {
-      if (auto a = pool_->allocate(size)) return a;
+    reclaim_until_fits(size, pool, &freed);
+    if (p.largest_free() >= size && freed > 0) continue;
+    if (p.largest_free() >= size) {
+      if (auto a = p.allocate(size)) return a;
     }
     counters_.pool_alloc_failures.fetch_add(1);
     return nullptr;
   }
 }
 
-void Storage::reclaim_until_fits(uint64_t required, uint64_t* freed_blocks) {
+bool Storage::holds_memory_in(const SealedBlock& b, size_t pool) const {
+  // A slot's K and V come from one save call on one device, so one pool.
+  const PinnedPool& p = *pools_[pool];
+  for (const LayerBlockPtr& s : b.slots) {
+    if (s && p.contains(s->k_ptr)) return true;
+  }
+  return false;
+}
+
+std::vector<SealedBlockPtr> Storage::evict_lru(uint64_t max_blocks, uint64_t bytes, size_t pool) {
+  std::vector<SealedBlockPtr> out;
+  const bool any = pools_.size() == 1;
+  uint64_t freed = 0;
+  std::lock_guard<std::mutex> g(cache_mu_);
+  for (auto it = lru_.begin(); it != lru_.end() && out.size() < max_blocks && freed < bytes;) {
+    if (!any && !holds_memory_in(*it->second, pool)) {
+      ++it;
+      continue;
+    }
+    freed += it->second->footprint;
+    out.push_back(std::move(it->second));
+    index_.erase(it->first);
+    it = lru_.erase(it);
+  }
+  return out;  // dropped by the caller outside the cache lock: frees pool memory
+}
+
+void Storage::reclaim_until_fits(uint64_t required, size_t pool, uint64_t* freed_blocks) {
   // reclaim_until_allocator_can_allocate (storage.rs:565-608)
   *freed_blocks = 0;
   if (required == 0) return;
-  while (pool_->largest_free() < required) {
-    std::vector<SealedBlockPtr> evicted;
-    {
-      std::lock_guard<std::mutex> g(cache_mu_);
-      for (uint64_t i = 0; i < kReclaimBatch && !lru_.empty(); ++i) {
-        evicted.push_back(std::move(lru_.front().second));
-        index_.erase(lru_.front().first);
-        lru_.pop_front();
-      }
-    }
+  while (pools_[pool]->largest_free() < required) {
+    std::vector<SealedBlockPtr> evicted = evict_lru(kReclaimBatch, UINT64_MAX, pool);
     if (evicted.empty()) break;
     *freed_blocks += evicted.size();
     counters_.evictions.fetch_add(evicted.size());
-    evicted.clear();  // drop outside the cache lock: frees pool memory
+    evicted.clear();
   }
 }
 
+void Storage::usage(uint64_t* used, uint64_t* total) {
+  uint64_t u = 0, t = 0;
+  for (const auto& p : pools_) {
+    uint64_t pu = 0, pt = 0;
+    p->usage(&pu, &pt);
+    u += pu;
+    t += pt;
+  }
+  *used = u;
+  *total = t;
+}
+
+uint64_t Storage::largest_free() {
+  uint64_t m = 0;
+  for (const auto& p : pools_) m = std::max(m, p->largest_free());
+  return m;
+}
+
 void Storage::pre_evict_loop() {
-  // pre_evict_monitor (storage.rs:646-686)
+  // pre_evict_monitor (storage.rs:646-686). With several pools each keeps
+  // its share (by size) of the threshold and target free.
   std::unique_lock<std::mutex> lk(stop_mu_);
   while (!stop_) {
     stop_cv_.wait_for(lk, std::chrono::milliseconds(cfg_.pre_evict_interval_ms));
     if (stop_) break;
     lk.unlock();
-    uint64_t used = 0, total = 0;
-    pool_->usage(&used, &total);
-    const uint64_t free_bytes = total > used ? total - used : 0;
-    if (free_bytes < cfg_.pre_evict_threshold_bytes) {
-      const uint64_t need = cfg_.pre_evict_target_bytes > free_bytes ? cfg_.pre_evict_target_bytes - free_bytes : 0;
-      std::vector<SealedBlockPtr> evicted;
-      uint64_t freed = 0;
-      {
-        std::lock_guard<std::mutex> g(cache_mu_);
-        while (freed < need && !lru_.empty()) {
-          freed += lru_.front().second->footprint;
-          evicted.push_back(std::move(lru_.front().second));
-          index_.erase(lru_.front().first);
-          lru_.pop_front();
-        }
+    uint64_t all_used = 0, all_total = 0;
+    usage(&all_used, &all_total);
+    for (size_t i = 0; i < pools_.size(); ++i) {
+      uint64_t used = 0, total = 0;
+      pools_[i]->usage(&used, &total);
+      uint64_t threshold = cfg_.pre_evict_threshold_bytes, target = cfg_.pre_evict_target_bytes;
+      if (pools_.size() > 1 && all_total > 0) {
+        const double share = static_cast<double>(total) / static_cast<double>(all_total);
+        threshold = static_cast<uint64_t>(static_cast<double>(threshold) * share);
+        target = static_cast<uint64_t>(static_cast<double>(target) * share);
       }
-      counters_.evictions.fetch_add(evicted.size());
-      evicted.clear();
+      const uint64_t free_bytes = total > used ? total - used : 0;
+      if (free_bytes < threshold) {
+        const uint64_t need = target > free_bytes ? target - free_bytes : 0;
+        std::vector<SealedBlockPtr> evicted = evict_lru(UINT64_MAX, need, i);
+        counters_.evictions.fetch_add(evicted.size());
+        evicted.clear();
+      }
     }
     lk.lock();
   }

@@ -8,6 +8,7 @@
 // LayerBlock sharing it is dropped.
 #pragma once
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <condition_variable>
@@ -40,13 +41,19 @@ class PinnedPool : public std::enable_shared_from_this<PinnedPool> {
  public:
   // PinnedMemoryPool::new (pinned_pool.rs:67-113). The allocator unit is
   // max(reference unit, 64 B) so every allocation starts 64-byte aligned.
+  // numa_node >= 0 places the pool's pages on that node (PinnedMemory).
   static std::shared_ptr<PinnedPool> create(uint64_t bytes, PinKind kind, bool write_combined,
-                                            uint64_t unit_hint);
+                                            uint64_t unit_hint, int numa_node = -1);
   std::shared_ptr<PoolAllocation> allocate(uint64_t size);  // null when it cannot fit
   void usage(uint64_t* used, uint64_t* total);
   uint64_t largest_free();
   uint8_t* base() const { return mem_->data(); }
   PinKind kind() const { return mem_->kind(); }
+  const PinnedMemory& memory() const { return *mem_; }
+  bool contains(const void* p) const {
+    const uint8_t* q = static_cast<const uint8_t*>(p);
+    return q >= mem_->data() && q < mem_->data() + mem_->size();
+  }
   void free_internal(const ScaledOffsetAllocator::Allocation& a);
 
  private:
@@ -153,11 +160,16 @@ class TinyLfu {
 class Storage {
  public:
   Storage(std::shared_ptr<PinnedPool> pool, const StorageConfig& cfg);
+  // Several pools (one per NUMA node, say): every allocation names its pool,
+  // and reclaim for a pool evicts, in LRU order, only the cached blocks that
+  // hold memory in that pool. With one pool this is the reference's storage.
+  Storage(std::vector<std::shared_ptr<PinnedPool>> pools, const StorageConfig& cfg);
   ~Storage();
 
   // StorageEngine::allocate (storage.rs:405-433): evicts LRU blocks until the
-  // allocator reports a large enough free region.
-  std::shared_ptr<PoolAllocation> allocate(uint64_t size);
+  // allocator reports a large enough free region. `pool` indexes the pools
+  // (out-of-range values use the last one).
+  std::shared_ptr<PoolAllocation> allocate(uint64_t size, size_t pool = 0);
   bool inflight_has_slot(const std::string& ns, const std::string& hash, uint64_t slot);
   // The save-side dedup answer, !cache_contains && !inflight_has_slot, for
   // every (hash, slot) of one hash list, from one cache and one inflight
@@ -202,11 +214,19 @@ class Storage {
   BlockView cache_view();
   BlockView inflight_view();
   StorageCounters& counters() { return counters_; }
-  PinnedPool& pool() { return *pool_; }
+  PinnedPool& pool(size_t i = 0) { return *pools_[std::min(i, pools_.size() - 1)]; }
+  size_t pool_count() const { return pools_.size(); }
+  // Totals over all pools; largest_free is the largest of the pools'.
+  void usage(uint64_t* used, uint64_t* total);
+  uint64_t largest_free();
 
  private:
   bool cache_insert_locked(const BlockKey& key, SealedBlockPtr block);  // TinyLFU admission
-  void reclaim_until_fits(uint64_t required, uint64_t* freed_blocks);
+  void reclaim_until_fits(uint64_t required, size_t pool, uint64_t* freed_blocks);
+  // Evicts cached blocks in LRU order until `bytes` of footprint are gone,
+  // taking only blocks that hold memory in `pool` when there are several.
+  std::vector<SealedBlockPtr> evict_lru(uint64_t max_blocks, uint64_t bytes, size_t pool);
+  bool holds_memory_in(const SealedBlock& b, size_t pool) const;
   void pre_evict_loop();
 
   struct Inflight {
@@ -222,7 +242,7 @@ class Storage {
   std::atomic<int64_t> last_sweep_ns_{0};
   using LruList = std::list<std::pair<BlockKey, SealedBlockPtr>>;
 
-  std::shared_ptr<PinnedPool> pool_;
+  std::vector<std::shared_ptr<PinnedPool>> pools_;
   StorageConfig cfg_;
   std::mutex inflight_mu_;
   std::unordered_map<BlockKey, Inflight, BlockKeyHash> inflight_;

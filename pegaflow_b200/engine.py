@@ -43,12 +43,22 @@ class PegaEngine:
         dfs_quota: int = 0,
         dfs_scan_interval_ms: int = 0,
         dfs_max_pack_size: int = 0,
+        numa_pools: str = "off",
     ):
         """``dfs_root`` turns on the packed-file tier: sealed blocks are
         written through to ``{dfs_root}/{namespace}/{uuid}.bin`` and read
-        back when ``query_prefetch`` finds them missing from the pool."""
+        back when ``query_prefetch`` finds them missing from the pool.
+
+        ``numa_pools`` splits the pool for an engine that drives several
+        GPUs: "off" (one pool, the default), "node" (one pool per NUMA node of
+        the visible GPUs) or "device" (one pool per GPU). Each pool sits on
+        its GPUs' NUMA node, and a save allocates from its GPU's pool."""
+        modes = {"off": 0, "node": 1, "device": 2}
+        if numa_pools not in modes:
+            raise ValueError(f"numa_pools must be one of {sorted(modes)}, not {numa_pools!r}")
         cfg = N.EngineConfig()
         N.lib.pf_engine_config_default(byref(cfg))
+        cfg.numa_pools = modes[numa_pools]
         cfg.pool_bytes = pool_size
         cfg.use_hugepages = 1 if use_hugepages else 0
         cfg.write_combined = 1 if write_combined else 0

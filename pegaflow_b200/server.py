@@ -262,6 +262,9 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--pre-evict-target", type=parse_memory_size, default=parse_memory_size("8gb"))
     ap.add_argument("--pre-evict-interval-ms", type=int, default=100)
     ap.add_argument("--disable-lfu-admission", action="store_true")
+    ap.add_argument("--numa-pools", choices=["off", "node", "device"], default="off",
+                    help="split the pool per NUMA node of the GPUs (or per GPU), each part on its GPUs' node; "
+                         "a save allocates from its GPU's part (not a reference flag)")
     ap.add_argument("--metrics-otel-endpoint", default="http://127.0.0.1:4321")
     ap.add_argument("--metrics-period-secs", type=int, default=5)
     ap.add_argument("--log-level", default="info")
@@ -293,7 +296,8 @@ def main(argv=None) -> int:
     dfs = dict(dfs_root=args.dfs_root, dfs_quota=args.dfs_quota,
                dfs_scan_interval_ms=args.dfs_scan_interval_ms) if args.dfs_local_index else {}
     engine = PegaEngine(args.pool_size, args.use_hugepages, enable_lfu_admission=not args.disable_lfu_admission,
-                        hint_value_size_bytes=args.hint_value_size or 0, pre_evict=pre_evict, **dfs)
+                        hint_value_size_bytes=args.hint_value_size or 0, pre_evict=pre_evict,
+                        numa_pools=args.numa_pools, **dfs)
     server, _, port = serve(engine, args.addr)
     log.info("pegaflow_b200 engine server listening on %s (port %d)", args.addr, port)
     server.wait_for_termination()

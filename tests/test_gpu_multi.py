@@ -107,3 +107,50 @@ def test_pool_is_pinned_for_every_device(cuda):
     Executor(1, load_mode="direct").load([LoadSpec(Layout.from_tensor(dst), np.arange(64) + 10, ks, ks + 64 * 32768)])
     torch.cuda.synchronize(1)
     assert torch.equal(dst[:, 10:74].cpu(), src[:, :64].cpu())
+
+
+def test_device_pools_keep_each_gpus_blocks(cuda):
+    """numa_pools="device": one pool per GPU. Filling GPU 1's pool evicts
+    GPU 1's oldest blocks and never GPU 0's, which a single shared pool of
+    the same total size would evict first (they are the least recently
+    used). Bytes restored from either pool are the saved ones."""
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from pegaflow_b200 import Layout, PegaEngine, PyLoadState
+
+    block = 16 * 8 * 128 * 2  # one K or V segment of a [2, nb, 16, 8, 128] bf16 layer
+    per_dev = 64 * 2 * block  # room for 64 blocks of one layer per GPU
+
+    def run(mode):
+        e = PegaEngine(2 * per_dev, enable_lfu_admission=False, numa_pools=mode)
+        ts = {}
+        for d in (0, 1):
+            t = kv(torch, (2, 256, 16, 8, 128), 40 + d, f"cuda:{d}")
+            lay = Layout.from_tensor(t)
+            e.register_context_layer(f"i{d}", f"ns{d}", d, "L0", lay.data_ptr, lay.size_bytes, lay.num_blocks,
+                                     lay.bytes_per_block, lay.kv_stride_bytes, lay.segments, 0, 1, 1)
+            ts[d] = t
+        old = [f"d0-{i}".encode() for i in range(32)]
+        e.batch_save_kv_blocks("i0", 0, 0, [("L0", list(range(32)), old)])
+        for k in range(6):  # 6 x 32 blocks on GPU 1: more than its pool holds
+            hs = [f"d1-{k}-{i}".encode() for i in range(32)]
+            e.batch_save_kv_blocks("i1", 0, 1, [("L0", list(range(32)), hs)])
+        hit0 = e.count_prefix_hit_blocks("i0", old)
+        if mode == "device":  # restore GPU 0's blocks elsewhere and compare
+            s = PyLoadState()
+            e.batch_load_kv_blocks("i0", 0, 0, s.shm_name(), ["L0"], list(range(100, 132)), old)
+            deadline = time.time() + 60
+            while not s.is_ready():
+                assert time.time() < deadline
+            assert s.get_state() == 1
+            torch.cuda.synchronize(0)
+            assert torch.equal(ts[0][:, 100:132], ts[0][:, 0:32])
+        m = e.metrics()
+        e.close()
+        return hit0, m["cache_block_evictions"]
+
+    hit_dev, ev_dev = run("device")
+    hit_one, ev_one = run("off")
+    assert hit_dev == 32 and ev_dev > 0  # GPU 1 evicted its own blocks only
+    assert hit_one == 0 and ev_one > 0   # one pool: GPU 0's older blocks went first
