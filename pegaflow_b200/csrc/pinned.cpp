@@ -113,6 +113,10 @@ PinnedMemory::PinnedMemory(size_t size, PinKind kind, bool write_combined, int n
     void* p = mmap(nullptr, aligned, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
     if (p == MAP_FAILED) throw cuda_init("mmap failed for a pool on NUMA node " + std::to_string(numa_node));
     numa_bound_ = bind_to_node(p, aligned, numa_node);
+    if (!numa_bound_) {
+      fprintf(stderr, "pegaflow_b200: mbind to NUMA node %d refused (errno %d); pool pages are not placed\n",
+              numa_node, errno);
+    }
     ptr_ = static_cast<uint8_t*>(p);
     size_ = aligned;
     mapped_ = true;
