@@ -3,6 +3,8 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <string_view>
+#include <unordered_set>
 
 #include "common.h"
 
@@ -448,12 +450,29 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
         }
       }
     }
-    std::unordered_map<std::string, bool> sealed_here;  // a repeated hash finds its block sealed
+    std::unordered_set<std::string_view> sealed_here;  // a repeated hash finds its block sealed
+    sealed_here.reserve(n);
+    seals.reserve(n);
+    // Every slot filled by this call: a hash with no inflight block seals at
+    // the last fill, so its block is built directly, without an inflight
+    // entry that would be created and erased at once.
+    const bool all_slots = fills.size() == total_slots;
     for (size_t i = 0; i < n; ++i) {
       if (cached[i]) continue;
       if (!sealed_here.empty() && sealed_here.count(hashes[i])) continue;
       key.hash = hashes[i];
       auto it = inflight_.find(key);
+      if (it == inflight_.end() && all_slots) {
+        auto sb = std::make_shared<SealedBlock>();
+        sb->slots.resize(total_slots);
+        for (const SlotFill& f : fills) {
+          sb->footprint += f.batch->blocks[i].size;
+          sb->slots[f.slot] = layer_block_at(f.batch, i);
+        }
+        sealed_here.insert(hashes[i]);
+        seals.push_back({fills.size() - 1, i, key, std::move(sb)});
+        continue;
+      }
       if (it == inflight_.end()) {
         Inflight fresh;
         fresh.slots.assign(total_slots, nullptr);
@@ -472,7 +491,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
           sb->slots = std::move(ib.slots);
           sb->footprint = ib.footprint;
           inflight_.erase(it);
-          sealed_here[hashes[i]] = true;
+          sealed_here.insert(hashes[i]);
           seals.push_back({f, i, key, std::move(sb)});
           break;
         }
@@ -480,20 +499,32 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
     }
   }
   if (seals.empty()) return;
-  std::stable_sort(seals.begin(), seals.end(), [](const Seal& a, const Seal& b) { return a.fill < b.fill; });
-  for (const Seal& s : seals) notify_sealed(s.key, s.block);
+  auto by_fill = [](const Seal& a, const Seal& b) { return a.fill < b.fill; };
+  if (!std::is_sorted(seals.begin(), seals.end(), by_fill)) std::stable_sort(seals.begin(), seals.end(), by_fill);
+  SealListener listener;
+  {
+    std::lock_guard<std::mutex> g(listener_mu_);
+    listener = seal_listener_;
+  }
+  if (listener) {
+    for (const Seal& s : seals) listener(s.key, s.block);
+  }
   std::vector<const Seal*> refused;
+  uint64_t inserted = 0, rejected = 0;
   {
     std::lock_guard<std::mutex> g(cache_mu_);
     for (Seal& s : seals) {
+      // The key stays with the seal: a refused block restarts inflight below.
       if (cache_insert_locked(s.key, std::move(s.block))) {
-        counters_.insertions.fetch_add(1);
+        ++inserted;
       } else {
-        counters_.admission_rejections.fetch_add(1);
+        ++rejected;
         if (s.fill + 1 < fills.size()) refused.push_back(&s);
       }
     }
   }
+  counters_.insertions.fetch_add(inserted);
+  counters_.admission_rejections.fetch_add(rejected);
   if (refused.empty()) return;
   std::lock_guard<std::mutex> gi(inflight_mu_);
   for (const Seal* s : refused) {
@@ -529,7 +560,7 @@ bool Storage::cache_insert_locked(const BlockKey& key, SealedBlockPtr block) {
     if (lfu_->get(key) < lfu_->get(lru_.front().first)) return false;
   }
   lru_.emplace_back(key, std::move(block));
-  index_[key] = std::prev(lru_.end());
+  index_.emplace_hint(it, lru_.back().first, std::prev(lru_.end()));
   return true;
 }
 
