@@ -23,6 +23,21 @@ def test_parse_memory_size_basic():
     assert parse_memory_size(" 2 tb ") == 2 << 40
 
 
+def test_server_flags():
+    """The reference server's flags (pegaflow-server/src/lib.rs:43-113) plus
+    --numa-pools, with their defaults."""
+    from pegaflow_b200.server import build_parser
+
+    a = build_parser().parse_args([])
+    assert (a.pool_size, a.numa_pools, a.disable_lfu_admission, a.dfs_local_index) == (30 << 30, "off", False, False)
+    a = build_parser().parse_args(["--pool-size", "2gb", "--numa-pools", "device", "--pre-evict",
+                                   "--dfs-local-index", "--dfs-root", "/x", "--dfs-quota", "1gb"])
+    assert (a.pool_size, a.numa_pools, a.pre_evict, a.dfs_root, a.dfs_quota) == (2 << 30, "device", True, "/x",
+                                                                                  1 << 30)
+    with pytest.raises(SystemExit):
+        build_parser().parse_args(["--numa-pools", "socket"])
+
+
 def test_parse_memory_size_invalid():
     from pegaflow_b200.server import parse_memory_size
 
