@@ -9,6 +9,7 @@
 #include <utility>
 #include <vector>
 
+#include "chunks.h"
 #include "pegaflow.h"
 #include "plan.h"
 
@@ -76,10 +77,6 @@ class Executor {
     uint64_t dense;
     uint64_t host;
     uint64_t bytes;
-  };
-  struct Chunk {
-    uint64_t tile_begin, tile_end;
-    uint64_t dense_begin, dense_end;
   };
   // A load layer whose destination blocks share bytes: copied in list order.
   struct SerialLoad {

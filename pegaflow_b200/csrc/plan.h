@@ -20,6 +20,8 @@
 // per tile, so a 4 KiB TP-8 segment and a 64 KiB block both run full width.
 #pragma once
 
+#include <cuda_runtime.h>
+
 #include <cstdint>
 
 namespace pf {

@@ -1,0 +1,134 @@
+// The staging-chunk cutter (pegaflow_b200/csrc/chunks.cpp) on random plans
+// and on the schedules the benchmark uses. Each chunk is relocated into one
+// staging slot by a kernel launch and drained or filled by copy-engine
+// copies, so the invariants below keep those inside the slot:
+//   - the chunks tile the plan: contiguous, non-empty, ending at total_tiles;
+//   - every chunk starts on a kDenseAlign boundary and spans at most a slot;
+//   - every tile's dense bytes lie inside its chunk's [dense_begin, dense_end);
+//   - chunk k spans at most limit_k: the first limit (clamped to [2 tiles,
+//     slot]) doubled k times, up to the slot.
+//
+// Build and run (tests/test_chunks.py does this):
+//   g++ -O1 -std=c++17 -I<repo>/pegaflow_b200/csrc -I<cuda>/include
+//       tests/chunks_test.cpp <csrc>/chunks.cpp
+//   ./chunks_test
+#include <algorithm>
+#include <cstdio>
+#include <random>
+#include <vector>
+
+#include "chunks.h"
+
+using namespace pf;
+
+namespace {
+
+struct Case {
+  std::vector<PlanLayer> layers;
+  uint64_t total_tiles = 0;
+};
+
+Case make_case(const std::vector<std::pair<uint32_t, uint32_t>>& unit_bytes_and_units, uint32_t n) {
+  Case c;
+  for (auto [ub, units] : unit_bytes_and_units) {
+    PlanLayer p{};
+    p.unit_bytes = ub;
+    p.units = units;
+    p.n = n;
+    p.tiles_per_unit = (ub + kTileBytes - 1) / kTileBytes;
+    p.tile_start = c.total_tiles;
+    p.tile_count = static_cast<uint64_t>(units) * n * p.tiles_per_unit;
+    c.total_tiles += p.tile_count;
+    c.layers.push_back(p);
+  }
+  return c;
+}
+
+// Returns an empty string when every invariant holds.
+const char* check(const Case& c, uint64_t slot, uint64_t first, const std::vector<Chunk>& ch) {
+  if (ch.empty()) return "no chunks";
+  if (ch.front().tile_begin != 0 || ch.back().tile_end != c.total_tiles) return "chunks do not span the plan";
+  uint64_t limit = std::min(slot, std::max<uint64_t>(first, 2 * kTileBytes));
+  for (size_t k = 0; k < ch.size(); ++k) {
+    if (ch[k].tile_end <= ch[k].tile_begin) return "empty chunk";
+    if (k + 1 < ch.size() && ch[k].tile_end != ch[k + 1].tile_begin) return "chunks not contiguous";
+    if (ch[k].dense_begin % kDenseAlign) return "chunk start not aligned";
+    if (ch[k].dense_end < ch[k].dense_begin || ch[k].dense_end - ch[k].dense_begin > limit) return "chunk over its limit";
+    if (limit > slot) return "limit above the slot";
+    limit = std::min(slot, limit * 2);
+  }
+  // Every tile's dense bytes inside its chunk.
+  size_t k = 0;
+  uint64_t dense = 0;
+  for (const PlanLayer& p : c.layers) {
+    dense = align_up(dense, kDenseAlign);
+    for (uint64_t t = 0; t < p.tile_count; ++t) {
+      const uint64_t tile = p.tile_start + t;
+      while (k < ch.size() && tile >= ch[k].tile_end) ++k;
+      if (k == ch.size() || tile < ch[k].tile_begin) return "tile outside every chunk";
+      const uint64_t ul = t / p.tiles_per_unit, tt = t % p.tiles_per_unit;
+      const uint64_t d0 = dense + ul * p.unit_bytes + tt * kTileBytes;
+      const uint64_t d1 = std::min<uint64_t>(d0 + kTileBytes, dense + (ul + 1) * p.unit_bytes);
+      if (d0 < ch[k].dense_begin || d1 > ch[k].dense_end) return "tile bytes outside its chunk";
+    }
+    dense += static_cast<uint64_t>(p.units) * p.n * p.unit_bytes;
+  }
+  return "";
+}
+
+std::vector<uint64_t> spans_mib(const std::vector<Chunk>& ch) {
+  std::vector<uint64_t> out;
+  for (const Chunk& c : ch) out.push_back((c.dense_end - c.dense_begin) >> 20);
+  return out;
+}
+
+}  // namespace
+
+int main() {
+  std::mt19937_64 rng(7);
+  const uint32_t sizes[] = {3, 4, 12, 45, 4096, 8192, 16384, 24576, 32768, 65536, 100000};
+  long cases = 0;
+  for (int it = 0; it < 50000; ++it) {
+    std::vector<std::pair<uint32_t, uint32_t>> spec;
+    const int nl = 1 + static_cast<int>(rng() % 6);
+    for (int i = 0; i < nl; ++i) spec.push_back({sizes[rng() % 11], 1 + static_cast<uint32_t>(rng() % 2)});
+    const Case c = make_case(spec, 1 + static_cast<uint32_t>(rng() % 50));
+    const uint64_t slot = align_up(std::max<uint64_t>(2 * kTileBytes, 1 + rng() % (1 << 22)), kDenseAlign);
+    const uint64_t first = rng() % (1 << 21);
+    std::vector<Chunk> ch;
+    cut_chunks(c.layers, c.total_tiles, slot, first, &ch);
+    const char* why = check(c, slot, first, ch);
+    if (*why) {
+      std::printf("FAIL case %d: %s\n", it, why);
+      return 1;
+    }
+    ++cases;
+  }
+
+  // The benchmark's schedules for one 1.25 GiB direction: 32 layers of 640
+  // blocks x (K, V) x 32 KiB, 512 MiB slots.
+  const Case llama = make_case(std::vector<std::pair<uint32_t, uint32_t>>(32, {32768, 2}), 640);
+  const uint64_t slot = 512ull << 20;
+  struct Want {
+    uint64_t first;
+    std::vector<uint64_t> mib;
+  };
+  const Want wants[] = {
+      {64ull << 20, {64, 128, 256, 512, 320}},     // growth from 64 MiB
+      {slot, {512, 512, 256}},                      // loads without per-layer flags: whole slots
+      {slot / 2, {256, 512, 512}},                  // saves: half a slot first
+      {40ull << 20, {40, 80, 160, 320, 512, 168}},  // a layer-wise load: first chunk = one 40 MiB layer
+  };
+  for (const Want& w : wants) {
+    std::vector<Chunk> ch;
+    cut_chunks(llama.layers, llama.total_tiles, slot, w.first, &ch);
+    if (*check(llama, slot, w.first, ch) || spans_mib(ch) != w.mib) {
+      std::printf("FAIL schedule with first chunk %llu MiB:", static_cast<unsigned long long>(w.first >> 20));
+      for (uint64_t m : spans_mib(ch)) std::printf(" %llu", static_cast<unsigned long long>(m));
+      std::printf("\n");
+      return 1;
+    }
+  }
+  std::printf("ok %ld random plans\n", cases);
+  return 0;
+}
