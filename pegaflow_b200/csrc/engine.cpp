@@ -353,7 +353,8 @@ std::shared_ptr<InstanceContext> Engine::get_or_create_instance(const std::strin
 
 std::shared_ptr<GpuContext> Engine::ensure_gpu(InstanceContext& inst, int device_id) {
   // InstanceContext::ensure_gpu (lib.rs:221-252). Workers are shared by all
-  // instances on a device (one executor and staging ring per GPU).
+  // instances on a device (one executor per GPU, with a save lane and a load
+  // lane).
   if (device_id < 0) throw invalid_argument("device_id " + std::to_string(device_id) + " must be >= 0");
   {
     std::shared_lock<std::shared_mutex> g(inst.gpu_mu);

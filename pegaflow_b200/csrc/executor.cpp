@@ -4,8 +4,11 @@
 // Load (staged):  H2D DMA -> HBM slot  ==event==>  unpack kernel -> paged KV
 // Slots form a ring; a slot is refilled only after the consumer of its last
 // contents has finished (ev_drained). Several copy streams keep more than one
-// DMA in flight on the host link. Direct mode skips the ring: the kernel
-// reads/writes mapped pinned host memory itself.
+// DMA in flight on the host link. Saves and loads each have a lane of their
+// own (streams, ring, plan buffers, host lock), so the two directions of the
+// link are used at once. Direct mode skips the ring: the kernel reads/writes
+// mapped pinned host memory itself. The chunks a transfer moves through the
+// ring are cut by cut_chunks (chunks.cpp).
 #include "executor.h"
 
 #include <algorithm>
