@@ -60,4 +60,15 @@ void cut_chunks(const std::vector<PlanLayer>& layers, uint64_t total_tiles, uint
   chunks->push_back({cur_tb, total_tiles, cur_db, last_end});
 }
 
+uint64_t layerwise_first_limit(const std::vector<PlanLayer>& layers, uint64_t first_chunk, uint64_t min_first) {
+  if (layers.empty()) return first_chunk;
+  auto layer_bytes = [](const PlanLayer& p) { return static_cast<uint64_t>(p.units) * p.n * p.unit_bytes; };
+  const uint64_t layer0 = layer_bytes(layers[0]);
+  uint64_t span = align_up(layer0, kDenseAlign);  // dense bytes, as the chunks count them
+  for (size_t i = 1; i < layers.size() && layer_bytes(layers[i]) * 8 <= layer0; ++i) {
+    span += align_up(layer_bytes(layers[i]), kDenseAlign);
+  }
+  return std::min(first_chunk, std::max(min_first, span));
+}
+
 }  // namespace pf

@@ -33,4 +33,10 @@ struct Chunk {
 void cut_chunks(const std::vector<PlanLayer>& layers, uint64_t total_tiles, uint64_t slot_bytes,
                 uint64_t first_limit, std::vector<Chunk>* chunks);
 
+// First-chunk limit for a load that raises per-layer flags: the dense span of
+// layer 0 and of the layers listed right after it that are at most an eighth
+// of its size (per-block scales beside their KV), so the first chunk ends
+// where those layers end; at least min_first, at most first_chunk.
+uint64_t layerwise_first_limit(const std::vector<PlanLayer>& layers, uint64_t first_chunk, uint64_t min_first);
+
 }  // namespace pf

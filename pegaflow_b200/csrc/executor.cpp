@@ -1053,16 +1053,8 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
     // cost of tens of microseconds while DMA streams), and the remainder,
     // the smallest chunk, comes last, where its unpack is the only work
     // left after the final DMA.
-    uint64_t first = layer_done ? first_chunk_ : slot_bytes_;
-    if (layer_done && !b.layers.empty()) {
-      auto layer_bytes = [](const PlanLayer& p) { return static_cast<uint64_t>(p.units) * p.n * p.unit_bytes; };
-      const uint64_t layer0 = layer_bytes(b.layers[0]);
-      uint64_t span = align_up(layer0, kDenseAlign);  // dense bytes, as the chunks count them
-      for (size_t i = 1; i < b.layers.size() && layer_bytes(b.layers[i]) * 8 <= layer0; ++i) {
-        span += align_up(layer_bytes(b.layers[i]), kDenseAlign);
-      }
-      first = std::min(first, std::max<uint64_t>(kLayerwiseMinFirstChunk, span));
-    }
+    const uint64_t first = layer_done ? layerwise_first_limit(b.layers, first_chunk_, kLayerwiseMinFirstChunk)
+                                      : slot_bytes_;
     std::vector<Chunk> chunks;
     make_chunks(b, first, &chunks);
     for (size_t k = 0; k < chunks.size(); ++k) {

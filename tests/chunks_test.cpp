@@ -129,6 +129,48 @@ int main() {
       return 1;
     }
   }
+  // Layer-wise loads: the first chunk ends where layer 0 (and the small
+  // layers right after it) end, so layer 0's flags rise after chunk 0.
+  const uint64_t kMin = 4ull << 20, kFirst = 64ull << 20;
+  {
+    // fp8 KV ([2, nb, 16, 8, 128] uint8: K and V units of 16 KiB) interleaved
+    // with its fp32 per-block scales (4-byte units), 265 blocks per layer.
+    std::vector<std::pair<uint32_t, uint32_t>> spec;
+    for (int l = 0; l < 32; ++l) {
+      spec.push_back({16384, 2});
+      spec.push_back({4, 1});
+    }
+    const Case fp8 = make_case(spec, 265);
+    const uint64_t first = layerwise_first_limit(fp8.layers, kFirst, kMin);
+    std::vector<Chunk> ch;
+    cut_chunks(fp8.layers, fp8.total_tiles, slot, first, &ch);
+    if (*check(fp8, slot, first, ch) || ch[0].tile_end != fp8.layers[2].tile_start) {
+      std::printf("FAIL fp8 first chunk: limit %llu, ends at tile %llu, layer 1 of KV starts at %llu\n",
+                  static_cast<unsigned long long>(first), static_cast<unsigned long long>(ch[0].tile_end),
+                  static_cast<unsigned long long>(fp8.layers[2].tile_start));
+      return 1;
+    }
+  }
+  {
+    const uint64_t first = layerwise_first_limit(llama.layers, kFirst, kMin);  // one 40 MiB layer
+    std::vector<Chunk> ch;
+    cut_chunks(llama.layers, llama.total_tiles, slot, first, &ch);
+    if (first != (40ull << 20) || ch[0].tile_end != llama.layers[1].tile_start) {
+      std::printf("FAIL llama first chunk %llu\n", static_cast<unsigned long long>(first));
+      return 1;
+    }
+  }
+  {
+    // Layers of 1.5 MiB: the 4 MiB floor applies; a cap below the layer wins.
+    const Case small = make_case(std::vector<std::pair<uint32_t, uint32_t>>(24, {24576, 1}), 64);
+    if (layerwise_first_limit(small.layers, kFirst, kMin) != kMin ||
+        layerwise_first_limit(llama.layers, 8ull << 20, kMin) != (8ull << 20) ||
+        layerwise_first_limit({}, kFirst, kMin) != kFirst) {
+      std::printf("FAIL first-chunk floor or cap\n");
+      return 1;
+    }
+  }
+
   std::printf("ok %ld random plans\n", cases);
   return 0;
 }
