@@ -27,7 +27,22 @@ def test_binding_covers_header(native):
 
 
 def test_abi_version(native):
-    assert native.lib.pf_abi_version() == 3
+    assert native.lib.pf_abi_version() == 3 == native.ABI_VERSION
+
+
+def test_config_defaults(native):
+    """Library defaults: the reference's 30 GiB write-combined pool with TinyLFU
+    admission (lib.rs:56, pinned_mem.rs:159, storage.rs:91), one pool (no NUMA
+    split), 2 x 512 MiB staging slots per lane."""
+    from ctypes import byref
+
+    e = native.EngineConfig()
+    native.lib.pf_engine_config_default(byref(e))
+    assert (e.pool_bytes, e.write_combined, e.enable_lfu_admission, e.numa_pools) == (30 << 30, 1, 1, 0)
+    assert (e.pre_evict_enabled, e.pre_evict_threshold_bytes, e.pre_evict_target_bytes) == (0, 5 << 30, 8 << 30)
+    x = native.ExecutorConfig()
+    native.lib.pf_executor_config_default(byref(x))
+    assert (x.staging_chunk_bytes, x.staging_slots, x.first_chunk_bytes) == (512 << 20, 2, 64 << 20)
 
 
 def test_library_is_sm100a_build(native):
