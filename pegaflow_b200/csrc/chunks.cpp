@@ -18,7 +18,7 @@ void cut_chunks(const std::vector<PlanLayer>& layers, uint64_t total_tiles, uint
   // to kDenseAlign so the slot shift (slot - dense_begin) keeps every
   // 16-byte-aligned dense address aligned, even when the chunk starts inside
   // a layer of unaligned units.
-  uint64_t cur_tb = 0, cur_db = 0, last_end = 0;
+  uint64_t cur_tb = 0, cur_db = 0, cur_df = 0, last_end = 0;
   uint64_t limit = std::min(slot_bytes, std::max<uint64_t>(first_limit, 2 * kTileBytes));
   bool first = true;
   uint64_t dense = 0;
@@ -31,6 +31,7 @@ void cut_chunks(const std::vector<PlanLayer>& layers, uint64_t total_tiles, uint
       const uint64_t ut = p.tile_start + ul * p.tiles_per_unit;
       if (first) {
         cur_tb = ut;
+        cur_df = ud;
         cur_db = ud / kDenseAlign * kDenseAlign;
         first = false;
       }
@@ -47,8 +48,9 @@ void cut_chunks(const std::vector<PlanLayer>& layers, uint64_t total_tiles, uint
         const uint64_t d0 = ud + static_cast<uint64_t>(t) * kTileBytes;
         const uint64_t d1 = std::min<uint64_t>(d0 + kTileBytes, ue);
         if (d1 - cur_db > limit) {
-          chunks->push_back({cur_tb, ut + t, cur_db, last_end});
+          chunks->push_back({cur_tb, ut + t, cur_db, last_end, cur_df});
           cur_tb = ut + t;
+          cur_df = d0;
           cur_db = d0 / kDenseAlign * kDenseAlign;
           limit = std::min(slot_bytes, limit * 2);
         }
@@ -57,7 +59,7 @@ void cut_chunks(const std::vector<PlanLayer>& layers, uint64_t total_tiles, uint
     }
     dense += nunits * p.unit_bytes;
   }
-  chunks->push_back({cur_tb, total_tiles, cur_db, last_end});
+  chunks->push_back({cur_tb, total_tiles, cur_db, last_end, cur_df});
 }
 
 uint64_t layerwise_first_limit(const std::vector<PlanLayer>& layers, uint64_t first_chunk, uint64_t min_first) {

@@ -18,10 +18,15 @@ constexpr uint64_t kDenseAlign = 256;
 
 inline uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
-// Tiles [tile_begin, tile_end) whose dense bytes lie in [dense_begin, dense_end).
+// Tiles [tile_begin, tile_end), whose dense bytes are [dense_first, dense_end).
+// dense_begin is dense_first rounded down to kDenseAlign: the chunk is placed
+// in a slot at (dense - dense_begin), which keeps 16-byte alignment, but the
+// bytes in [dense_begin, dense_first) belong to the previous chunk. Copies
+// between the slot and the host move [dense_first, dense_end) only.
 struct Chunk {
   uint64_t tile_begin, tile_end;
   uint64_t dense_begin, dense_end;
+  uint64_t dense_first;
 };
 
 // Cuts the plan's tiles, in order, into chunks whose dense span fits a limit

@@ -12,20 +12,9 @@
 #include "chunks.h"
 #include "pegaflow.h"
 #include "plan.h"
+#include "plan_build.h"
 
 namespace pf {
-
-// Geometry of one layer of a transfer, derived from its registration the
-// way the reference chooses its copy loop (gpu_worker.rs:218,326; transfer.rs:50-52).
-struct UnitGeometry {
-  uint32_t units;        // units per block
-  uint64_t unit_bytes;   // bytes per unit
-  uint64_t unit_stride;  // HBM distance between units of a block
-};
-UnitGeometry save_geometry(const pf_layer_desc& l);
-UnitGeometry load_geometry(const pf_layer_desc& l);
-bool is_split_layout(const pf_layer_desc& l);       // lib.rs:636
-bool is_contiguous_layout(const pf_layer_desc& l);  // transfer.rs:50-52
 
 // Staging defaults. While the copy engines stream a D2H/H2D, every kernel
 // launch on the device pays a fixed latency of tens of microseconds, so the
@@ -37,11 +26,6 @@ constexpr uint64_t kDefaultFirstChunkBytes = 64ull << 20;
 // Lower bound of a layer-wise load's first chunk (which holds layer 0 and
 // the small layers listed right after it).
 constexpr uint64_t kLayerwiseMinFirstChunk = 4ull << 20;
-
-// Layout checks of register_context_layer (lib.rs:389-449).
-void validate_layout(const pf_layer_desc& l, const char* layer_name);
-// transfer::segment_offset (transfer.rs:18-47).
-uint64_t segment_offset(const pf_layer_desc& l, uint64_t block_idx, uint64_t segment_idx);
 
 class Executor {
  public:
@@ -73,29 +57,7 @@ class Executor {
   void set_timing(bool on);
 
  private:
-  struct Run {  // one contiguous (dense offset, host address, bytes) extent
-    uint64_t dense;
-    uint64_t host;
-    uint64_t bytes;
-  };
-  // A load layer whose destination blocks share bytes: copied in list order.
-  struct SerialLoad {
-    pf_layer_desc layer;
-    uint32_t done_index;
-    std::vector<int64_t> ids;
-    std::vector<uint64_t> k, v;
-  };
-  struct Built {
-    std::vector<PlanLayer> layers;
-    std::vector<uint32_t> ids;
-    std::vector<uint64_t> side_base;
-    std::vector<uint64_t> side_ptrs;
-    std::vector<Run> runs;  // staged mode only
-    std::vector<SerialLoad> serial;
-    uint64_t total_tiles = 0;
-    uint64_t total_bytes = 0;
-  };
-
+  // Plans (plan_build.h) with this executor's device check.
   void build_save(const pf_save_layer* layers, uint64_t n, bool staged, Built* b);
   void build_load(const pf_load_layer* layers, uint64_t n, bool staged, Built* b);
   void build_p2p(const pf_p2p_layer* layers, uint64_t n, int peer, bool push, Built* b);

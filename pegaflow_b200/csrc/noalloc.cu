@@ -218,21 +218,24 @@ void save_noalloc(int device, const pf_save_layer* layers, uint64_t n_layers, cu
   // Chunks of whole tiles whose dense span fits the staging slot; each chunk
   // is packed, then drained by D2H copies, in order on the caller's stream.
   const uint64_t slot = kNoAllocStagingBytes;
-  auto flush = [&](uint64_t tb, uint64_t te, uint64_t db, uint64_t de) {
+  // db: the chunk's slot base (its first byte rounded down to kAlign); df: its
+  // first byte. Only [df, de) is copied out: the slot bytes before df were not
+  // packed by this chunk and would overwrite the previous chunk's last bytes.
+  auto flush = [&](uint64_t tb, uint64_t te, uint64_t db, uint64_t df, uint64_t de) {
     a.tile_begin = tb;
     a.tile_end = te;
     a.side_shift = static_cast<int64_t>(reinterpret_cast<uint64_t>(sc.staging)) - static_cast<int64_t>(db);
     const uint64_t grid = std::min<uint64_t>((te - tb + 7) / 8, static_cast<uint64_t>(sc.sms) * sc.ctas);
     cuda_check(launch_copy(kPack, false, a, static_cast<int>(std::max<uint64_t>(grid, 1)), stream), "kernel launch");
     for (const Extent& e : extents) {
-      const uint64_t lo = std::max(e.dense, db), hi = std::min(e.dense + e.bytes, de);
+      const uint64_t lo = std::max(e.dense, df), hi = std::min(e.dense + e.bytes, de);
       if (hi <= lo) continue;
       cuda_check(cudaMemcpyAsync(reinterpret_cast<void*>(e.host + (lo - e.dense)), sc.staging + (lo - db), hi - lo,
                                  cudaMemcpyDeviceToHost, stream),
                  "cudaMemcpyAsync D2H");
     }
   };
-  uint64_t cur_tb = 0, cur_db = 0, last_end = 0;
+  uint64_t cur_tb = 0, cur_db = 0, cur_df = 0, last_end = 0;
   bool first = true;
   uint64_t d = 0;
   for (const PlanLayer& p : table) {
@@ -243,6 +246,7 @@ void save_noalloc(int device, const pf_save_layer* layers, uint64_t n_layers, cu
       const uint64_t ut = p.tile_start + ul * p.tiles_per_unit;
       if (first) {
         cur_tb = ut;
+        cur_df = ud;
         cur_db = ud / kAlign * kAlign;
         first = false;
       }
@@ -254,8 +258,9 @@ void save_noalloc(int device, const pf_save_layer* layers, uint64_t n_layers, cu
         const uint64_t d0 = ud + static_cast<uint64_t>(t) * kTileBytes;
         const uint64_t d1 = std::min<uint64_t>(d0 + kTileBytes, ue);
         if (d1 - cur_db > slot) {
-          flush(cur_tb, ut + t, cur_db, last_end);
+          flush(cur_tb, ut + t, cur_db, cur_df, last_end);
           cur_tb = ut + t;
+          cur_df = d0;
           cur_db = d0 / kAlign * kAlign;
         }
         last_end = d1;
@@ -263,7 +268,7 @@ void save_noalloc(int device, const pf_save_layer* layers, uint64_t n_layers, cu
     }
     d += nunits * p.unit_bytes;
   }
-  flush(cur_tb, tiles, cur_db, last_end);
+  flush(cur_tb, tiles, cur_db, cur_df, last_end);
 }
 
 }  // namespace

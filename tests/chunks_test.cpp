@@ -3,8 +3,11 @@
 // staging slot by a kernel launch and drained or filled by copy-engine
 // copies, so the invariants below keep those inside the slot:
 //   - the chunks tile the plan: contiguous, non-empty, ending at total_tiles;
-//   - every chunk starts on a kDenseAlign boundary and spans at most a slot;
-//   - every tile's dense bytes lie inside its chunk's [dense_begin, dense_end);
+//   - every chunk's slot base is on a kDenseAlign boundary, less than one
+//     step before its first byte, and the chunk spans at most a slot;
+//   - every tile's dense bytes lie inside its chunk's [dense_first, dense_end),
+//     and those ranges never overlap between chunks (a copy of one chunk must
+//     not touch bytes another chunk moves);
 //   - chunk k spans at most limit_k: the first limit (clamped to [2 tiles,
 //     slot]) doubled k times, up to the slot.
 //
@@ -53,6 +56,12 @@ const char* check(const Case& c, uint64_t slot, uint64_t first, const std::vecto
     if (ch[k].tile_end <= ch[k].tile_begin) return "empty chunk";
     if (k + 1 < ch.size() && ch[k].tile_end != ch[k + 1].tile_begin) return "chunks not contiguous";
     if (ch[k].dense_begin % kDenseAlign) return "chunk start not aligned";
+    if (ch[k].dense_first < ch[k].dense_begin || ch[k].dense_first - ch[k].dense_begin >= kDenseAlign) {
+      return "first byte not within one alignment step of the slot base";
+    }
+    // The chunks' own byte ranges never overlap: a copy of chunk k+1 must not
+    // touch the bytes chunk k moves.
+    if (k + 1 < ch.size() && ch[k].dense_end > ch[k + 1].dense_first) return "chunk byte ranges overlap";
     if (ch[k].dense_end < ch[k].dense_begin || ch[k].dense_end - ch[k].dense_begin > limit) return "chunk over its limit";
     if (limit > slot) return "limit above the slot";
     limit = std::min(slot, limit * 2);
@@ -69,7 +78,7 @@ const char* check(const Case& c, uint64_t slot, uint64_t first, const std::vecto
       const uint64_t ul = t / p.tiles_per_unit, tt = t % p.tiles_per_unit;
       const uint64_t d0 = dense + ul * p.unit_bytes + tt * kTileBytes;
       const uint64_t d1 = std::min<uint64_t>(d0 + kTileBytes, dense + (ul + 1) * p.unit_bytes);
-      if (d0 < ch[k].dense_begin || d1 > ch[k].dense_end) return "tile bytes outside its chunk";
+      if (d0 < ch[k].dense_first || d1 > ch[k].dense_end) return "tile bytes outside its chunk";
     }
     dense += static_cast<uint64_t>(p.units) * p.n * p.unit_bytes;
   }

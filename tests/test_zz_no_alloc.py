@@ -103,3 +103,29 @@ def test_noalloc_refuses_a_plan_beyond_its_scratch(cuda, native):
     rc = save_noalloc(native, [spec], 0)
     assert rc == native.PF_ERR_INVALID_ARGUMENT
     assert "exceeds the no-allocation limit" in native.lib.pf_last_error().decode()
+
+
+def test_noalloc_save_of_unaligned_units_across_chunks(cuda, native, oracle):
+    """45-byte units (a [2, nb, 5, 9] uint8 layer) over three 8 MiB staging
+    chunks: chunk boundaries fall off the 256-byte slot alignment. Each chunk
+    copies out only its own bytes, so every boundary matches the oracle (the
+    copies once started at the aligned slot base and overwrote the previous
+    chunk's last bytes with stale slot bytes)."""
+    torch = cuda
+    from pegaflow_b200 import Layout, PinnedBuffer, SaveSpec
+
+    nb, n = 250_000, 200_000  # 2 x 200k x 45 B = 18 MB: three chunks
+    t = kv(torch, (2, nb, 5, 9), torch.uint8, 31)
+    lay = Layout.from_tensor(t)
+    assert lay.split and lay.bytes_per_block == 45
+    ids = np.random.default_rng(32).permutation(nb)[:n]
+    pool = PinnedBuffer(2 * n * 45)
+    pool.numpy()[:] = 0xAB
+    stream = torch.cuda.Stream()
+    native.check(save_noalloc(native, [SaveSpec(lay, ids, pool.ptr, pool.ptr + n * 45)], stream.cuda_stream))
+    stream.synchronize()
+    host = t.cpu().contiguous().view(-1).numpy()
+    ol = oracle.Layout(lay.size_bytes, lay.num_blocks, lay.bytes_per_block, lay.kv_stride_bytes, lay.segments)
+    k_ref, v_ref = oracle.np_save_layer(ol, host, ids)
+    np.testing.assert_array_equal(pool.numpy()[: n * 45], k_ref)
+    np.testing.assert_array_equal(pool.numpy()[n * 45:], v_ref)
