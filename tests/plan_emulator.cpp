@@ -8,6 +8,9 @@
 // unit sizes from 4 bytes to over 64 KiB; staged mode with small slots, and
 // direct mode; repeated destination ids; and layouts whose blocks share
 // bytes (the ordered-copy path).
+// Peer copies (plan_p2p, the P/D handoff) are replayed too, as pulls and as
+// pushes: every destination block must hold its source block's bytes, the
+// last of repeated destinations winning.
 //
 // Build and run (tests/test_plan_emulator.py does this):
 //   gcc -O1 -c oracle/pf_oracle.c -o pf_oracle.o
@@ -42,8 +45,12 @@ using namespace pf;
 namespace {
 
 // The copy kernel's work for tiles [tb, te): kernels.cu, kv_copy_kernel.
-void run_tiles(const Built& b, bool pack, bool table, uint64_t tb, uint64_t te, int64_t shift) {
-  for (uint64_t tile = tb; tile < te; ++tile) {
+// Warps run tiles in no fixed order; `backwards` replays them last to first,
+// so a plan whose result depends on the order fails one of the two replays.
+void run_tiles(const Built& b, bool pack, bool table, uint64_t tb, uint64_t te, int64_t shift,
+               bool backwards = false) {
+  for (uint64_t k = tb; k < te; ++k) {
+    const uint64_t tile = backwards ? te - 1 - (k - tb) : k;
     size_t l = 0;
     while (l + 1 < b.layers.size() && b.layers[l + 1].tile_start <= tile) ++l;
     const PlanLayer& L = b.layers[l];
@@ -102,23 +109,23 @@ void run_serial(const Built& b) {
 }
 
 // A staged or direct save / load as Executor::save / Executor::load run it.
-void run_save(const Built& b, bool staged, uint64_t slot_bytes, uint64_t first) {
-  if (!staged) return run_tiles(b, true, false, 0, b.total_tiles, 0);
+void run_save(const Built& b, bool staged, uint64_t slot_bytes, uint64_t first, bool backwards) {
+  if (!staged) return run_tiles(b, true, false, 0, b.total_tiles, 0, backwards);
   std::vector<uint8_t> slot(slot_bytes + 64);
   uint8_t* s = slot.data();
   std::vector<Chunk> chunks;
   cut_chunks(b.layers, b.total_tiles, slot_bytes, first, &chunks);
   for (const Chunk& c : chunks) {
     run_tiles(b, true, false, c.tile_begin, c.tile_end,
-              static_cast<int64_t>(reinterpret_cast<uint64_t>(s)) - static_cast<int64_t>(c.dense_begin));
+              static_cast<int64_t>(reinterpret_cast<uint64_t>(s)) - static_cast<int64_t>(c.dense_begin), backwards);
     run_copies(b, c, s, true);
   }
 }
 
-void run_load(const Built& b, bool staged, uint64_t slot_bytes, uint64_t first) {
+void run_load(const Built& b, bool staged, uint64_t slot_bytes, uint64_t first, bool backwards) {
   if (b.total_tiles) {
     if (!staged) {
-      run_tiles(b, false, true, 0, b.total_tiles, 0);
+      run_tiles(b, false, true, 0, b.total_tiles, 0, backwards);
     } else {
       std::vector<uint8_t> slot(slot_bytes + 64);
       uint8_t* s = slot.data();
@@ -127,7 +134,8 @@ void run_load(const Built& b, bool staged, uint64_t slot_bytes, uint64_t first) 
       for (const Chunk& c : chunks) {
         run_copies(b, c, s, false);
         run_tiles(b, false, false, c.tile_begin, c.tile_end,
-                  static_cast<int64_t>(reinterpret_cast<uint64_t>(s)) - static_cast<int64_t>(c.dense_begin));
+                  static_cast<int64_t>(reinterpret_cast<uint64_t>(s)) - static_cast<int64_t>(c.dense_begin),
+                  backwards);
       }
     }
   }
@@ -149,6 +157,16 @@ struct Layer {
   }
 };
 
+// Random bytes, eight per draw.
+void fill(std::vector<uint8_t>& v, std::mt19937_64& rng) {
+  size_t i = 0;
+  for (; i + 8 <= v.size(); i += 8) {
+    const uint64_t r = rng();
+    std::memcpy(v.data() + i, &r, 8);
+  }
+  for (; i < v.size(); ++i) v[i] = static_cast<uint8_t>(rng());
+}
+
 Layer random_layer(std::mt19937_64& rng) {
   static const uint64_t bpbs[] = {4, 12, 45, 4096, 8196, 32768, 100000};
   const uint64_t bpb = bpbs[rng() % 7];
@@ -169,7 +187,7 @@ Layer random_layer(std::mt19937_64& rng) {
       break;
   }
   L.cache.resize(L.ol.size_bytes);
-  for (auto& x : L.cache) x = static_cast<uint8_t>(rng());
+  fill(L.cache, rng);
   return L;
 }
 
@@ -180,7 +198,7 @@ int main(int argc, char** argv) {
   std::mt19937_64 rng(11);
   const DeviceCheck no_check = [](int, const pf_layer_desc&) {};
   char err[256];
-  long saves = 0, loads = 0, serial = 0;
+  long saves = 0, loads = 0, serial = 0, peers = 0;
   for (int c = 0; c < cases; ++c) {
     const int nl = 1 + static_cast<int>(rng() % 4);
     std::vector<Layer> layers;
@@ -205,7 +223,7 @@ int main(int argc, char** argv) {
     }
     Built bs;
     plan_save(sl.data(), nl, staged, 0, no_check, &bs);
-    run_save(bs, staged, slot_bytes, first);
+    run_save(bs, staged, slot_bytes, first, (c & 2) != 0);
     for (int i = 0; i < nl; ++i) {
       const Layer& L = layers[i];
       std::vector<uint8_t> k(pool_k[i].size()), v(pool_v[i].size());
@@ -225,7 +243,7 @@ int main(int argc, char** argv) {
     // ---- load: the saved blocks into other (possibly repeated) ids ----
     std::vector<Layer> dst = layers;  // same layouts, fresh bytes
     for (auto& L : dst) {
-      for (auto& x : L.cache) x = static_cast<uint8_t>(rng());
+      fill(L.cache, rng);
     }
     std::vector<std::vector<int64_t>> dids(nl);
     std::vector<std::vector<const void*>> ksrc(nl), vsrc(nl);
@@ -265,7 +283,7 @@ int main(int argc, char** argv) {
       continue;
     }
     serial += bl.serial.empty() ? 0 : 1;
-    run_load(bl, staged, slot_bytes, first);
+    run_load(bl, staged, slot_bytes, first, (c & 2) != 0);
     for (int i = 0; i < nl; ++i) {
       std::vector<const uint8_t*> kp(ksrc[i].size()), vp(vsrc[i].size());
       for (size_t j = 0; j < kp.size(); ++j) kp[j] = static_cast<const uint8_t*>(ksrc[i][j]);
@@ -282,7 +300,62 @@ int main(int argc, char** argv) {
       }
     }
     ++loads;
+
+    // ---- peer copies (P/D handoff): pull and push between two "devices" ----
+    // Copy identity: each destination block gets its source block's bytes,
+    // and for a repeated destination the last occurrence wins.
+    for (int push = 0; push < 2; ++push) {
+      const int np = 1 + static_cast<int>(rng() % 3);
+      std::vector<Layer> srcs, dsts;
+      std::vector<std::vector<int64_t>> sidx(np), didx(np);
+      std::vector<pf_p2p_layer> pl(np);
+      for (int i = 0; i < np; ++i) {
+        static const uint64_t bpbs[] = {4, 45, 4096, 32768, 100000};
+        const uint64_t bpb = bpbs[rng() % 5];
+        const bool split = rng() % 2;
+        // At least two blocks a side: a split layout of one block is a contiguous one.
+        const uint64_t nbs = 2 + rng() % 30, nbd = 2 + rng() % 30;
+        Layer S, D;
+        S.ol = split ? or_layout{2 * nbs * bpb, nbs, bpb, nbs * bpb, 2} : or_layout{nbs * bpb, nbs, bpb, 0, 1};
+        D.ol = split ? or_layout{2 * nbd * bpb, nbd, bpb, nbd * bpb, 2} : or_layout{nbd * bpb, nbd, bpb, 0, 1};
+        S.cache.resize(S.ol.size_bytes);
+        D.cache.resize(D.ol.size_bytes);
+        fill(S.cache, rng);
+        fill(D.cache, rng);
+        const uint64_t n = 1 + rng() % std::min(nbs, nbd);
+        for (uint64_t j = 0; j < n; ++j) {
+          sidx[i].push_back(static_cast<int64_t>(rng() % nbs));
+          didx[i].push_back(static_cast<int64_t>(rng() % nbd));
+        }
+        srcs.push_back(std::move(S));
+        dsts.push_back(std::move(D));
+      }
+      std::vector<Layer> want = dsts;
+      for (int i = 0; i < np; ++i) {
+        pl[i] = pf_p2p_layer{srcs[i].desc(), dsts[i].desc(), sidx[i].data(), didx[i].data(), sidx[i].size()};
+        const uint64_t bpb = srcs[i].ol.bytes_per_block;
+        const int units = srcs[i].ol.segments == 2 ? 2 : 1;
+        for (size_t j = 0; j < sidx[i].size(); ++j) {
+          for (int u = 0; u < units; ++u) {
+            std::memcpy(want[i].cache.data() + didx[i][j] * bpb + u * want[i].ol.kv_stride_bytes,
+                        srcs[i].cache.data() + sidx[i][j] * bpb + u * srcs[i].ol.kv_stride_bytes, bpb);
+          }
+        }
+      }
+      Built bp;
+      plan_p2p(pl.data(), np, 0, 1, push != 0, no_check, &bp);
+      run_tiles(bp, push != 0, true, 0, bp.total_tiles, 0, /*backwards=*/(c & 1) != 0);
+      for (int i = 0; i < np; ++i) {
+        if (want[i].cache != dsts[i].cache) {
+          std::printf("FAIL case %d: peer %s layer %d differs from copy identity (segments %llu, bpb %llu)\n", c,
+                      push ? "push" : "pull", i, (unsigned long long)dsts[i].ol.segments,
+                      (unsigned long long)dsts[i].ol.bytes_per_block);
+          return 1;
+        }
+      }
+      ++peers;
+    }
   }
-  std::printf("ok saves=%ld loads=%ld serial=%ld\n", saves, loads, serial);
+  std::printf("ok saves=%ld loads=%ld serial=%ld peers=%ld\n", saves, loads, serial, peers);
   return 0;
 }

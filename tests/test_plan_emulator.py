@@ -2,7 +2,8 @@
 (tests/plan_emulator.cpp): plan_save / plan_load and the staging-chunk cutter
 are replayed on host arrays with the copy kernel's tile addressing and the
 copy-engine runs, and the pool and restored bytes must equal the C oracle's
-restatement of the reference's copies. It caught a save bug the GPU tests
+restatement of the reference's copies; peer-copy plans (plan_p2p) must give
+copy identity. It caught a save bug the GPU tests
 missed by timing: a chunk whose first byte is not 256-byte aligned had its
 copy start at the aligned slot base, so stale slot bytes could overwrite the
 previous chunk's last bytes in the pool."""
@@ -31,4 +32,4 @@ def test_plans_replayed_on_the_cpu_match_the_oracle():
     line = out.stdout.strip().splitlines()[-1]
     assert line.startswith("ok"), line
     counts = dict(kv.split("=") for kv in line.split()[1:])
-    assert int(counts["loads"]) > 2500 and int(counts["serial"]) > 100, line
+    assert int(counts["loads"]) > 2500 and int(counts["serial"]) > 100 and int(counts["peers"]) > 5000, line
