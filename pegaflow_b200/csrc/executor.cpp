@@ -40,8 +40,9 @@ struct HostTimer {
   }
 };
 
-// The KV tensor must be device memory of this executor's device.
-void check_device_range(int device, const pf_layer_desc& l) {
+}  // namespace
+
+void check_device_memory(int device, const pf_layer_desc& l) {
   for (uint64_t addr : {l.data_ptr, l.data_ptr + l.size_bytes - 1}) {
     cudaPointerAttributes attr{};
     cudaError_t err = cudaPointerGetAttributes(&attr, reinterpret_cast<const void*>(addr));
@@ -54,8 +55,6 @@ void check_device_range(int device, const pf_layer_desc& l) {
     }
   }
 }
-
-}  // namespace
 
 // ---------------------------------------------------------------------------
 // Executor lifecycle
@@ -159,15 +158,15 @@ Executor::~Executor() {
 // ---------------------------------------------------------------------------
 
 void Executor::build_save(const pf_save_layer* layers, uint64_t n_layers, bool staged, Built* b) {
-  plan_save(layers, n_layers, staged, device_, check_device_range, b);
+  plan_save(layers, n_layers, staged, device_, check_device_memory, b);
 }
 
 void Executor::build_load(const pf_load_layer* layers, uint64_t n_layers, bool staged, Built* b) {
-  plan_load(layers, n_layers, staged, device_, check_device_range, b);
+  plan_load(layers, n_layers, staged, device_, check_device_memory, b);
 }
 
 void Executor::build_p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push, Built* b) {
-  plan_p2p(layers, n_layers, device_, peer, push, check_device_range, b);
+  plan_p2p(layers, n_layers, device_, peer, push, check_device_memory, b);
 }
 
 void Executor::enable_peer(int peer) {

@@ -27,6 +27,11 @@ constexpr uint64_t kDefaultFirstChunkBytes = 64ull << 20;
 // the small layers listed right after it).
 constexpr uint64_t kLayerwiseMinFirstChunk = 4ull << 20;
 
+// Throws unless the KV tensor [data_ptr, data_ptr + size_bytes) is device
+// (or managed) memory of `device`: the DeviceCheck the executor's and the
+// no-allocation save's plans use.
+void check_device_memory(int device, const pf_layer_desc& l);
+
 class Executor {
  public:
   Executor(int device, const pf_executor_config& cfg);

@@ -8,6 +8,8 @@
 // unit sizes from 4 bytes to over 64 KiB; staged mode with small slots, and
 // direct mode; repeated destination ids; and layouts whose blocks share
 // bytes (the ordered-copy path).
+// The no-allocation save (noalloc.cu) runs the same plan, cutter and copies
+// with a first chunk of a whole slot; a fifth of the cases cut that way.
 // Peer copies (plan_p2p, the P/D handoff) are replayed too, as pulls and as
 // pushes: every destination block must hold its source block's bytes, the
 // last of repeated destinations winning.
@@ -205,7 +207,8 @@ int main(int argc, char** argv) {
     for (int i = 0; i < nl; ++i) layers.push_back(random_layer(rng));
     const bool staged = rng() % 4 != 0;
     const uint64_t slot_bytes = align_up(std::max<uint64_t>(2 * kTileBytes, rng() % (1 << 20)), kDenseAlign);
-    const uint64_t first = rng() % (1 << 19);
+    uint64_t first = rng() % (1 << 19);
+    if (c % 5 == 0) first = slot_bytes;  // whole slots from the start: the no-allocation save's cut
 
     // ---- save: every layer's chosen blocks into its own pool regions ----
     std::vector<std::vector<int64_t>> ids(nl);
