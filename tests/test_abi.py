@@ -51,3 +51,17 @@ def test_library_is_sm100a_build(native):
     from pegaflow_b200 import build
 
     assert ["-gencode", "arch=compute_100a,code=sm_100a"] == build.ARCH
+
+
+def test_noalloc_argument_errors_need_no_gpu(native):
+    """The no-allocation save refuses a null layer array before touching CUDA,
+    and on a host without a GPU an empty save fails with the CUDA-init code
+    (lib.rs:58-67's CudaInit variant) instead of crashing."""
+    import torch
+
+    rc = native.lib.pf_save_blocks_noalloc(0, None, 1, None)
+    assert rc == native.PF_ERR_INVALID_ARGUMENT
+    assert "null layers" in native.lib.pf_last_error().decode()
+    if not torch.cuda.is_available():
+        assert native.lib.pf_save_blocks_noalloc(0, None, 0, None) == native.PF_ERR_CUDA_INIT
+        assert native.lib.pf_save_blocks_noalloc(-1, None, 0, None) == native.PF_ERR_CUDA_INIT
