@@ -22,7 +22,8 @@
 namespace pf {
 
 // ---------------------------------------------------------------------------
-// The plans' one CUDA-side check (the plans themselves: plan_build.cpp)
+// Host timing, and the plans' one CUDA-side check (the plans themselves:
+// plan_build.cpp)
 // ---------------------------------------------------------------------------
 
 namespace {
