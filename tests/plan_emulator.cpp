@@ -12,7 +12,9 @@
 // with a first chunk of a whole slot; a fifth of the cases cut that way.
 // Peer copies (plan_p2p, the P/D handoff) are replayed too, as pulls and as
 // pushes: every destination block must hold its source block's bytes, the
-// last of repeated destinations winning.
+// last of repeated destinations winning. Copies within one tensor on one
+// device must keep identity, and a pair that reads the block it writes must
+// be refused.
 //
 // Build and run (tests/test_plan_emulator.py does this):
 //   gcc -O1 -c oracle/pf_oracle.c -o pf_oracle.o
@@ -200,7 +202,7 @@ int main(int argc, char** argv) {
   std::mt19937_64 rng(11);
   const DeviceCheck no_check = [](int, const pf_layer_desc&) {};
   char err[256];
-  long saves = 0, loads = 0, serial = 0, peers = 0;
+  long saves = 0, loads = 0, serial = 0, peers = 0, within = 0;
   for (int c = 0; c < cases; ++c) {
     const int nl = 1 + static_cast<int>(rng() % 4);
     std::vector<Layer> layers;
@@ -358,7 +360,55 @@ int main(int argc, char** argv) {
       }
       ++peers;
     }
+
+    // ---- one device, one tensor: blocks copied within it ----
+    // Sources from the first half of the blocks, destinations from the second:
+    // copy identity. A pair that reads the block it writes is refused, since
+    // the result would depend on the order the warps run in.
+    {
+      const uint64_t bpb = (c & 4) ? 45 : 4096;
+      const uint64_t nb = 4 + rng() % 40, half = nb / 2;
+      const bool split = rng() % 2;
+      Layer T;
+      T.ol = split ? or_layout{2 * nb * bpb, nb, bpb, nb * bpb, 2} : or_layout{nb * bpb, nb, bpb, 0, 1};
+      T.cache.resize(T.ol.size_bytes);
+      fill(T.cache, rng);
+      const uint64_t n = 1 + rng() % half;
+      std::vector<int64_t> si, di;
+      for (uint64_t j = 0; j < n; ++j) {
+        si.push_back(static_cast<int64_t>(rng() % half));
+        di.push_back(static_cast<int64_t>(half + rng() % (nb - half)));
+      }
+      std::vector<uint8_t> want = T.cache;
+      for (uint64_t j = 0; j < n; ++j) {
+        for (int u = 0; u < (split ? 2 : 1); ++u) {
+          std::memcpy(want.data() + di[j] * bpb + u * T.ol.kv_stride_bytes,
+                      T.cache.data() + si[j] * bpb + u * T.ol.kv_stride_bytes, bpb);
+        }
+      }
+      pf_p2p_layer one{T.desc(), T.desc(), si.data(), di.data(), n};
+      Built bt;
+      plan_p2p(&one, 1, 0, 0, false, no_check, &bt);
+      run_tiles(bt, false, true, 0, bt.total_tiles, 0, (c & 1) != 0);
+      if (T.cache != want) {
+        std::printf("FAIL case %d: copy within one tensor differs from copy identity\n", c);
+        return 1;
+      }
+      si.back() = di.back();  // the last pair for a destination is always kept
+      Built bo;
+      bool refused = false;
+      try {
+        plan_p2p(&one, 1, 0, 0, false, no_check, &bo);
+      } catch (const std::exception&) {
+        refused = true;
+      }
+      if (!refused) {
+        std::printf("FAIL case %d: a block read and written by one copy was not refused\n", c);
+        return 1;
+      }
+      ++within;
+    }
   }
-  std::printf("ok saves=%ld loads=%ld serial=%ld peers=%ld\n", saves, loads, serial, peers);
+  std::printf("ok saves=%ld loads=%ld serial=%ld peers=%ld within=%ld\n", saves, loads, serial, peers, within);
   return 0;
 }

@@ -33,3 +33,4 @@ def test_plans_replayed_on_the_cpu_match_the_oracle():
     assert line.startswith("ok"), line
     counts = dict(kv.split("=") for kv in line.split()[1:])
     assert int(counts["loads"]) > 2500 and int(counts["serial"]) > 100 and int(counts["peers"]) > 5000, line
+    assert int(counts["within"]) == 3000, line
