@@ -207,8 +207,14 @@ int pf_p2p_transfer(pf_executor* exec, int32_t peer_device, int push,
  * exceeds 1 MiB, or with a copy unit above 4 MiB, fails with
  * PF_ERR_INVALID_ARGUMENT. The first call on a device resolves the arrays'
  * addresses (cudaGetSymbolAddress) and should come before any stream capture.
+ * The arrays are reserved in device memory when that first call loads the
+ * library's device code on the device (CUDA loads modules lazily), so make
+ * the first call before the caller's allocator claims HBM: the warm-up call
+ * pf_save_blocks_noalloc(device, NULL, 0, stream) loads the code, reserves
+ * the arrays and moves nothing. Later calls take no device memory.
  * All calls on a device share the arrays, so calls that overlap on the GPU
- * race; keep them ordered on one stream. Calls no cudaMalloc or cudaFree. */
+ * race; keep them ordered on one stream. Calls no cudaMalloc or cudaFree.
+ * The caller's current device is current again when the call returns. */
 int pf_save_blocks_noalloc(int32_t device_id, const pf_save_layer* layers,
                            uint64_t n_layers, void* stream);
 

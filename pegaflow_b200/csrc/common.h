@@ -1,6 +1,7 @@
 // Shared helpers: status + thread-local error message, CUDA error mapping.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -55,6 +56,60 @@ inline void cuda_check(cudaError_t err, const char* what) {
     throw storage_error(std::string(what) + " failed: " + cudaGetErrorString(err));
   }
 }
+
+// The driver's current-context calls, resolved through the runtime so the
+// library needs no libcuda at link time. Either pointer is null when the
+// driver does not provide it.
+struct CtxCalls {
+  CUresult (*get)(CUcontext*) = nullptr;
+  CUresult (*set)(CUcontext) = nullptr;
+};
+
+inline const CtxCalls& ctx_calls() {
+  static const CtxCalls calls = [] {
+    CtxCalls c;
+    void* g = nullptr;
+    void* s = nullptr;
+    cudaDriverEntryPointQueryResult qg{}, qs{};
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &g, 4000, cudaEnableDefault, &qg) == cudaSuccess &&
+        cudaGetDriverEntryPointByVersion("cuCtxSetCurrent", &s, 4000, cudaEnableDefault, &qs) == cudaSuccess &&
+        qg == cudaDriverEntryPointSuccess && qs == cudaDriverEntryPointSuccess) {
+      c.get = reinterpret_cast<CUresult (*)(CUcontext*)>(g);
+      c.set = reinterpret_cast<CUresult (*)(CUcontext)>(s);
+    }
+    cudaGetLastError();
+    return c;
+  }();
+  return calls;
+}
+
+// Makes `device` current on the calling thread for one scope, then puts the
+// caller's own context back, including "no context": a caller working on
+// device 1 that saves for device 0 finds device 1 current afterwards, and a
+// thread that had no context gets none. With the runtime linked statically
+// the current device is the driver's current context, which every other
+// CUDA user in the process (torch included) sees.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    const CtxCalls& c = ctx_calls();
+    if (c.get && c.set && c.get(&prev_) == CUDA_SUCCESS) restore_ = true;
+    const cudaError_t err = cudaSetDevice(device);
+    if (err != cudaSuccess) {
+      if (restore_) c.set(prev_);
+      cuda_check(err, "cudaSetDevice");
+    }
+  }
+  ~DeviceGuard() {
+    if (restore_) ctx_calls().set(prev_);
+  }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+ private:
+  CUcontext prev_ = nullptr;
+  bool restore_ = false;
+};
 
 // Runs f, converting exceptions into a status code + thread-local message.
 template <typename F>

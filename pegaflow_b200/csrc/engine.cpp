@@ -43,7 +43,12 @@ DeviceWorker::~DeviceWorker() {
   }
   cv_.notify_all();
   if (thread_.joinable()) thread_.join();
-  cudaSetDevice(exec_->device());
+  std::unique_ptr<DeviceGuard> on;
+  try {
+    on = std::make_unique<DeviceGuard>(exec_->device());
+  } catch (const Error&) {
+    // Destroy the streams in whatever context is current; nothing here may throw.
+  }
   for (cudaStream_t s : all_save_streams_) cudaStreamDestroy(s);
 }
 
@@ -54,7 +59,7 @@ cudaStream_t DeviceWorker::acquire_save_stream() {
     free_save_streams_.pop_back();
     return s;
   }
-  cuda_check(cudaSetDevice(exec_->device()), "cudaSetDevice");
+  DeviceGuard on(exec_->device());
   cudaStream_t s = nullptr;
   cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate(save)");
   all_save_streams_.push_back(s);
@@ -81,7 +86,10 @@ bool DeviceWorker::wait_idle(double timeout_s) {
 }
 
 void DeviceWorker::load_loop() {
-  // load_worker_loop (gpu_worker.rs:141-181)
+  // load_worker_loop (gpu_worker.rs:141-181). This thread belongs to the
+  // worker, so its device stays current for the thread's life (LoadState
+  // polling and flag buffers run in that context).
+  if (cudaSetDevice(exec_->device()) != cudaSuccess) cudaGetLastError();
   for (;;) {
     LoadTask task;
     {
@@ -589,6 +597,9 @@ void Engine::batch_save(const std::string& instance_id, uint64_t tp_rank, int de
     // The call orders on a stream of its own, so concurrent saves on this
     // device (other instances, other RPC threads) each wait only for their
     // own copies; the executor's save lane still runs them in order.
+    // The copy and its stream wait run with the save's device current; the
+    // caller's own context is current again when the call returns.
+    DeviceGuard on(ex.device());
     struct StreamLease {
       DeviceWorker* w;
       cudaStream_t s;

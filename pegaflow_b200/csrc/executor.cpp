@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cstring>
+#include <memory>
 #include <string>
 
 #include "common.h"
@@ -70,7 +71,7 @@ Executor::Executor(int device, const pf_executor_config& cfg) : device_(device),
   if (device < 0 || device >= count) {
     throw cuda_init("device " + std::to_string(device) + " out of range (" + std::to_string(count) + " devices)");
   }
-  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  DeviceGuard on(device);
   cuda_check(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
   if (cfg_.staging_chunk_bytes == 0) cfg_.staging_chunk_bytes = kDefaultSlotBytes;
   if (cfg_.staging_slots == 0) cfg_.staging_slots = kDefaultSlots;
@@ -140,7 +141,12 @@ void Executor::destroy_lane(Lane& l) {
 }
 
 Executor::~Executor() {
-  cudaSetDevice(device_);
+  std::unique_ptr<DeviceGuard> on;
+  try {
+    on = std::make_unique<DeviceGuard>(device_);
+  } catch (const Error&) {
+    // Tear down in whatever context is current; nothing here may throw.
+  }
   cudaDeviceSynchronize();
   for (auto& p : timed_) {
     cudaEventDestroy(p.first);
@@ -189,7 +195,7 @@ void Executor::enable_peer(int peer) {
 
 void Executor::p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push, cudaStream_t caller) {
   HostTimer timer{&stats_.host_ms, &stats_mu_};
-  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  DeviceGuard on(device_);
   Lane& L = load_lane_;
   std::lock_guard<std::mutex> g(L.mu);
   enable_peer(peer);
@@ -207,6 +213,7 @@ void Executor::p2p(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool
 }
 
 void Executor::p2p_sync(const pf_p2p_layer* layers, uint64_t n_layers, int peer, bool push) {
+  DeviceGuard on(device_);
   p2p(layers, n_layers, peer, push, own_stream_);
   cuda_check(cudaStreamSynchronize(own_stream_), "cudaStreamSynchronize(p2p)");
 }
@@ -417,7 +424,7 @@ uint64_t Executor::copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool
 
 void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t caller) {
   HostTimer timer{&stats_.host_ms, &stats_mu_};
-  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  DeviceGuard on(device_);
   const bool staged = cfg_.save_mode != PF_MODE_DIRECT;
   Built b;
   build_save(layers, n_layers, staged, &b);
@@ -476,7 +483,7 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
 
 void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t caller, int64_t* layer_done) {
   HostTimer timer{&stats_.host_ms, &stats_mu_};
-  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  DeviceGuard on(device_);
   const bool staged = cfg_.load_mode != PF_MODE_DIRECT;
   Built b;
   build_load(layers, n_layers, staged, &b);
@@ -570,16 +577,19 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
 }
 
 void Executor::save_sync(const pf_save_layer* layers, uint64_t n_layers) {
+  DeviceGuard on(device_);
   save(layers, n_layers, save_stream_);
   cuda_check(cudaStreamSynchronize(save_stream_), "cudaStreamSynchronize(save)");
 }
 
 void Executor::load_sync(const pf_load_layer* layers, uint64_t n_layers, int64_t* layer_done) {
+  DeviceGuard on(device_);
   load(layers, n_layers, own_stream_, layer_done);
   cuda_check(cudaStreamSynchronize(own_stream_), "cudaStreamSynchronize(load)");
 }
 
 void Executor::stats(pf_executor_stats* out) {
+  DeviceGuard on(device_);
   // Wait for the spans issued so far without holding the mutex, so that
   // calls on either lane keep launching meanwhile.
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;

@@ -87,7 +87,7 @@ void save_noalloc(int device, const pf_save_layer* layers, uint64_t n_layers, cu
   if (device < 0 || device >= count || device >= kMaxDevices) {
     throw cuda_init("device " + std::to_string(device) + " out of range");
   }
-  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  DeviceGuard on(device);
   DeviceScratch& sc = scratch_for(device);
 
   // The executor's staged save plan (same checks, geometry, dense layout and

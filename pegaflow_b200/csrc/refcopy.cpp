@@ -82,7 +82,7 @@ uint64_t refcopy_runs(const std::vector<std::pair<uint64_t, const uint8_t*>>& xf
 }  // namespace
 
 void refcopy_save(int device, const pf_save_layer* layers, uint64_t n) {
-  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  DeviceGuard on(device);
   for (uint64_t li = 0; li < n; ++li) {
     validate_layout(layers[li].layer, ("#" + std::to_string(li)).c_str());
     refcopy_save_layer(layers[li]);
@@ -90,7 +90,7 @@ void refcopy_save(int device, const pf_save_layer* layers, uint64_t n) {
 }
 
 uint64_t refcopy_load(int device, const pf_load_layer* layers, uint64_t n) {
-  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  DeviceGuard on(device);
   cudaStream_t stream;
   cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
   uint64_t runs = 0;

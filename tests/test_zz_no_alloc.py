@@ -129,3 +129,32 @@ def test_noalloc_save_of_unaligned_units_across_chunks(cuda, native, oracle):
     k_ref, v_ref = oracle.np_save_layer(ol, host, ids)
     np.testing.assert_array_equal(pool.numpy()[: n * 45], k_ref)
     np.testing.assert_array_equal(pool.numpy()[n * 45:], v_ref)
+
+
+def test_noalloc_takes_no_device_memory_after_warm_up(cuda, native):
+    """The point of the entry point: after the warm-up call (no layers), which
+    loads the library's device code and so reserves the fixed arrays, a
+    multi-chunk save leaves the device's free memory exactly as it was. The
+    callers it serves have already handed all free HBM to their own
+    allocator, so a save that took any would fail there."""
+    torch = cuda
+    from pegaflow_b200 import PinnedBuffer
+
+    stream = torch.cuda.Stream()
+    native.check(native.lib.pf_save_blocks_noalloc(0, None, 0, ctypes.c_void_p(stream.cuda_stream)))
+    rng = np.random.default_rng(41)
+    tensors = [kv(torch, (2, 512, 16, 8, 128), torch.bfloat16, 50 + i) for i in range(2)]
+    ids_list = [rng.permutation(512)[:192] for _ in range(2)]  # 24 MiB: three 8 MiB chunks
+    _, size = specs_for(tensors, ids_list, 0)
+    pool = PinnedBuffer(size)
+    specs, _ = specs_for(tensors, ids_list, pool.ptr)
+    torch.cuda.synchronize()
+    for _ in range(2):
+        free_before = torch.cuda.mem_get_info(0)[0]
+        native.check(save_noalloc(native, specs, stream.cuda_stream))
+        stream.synchronize()
+        assert torch.cuda.mem_get_info(0)[0] == free_before
+    k = specs[0]
+    got = pool.numpy()[k.k_dst - pool.ptr:k.k_dst - pool.ptr + 192 * 32768]
+    want = tensors[0][0, torch.as_tensor(ids_list[0], device="cuda")].contiguous().view(torch.uint8).cpu().numpy()
+    np.testing.assert_array_equal(got, want.reshape(-1))
