@@ -1,24 +1,31 @@
 #!/usr/bin/env python
 """KV-cache block save/load throughput on B200 (one process per GPU).
 
-Workload (default): Llama-3.1-8B-shaped paged KV, 32 layers
-of KV-first [2, 8192, 16, 8, 128] bf16 ~N(0,1) per GPU; one 10,240-token
-prefix = 640 blocks saved (all layers) to the pinned pool and restored into
-640 other block ids. Seeded synthetic data; block ids seeded-shuffled (or
-sorted with --order sorted). Each rank runs its own copy on its own GPU into
-its own pool (weak scaling; no collective on the data path).
+Workload (default, BASELINE config 3 at TP=N): Llama-3-70B-shaped paged KV,
+80 layers of KV-first [2, 4096, 16, 8/N, 128] bf16 ~N(0,1) per rank, each of
+the N ranks holding its own slice of the 8 KV heads on its own GPU; 2,048
+blocks (one 32,768-token prefix) saved from seeded-shuffled ids into the
+rank's pinned pool region and restored into 2,048 other ids. At N=1 this is
+TP1 of the same config. Seeded synthetic data; no collective on the data path.
+`--workload llama8b` runs BASELINE config 1 (32 layers x 640 blocks) instead.
 
-One step = save of the 640 blocks x 32 layers + load of them back.
-  value : payload GB/s (save + load bytes / time) of the transfer executor,
-          device-timed with CUDA events on the calling stream, max over ranks.
+One step = save of the blocks x layers + load of them back.
+  value : payload GB/s of all ranks (save + load bytes / time) of the transfer
+          executor, device-timed with CUDA events on the calling stream, the
+          slowest rank's time.
   e2e   : the same through the engine API (PegaEngine.batch_save_kv_blocks +
           batch_load_kv_blocks + LoadState completion), host wall clock.
-Also reported: save/load split, p50 load ms, host-link peak and fraction, the
-pack/unpack kernel HBM roofline, the reference's own copy strategy timed on the
-same GPU, and a CPU gather/scatter baseline.
+  verified : every restored block equals its source bit for bit, on every rank
+          (destinations are zeroed before each timed region).
+Also reported: save/load split, p50 load ms, host-link peaks (each GPU alone
+and all at once) and fractions, the pack/unpack kernel HBM roofline, the other
+block order, configs[1] in both orders (N=1), a P/D NVLink handoff check
+(N>=2), the reference's own copy strategy timed on the same GPU, and a CPU
+gather/scatter baseline.
 
 --impl reference: the reference's CPU implementation of the path (the oracle
-port of its copies, multi-threaded) on this host's cores; rank 0 only.
+port of its copies, multi-threaded) on this host's cores over the whole job
+(all N head shards); rank 0 only.
 """
 
 from __future__ import annotations
@@ -127,7 +134,7 @@ def measured_peaks() -> dict:
 
 # DRAM bytes per payload byte of one pack or unpack launch, from one ncu
 # capture of dram__bytes_read.sum / dram__bytes_write.sum on 128 MiB staging
-# chunks (larger than L2; profiles/kv_copy_kernel_llama8b.md, section 2b).
+# chunks (larger than L2), not a per-run measurement.
 # Reads equal the payload (no re-reads); writes still in the 126 MB L2 when
 # the kernel ends reach DRAM after it, so the write figure is below 1.
 TRAFFIC_READ_PER_BYTE = 134_251_584 / 134_217_728
@@ -278,26 +285,29 @@ def payload_bytes(tensors, n) -> int:
 class CpuWorkload:
     """Oracle port of the reference's copies (multi-threaded memcpy gather and
     scatter) on host-resident buffers with the workload's layout: a bounded
-    sample of `max_layers` layers with the workload's block lists.
+    sample of `max_layers` layers of every TP shard (`world` shards of
+    heads/world KV heads each, with each rank's own block lists).
 
     `pool` picks the memory the pool regions live in: "malloc" (cacheable
     pages), "pinned" (page-locked, cacheable) or "pinned_wc" (page-locked and
     write-combined, the reference's pool memory, pinned_mem.rs:159, which the
     CPU reads uncached)."""
 
-    def __init__(self, wl: dict, threads: int, max_layers: int = 8, pool: str = "malloc"):
+    def __init__(self, wl: dict, threads: int, max_layers: int = 8, pool: str = "malloc", world: int = 1,
+                 order: str = "shuffled"):
         from oracle import oracle
+        from pegaflow_b200.ranks import block_lists
 
         self.oracle = oracle
         oracle.build()
         self.threads = threads
         self._keep = []
         L = min(wl["layers"], max_layers)
-        nb, bs, hd, heads = wl["num_blocks"], wl["block_size"], wl["head_dim"], wl["heads"]
+        nb, bs, hd = wl["num_blocks"], wl["block_size"], wl["head_dim"]
+        shards = world if wl.get("tp") else 1
+        heads = wl["heads"] // shards
         seg = bs * heads * hd * 2
         n = wl["blocks"]
-        src = np.random.default_rng(3).permutation(nb)[:n]
-        dst = np.random.default_rng(4).permutation(nb)[:n]
 
         def region(nbytes):
             if pool == "malloc":
@@ -311,16 +321,20 @@ class CpuWorkload:
             return arr
 
         self.saves, self.loads = [], []
-        for i in range(L):
-            lay = oracle.Layout(nb * seg, nb, seg, 0, 1) if wl.get("separate") else \
-                oracle.Layout(2 * nb * seg, nb, seg, nb * seg, 2)
-            cache = np.empty(lay.size_bytes, np.uint8)
-            cache[::4096] = i  # fault every page in before timing
-            kp = region(n * seg)
-            vp = region(n * seg) if lay.split else None
-            self.saves.append((lay, cache, src, kp, vp))
-            self.loads.append((lay, cache, dst, kp, vp))
-        self.sample = f"{L} of {wl['layers']} layers x {n} blocks (save + load), host-resident buffers, pool: {pool}"
+        for r in range(shards):
+            src, dst = block_lists(nb, n, r, order)
+            for i in range(L):
+                lay = oracle.Layout(nb * seg, nb, seg, 0, 1) if wl.get("separate") else \
+                    oracle.Layout(2 * nb * seg, nb, seg, nb * seg, 2)
+                cache = np.empty(lay.size_bytes, np.uint8)
+                cache[::4096] = i  # fault every page in before timing
+                kp = region(n * seg)
+                vp = region(n * seg) if lay.split else None
+                self.saves.append((lay, cache, src, kp, vp))
+                self.loads.append((lay, cache, dst, kp, vp))
+        shard_txt = f"{shards} TP shards x " if shards > 1 else ""
+        self.sample = (f"{shard_txt}{L} of {wl['layers']} layers x {n} blocks ({order} ids; save + load), "
+                       f"host-resident buffers, pool: {pool}")
 
     def close(self) -> None:
         for b in self._keep:
@@ -347,11 +361,15 @@ class CpuWorkload:
 
 
 def run_reference_arm(args, wl) -> None:
+    """The reference's CPU implementation of the path (the oracle port of its
+    copies) on every host core, over the whole job: at N GPUs of the TP
+    workload, all N head shards, so its GB/s compares with the b200 arm's
+    whole-job value. Rank 0 alone runs; the other ranks exit at once."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    cw = CpuWorkload(wl, threads)
+    cw = CpuWorkload(wl, threads, world=args.gpus, order=args.order)
     for _ in range(args.warmup):
         cw.step()
     times, vals = [], []
@@ -366,7 +384,7 @@ def run_reference_arm(args, wl) -> None:
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(times), 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
-        "data": "synthetic (host-resident, seeded block lists)", "config": config_block(args, wl),
+        "data": "synthetic (host-resident, seeded block lists)", "config": config_block(args, wl, args.gpus),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": cw.sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference path is Rust over cudarc copies with no CPU implementation and cannot be built "
@@ -776,17 +794,227 @@ def run_duplex(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def config_block(args, wl) -> dict:
-    return {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
-            "blocks_moved": wl["blocks"], "block_ids": args.order, "kv_dtype": "fp16" if wl.get("separate") else "bf16",
-            "save_mode": args.save_mode, "load_mode": args.load_mode,
-            "staging": {"slot_MiB": args.chunk_mib or 512, "slots": args.slots or 2, "lanes": "save, load",
-                        "first_chunk_MiB": args.first_chunk_mib or 64, "growth": "x2 per chunk",
-                        "save_first_chunk": "max(first chunk, half a slot)",
-                        "load_first_chunk": "a whole slot; with per-layer flags (the e2e engine loads) "
-                                            "the first layer, at most the first chunk"},
-            "l2": "inputs larger than L2 (payload >= 36 MiB per layer set; KV cache >> 126 MB)",
-            "parallelism": f"dp{args.gpus} (independent ranks, weak scaling)"}
+def config_block(args, wl, world: int) -> dict:
+    cfg = {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
+           "blocks_moved": wl["blocks"], "block_ids": args.order,
+           "kv_dtype": "fp16" if wl.get("separate") else "bf16",
+           "save_mode": args.save_mode, "load_mode": args.load_mode,
+           "staging": {"slot_MiB": args.chunk_mib or 512, "slots": args.slots or 2, "lanes": "save, load",
+                       "first_chunk_MiB": args.first_chunk_mib or 64, "growth": "x2 per chunk",
+                       "save_first_chunk": "max(first chunk, half a slot)",
+                       "load_first_chunk": "a whole slot; with per-layer flags (the e2e engine loads) "
+                                           "the first layer, at most the first chunk"},
+           "l2": "inputs larger than L2 (payload >= 36 MiB per layer set; KV cache >> 126 MB)"}
+    if wl.get("tp"):
+        cfg["tp"] = world
+        cfg["heads_per_rank"] = wl["heads"] // world
+        cfg["parallelism"] = (f"tp{world} (one process per GPU; each rank saves and restores its own KV head "
+                              "shard in its own pool region; no collective on the data path)")
+    else:
+        cfg["parallelism"] = f"dp{world} (independent ranks, weak scaling)"
+    return cfg
+
+
+# ----------------------------------------------------------------------------- byte checks
+
+
+def _block_dim(t) -> int:
+    """Dimension of the block index: 1 for KV-first [2, nb, ...], else 0."""
+    return 1 if (t.dim() == 5 and t.shape[0] == 2) else 0
+
+
+def scribble(torch, tensors, ids) -> None:
+    """Zero the destination blocks, so a later check sees only bytes that the
+    transfers after this call restored."""
+    idx = torch.as_tensor(np.asarray(ids), device=tensors[0].device)
+    for t in tensors:
+        t.index_fill_(_block_dim(t), idx, 0)
+
+
+def restored(torch, tensors, src, dst) -> bool:
+    """Every destination block equals its source block, bit for bit (sources
+    and destinations are disjoint, so sources are never overwritten)."""
+    si = torch.as_tensor(np.asarray(src), device=tensors[0].device)
+    di = torch.as_tensor(np.asarray(dst), device=tensors[0].device)
+    return all(torch.equal(t.index_select(_block_dim(t), di), t.index_select(_block_dim(t), si)) for t in tensors)
+
+
+def pool_matches(torch, tensors, saves, pool, src) -> bool:
+    """The pinned pool holds each layer's K region, then its V region, in the
+    order of the block list (lib.rs:639-679): checked on the first and last
+    layer against the source blocks."""
+    si = torch.as_tensor(np.asarray(src), device=tensors[0].device)
+    host = pool.numpy()
+    for li in sorted({0, len(tensors) - 1}):
+        t, sp = tensors[li], saves[li]
+        parts = [(t[0], sp.k_dst), (t[1], sp.v_dst)] if sp.layout.split else [(t, sp.k_dst)]
+        for kv, base in parts:
+            want = kv.index_select(0, si).contiguous().view(-1).view(torch.uint8)
+            off = base - pool.ptr
+            got = torch.from_numpy(host[off:off + want.numel()].copy()).to(t.device)
+            if not torch.equal(got, want):
+                return False
+    return True
+
+
+def executor_rates(torch, ex, stream, saves, loads, payload: int, steps: int, warmup: int, barrier) -> dict:
+    """Save then load, `steps` times on one stream, device-timed per step."""
+    sp = stream.cuda_stream
+    for _ in range(warmup):
+        ex.save(saves, stream=sp)
+        ex.load(loads, stream=sp)
+    stream.synchronize()
+    barrier()
+    evs = []
+    for _ in range(steps):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record(stream)
+        ex.save(saves, stream=sp)
+        e[1].record(stream)
+        ex.load(loads, stream=sp)
+        e[2].record(stream)
+        evs.append(e)
+    stream.synchronize()
+    save_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    load_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    total = sum(e[0].elapsed_time(e[2]) for e in evs)
+    return {"total_ms": total, "save_GBps": payload / (statistics.median(save_ms) / 1e3) / 1e9,
+            "load_GBps": payload / (statistics.median(load_ms) / 1e3) / 1e9,
+            "p50_load_ms": statistics.median(load_ms)}
+
+
+# ----------------------------------------------------------------------------- extra blocks
+
+
+def configs1_block(torch, args, ex, local: int) -> dict:
+    """BASELINE config 1 (Llama-3.1-8B shape, 32 layers x 640 blocks) on this
+    GPU through the same executor, once with seeded-shuffled and once with
+    sorted-contiguous block ids; bytes checked after each."""
+    from pegaflow_b200 import PinnedBuffer
+    from pegaflow_b200.ranks import block_lists
+
+    wl = WORKLOADS["llama8b"]
+    tensors, _, _ = make_workload(torch, wl, local, 0, 1, "shuffled")
+    n = wl["blocks"]
+    payload = payload_bytes(tensors, n)
+    pool = PinnedBuffer(payload + wl["layers"] * 8192 + (1 << 20), write_combined=True)
+    stream = torch.cuda.Stream(local)
+    out = {"desc": wl["desc"], "payload_bytes_per_direction": payload}
+    for order in ("shuffled", "sorted"):
+        src, dst = block_lists(wl["num_blocks"], n, 0, order)
+        saves, loads, _ = executor_specs(tensors, src, dst, pool.ptr)
+        scribble(torch, tensors, dst)
+        r = executor_rates(torch, ex, stream, saves, loads, payload, max(3, min(args.steps, 10)), 2, lambda: None)
+        out[order] = {"GBps": round(2 * payload * max(3, min(args.steps, 10)) / (r["total_ms"] / 1e3) / 1e9, 3),
+                      "save_GBps": round(r["save_GBps"], 3), "load_GBps": round(r["load_GBps"], 3),
+                      "p50_load_ms": round(r["p50_load_ms"], 3),
+                      "verified": restored(torch, tensors, src, dst) and pool_matches(torch, tensors, saves, pool, src)}
+    pool.close()
+    del tensors
+    torch.cuda.empty_cache()
+    return out
+
+
+def pd_check(torch, ex0, reps: int = 10) -> dict:
+    """BASELINE config 2's handoff for one request, inside the multi-GPU run:
+    Qwen3-8B-shaped KV (36 layers of [2, 1024, 16, 8, 128] bf16) on GPU0 and
+    GPU1, 313 seeded blocks moved GPU0 -> GPU1 by the decode-side pull kernel
+    (plain 16-byte peer loads over NVLink), bytes checked, timed against the
+    1 GiB peer-copy peak and against one host-pool bounce (save on GPU0, load
+    on GPU1). Runs in rank 0's process; the other ranks wait on the host."""
+    from pegaflow_b200 import Executor, Layout, LoadSpec, P2PSpec, PinnedBuffer, SaveSpec
+
+    layers, nb, n = 36, 1024, 313
+    g0 = torch.Generator(device="cuda:0").manual_seed(7)
+    g1 = torch.Generator(device="cuda:1").manual_seed(8)
+    shape = (2, nb, 16, 8, 128)
+    src = [torch.randn(shape, generator=g0, device="cuda:0").to(torch.bfloat16) for _ in range(layers)]
+    dst = [torch.randn(shape, generator=g1, device="cuda:1").to(torch.bfloat16) for _ in range(layers)]
+    si = np.random.default_rng(4).permutation(nb)[:n]
+    di = np.random.default_rng(10_000).permutation(nb)[:n]
+    si0 = torch.as_tensor(si, device="cuda:0")
+    payload = n * layers * 2 * 32768
+    dev_before = torch.cuda.current_device()
+    ex1 = Executor(1)
+    s0, s1 = torch.cuda.Stream("cuda:0"), torch.cuda.Stream("cuda:1")
+    specs = [P2PSpec(Layout.from_tensor(x), Layout.from_tensor(y), si, di) for x, y in zip(src, dst)]
+
+    def expected_ok() -> bool:
+        return all(torch.equal(y.index_select(1, torch.as_tensor(di, device="cuda:1")),
+                               x.index_select(1, si0).to("cuda:1")) for x, y in zip(src, dst))
+
+    ex1.p2p(specs, 0, push=False, stream=s1.cuda_stream)  # warm-up (enables peer access)
+    s1.synchronize()
+    scribble(torch, dst, di)
+    torch.cuda.synchronize(1)
+    ms = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s1)
+        ex1.p2p(specs, 0, push=False, stream=s1.cuda_stream)
+        e1.record(s1)
+        ms.append((e0, e1))
+    s1.synchronize()
+    pull_ms = [a.elapsed_time(b) for a, b in ms]
+    pull_ok = expected_ok()
+
+    # Peer copy peak: 1 GiB cudaMemcpyPeer GPU0 -> GPU1, best of 4.
+    a = torch.empty(1 << 30, dtype=torch.uint8, device="cuda:0")
+    b = torch.empty(1 << 30, dtype=torch.uint8, device="cuda:1")
+    peak = 0.0
+    for _ in range(4):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s1):
+            e0.record(s1)
+            b.copy_(a, non_blocking=True)
+            e1.record(s1)
+        e1.synchronize()
+        peak = max(peak, (1 << 30) / (e0.elapsed_time(e1) / 1e3) / 1e9)
+    del a, b
+
+    # One request through the host pool: the reference's handoff (docs/pd.md).
+    pool = PinnedBuffer(payload + layers * 4096, write_combined=True)
+    saves, loads, off = [], [], 0
+    for x, y in zip(specs, dst):
+        k, v = pool.ptr + off, pool.ptr + off + n * 32768
+        ks = np.arange(n, dtype=np.uint64) * 32768 + k
+        saves.append(SaveSpec(x.src, si, k, v))
+        loads.append(LoadSpec(Layout.from_tensor(y), di, ks, ks + n * 32768))
+        off += 2 * n * 32768 + 4096
+    scribble(torch, dst, di)
+    torch.cuda.synchronize(1)
+    bounce_ms = []
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s1)
+        s0.wait_event(e0)
+        ex0.save(saves, stream=s0.cuda_stream)
+        ev = torch.cuda.Event()
+        ev.record(s0)
+        s1.wait_event(ev)
+        ex1.load(loads, stream=s1.cuda_stream)
+        e1.record(s1)
+        e1.synchronize()
+        bounce_ms.append(e0.elapsed_time(e1))
+    bounce_ok = expected_ok()
+    launches = ex1.stats()["kernel_launches"]
+    pool.close()
+    ex1.close()
+    dev_after = torch.cuda.current_device()
+    del src, dst
+    torch.cuda.synchronize(1)
+    torch.cuda.empty_cache()
+    pull_gbps = payload / (statistics.median(pull_ms) / 1e3) / 1e9
+    bounce_gbps = payload / (statistics.median(bounce_ms) / 1e3) / 1e9
+    return {"workload": "qwen3_pd, one request: 36 layers x 313 blocks GPU0 -> GPU1",
+            "payload_bytes": payload, "p2p_pull_GBps": round(pull_gbps, 2),
+            "p2p_pull_p50_ms": round(statistics.median(pull_ms), 3),
+            "peer_copy_peak_GBps": round(peak, 1), "frac_of_peer_peak": round(pull_gbps / peak, 3),
+            "host_pool_bounce_GBps": round(bounce_gbps, 2), "p2p_over_bounce": round(pull_gbps / bounce_gbps, 2),
+            "verified": bool(pull_ok and bounce_ok), "device_restored": dev_after == dev_before,
+            "gpu1_launches": launches,
+            "how": "pull: kernel on GPU1 reads GPU0's paged KV with plain 16-byte peer loads (no TMA, no multicast); "
+                   "median of 10 device-timed requests; bounce: executor save on GPU0 then load on GPU1, median of 3"}
 
 
 # ----------------------------------------------------------------------------- main arm
@@ -799,7 +1027,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["qwen3_pd", "llama8b_fp8_evict", "llama8b_duplex"],
-                    default="llama8b")
+                    default="llama70b_tp")
     ap.add_argument("--fp8-requests", type=int, default=64)
     ap.add_argument("--fp8-pool-gb", type=int, default=30)
     ap.add_argument("--fp8-compute-ms", type=float, default=0.5)
@@ -817,6 +1045,8 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=0, help="engine-API steps (default: --steps)")
     ap.add_argument("--no-refcopy", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the other-order, configs[1] and P/D blocks (short profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling runs)")
     args = ap.parse_args()
@@ -862,13 +1092,21 @@ def main() -> int:
     rank, world, local = ranks.rank, ranks.world, ranks.local
     barrier, max_over_ranks, min_over_ranks = ranks.barrier, ranks.max, ranks.min
 
-    from pegaflow_b200 import Executor, PegaEngine, PinnedBuffer, PyLoadState, refcopy_load, refcopy_save
-
-    from pegaflow_b200.ranks import bind_to_gpu_cpus
+    from pegaflow_b200 import Executor, Layout, PegaEngine, PinnedBuffer, PyLoadState, refcopy_load, refcopy_save
+    from pegaflow_b200.ranks import bind_to_gpu_cpus, block_lists
 
     cpus = bind_to_gpu_cpus(local)
     peaks = measured_peaks()
-    link = link_peaks(torch, local, barrier if world > 1 else None)  # all ranks at once
+    # Host-link peaks: each rank alone (the others wait on the host), then
+    # every rank at once (its share of the link while all GPUs copy).
+    link_alone = None
+    for r in range(world):
+        ranks.host_barrier()
+        if r == rank:
+            link_alone = link_peaks(torch, local)
+    ranks.host_barrier()
+    link = link_peaks(torch, local, barrier) if world > 1 else dict(link_alone)
+    alone_d2h_all, alone_h2d_all = ranks.gather(link_alone["d2h"]), ranks.gather(link_alone["h2d"])
     link_d2h_all, link_h2d_all = ranks.gather(link["d2h"]), ranks.gather(link["h2d"])
     tensors, src, dst = make_workload(torch, wl, local, rank, world, args.order)
     n = len(src)
@@ -897,6 +1135,8 @@ def main() -> int:
     for _ in range(args.warmup):
         step()
     stream.synchronize()
+    scribble(torch, tensors, dst)  # the check below then sees only what the timed steps restored
+    torch.cuda.synchronize()
 
     ex.reset_stats()
     ex.set_timing(True)
@@ -925,18 +1165,44 @@ def main() -> int:
     my_save = payload / (statistics.median(save_ms) / 1e3) / 1e9
     my_load = payload / (statistics.median(load_ms) / 1e3) / 1e9
     save_gbps, load_gbps = min_over_ranks(my_save), min_over_ranks(my_load)
-    # Each rank against its own share of the link (measured with all ranks copying).
+    # Each rank against its own peaks: measured alone, and measured while every rank copies.
+    save_frac_alone = min_over_ranks(my_save / link_alone["d2h"])
+    load_frac_alone = min_over_ranks(my_load / link_alone["h2d"])
     save_frac = min_over_ranks(my_save / link["d2h"])
     load_frac = min_over_ranks(my_load / link["h2d"])
     p50_load = max_over_ranks(statistics.median(load_ms))
-    kernel_gbps = st["kernel_bytes"] / (st["kernel_ms"] / 1e3) / 1e9 if st["kernel_ms"] > 0 else None
+    kernel_gbps = st["kernel_bytes"] / (st["kernel_ms"] / 1e3) / 1e9 if st["kernel_ms"] > 0 else 0.0
+    kernel_all = ranks.gather(kernel_gbps)
+    launch_us_all = ranks.gather(st["kernel_ms"] * 1e3 / max(1, st["timed_launches"]))
+    verified_main = ranks.all_true(restored(torch, tensors, src, dst)
+                                   and pool_matches(torch, tensors, saves, pool, src))
 
     # Saves alone and loads alone, started on every rank at once: the same
-    # traffic pattern as the link peaks, so the fractions compare like with like
-    # (inside a step, ranks drift apart and one rank's saves meet another's loads).
+    # traffic pattern as the concurrent link peaks, so the fractions compare like
+    # with like (inside a step, ranks drift apart and one rank's saves meet
+    # another's loads).
     al_save = aligned_rates(torch, stream, lambda: ex.save(saves, stream=sp), payload, barrier)
     al_load = aligned_rates(torch, stream, lambda: ex.load(loads, stream=sp), payload, barrier)
     al_save_all, al_load_all = ranks.gather(al_save), ranks.gather(al_load)
+
+    # The other block order, same tensors and executor (sorted-contiguous runs
+    # are where the reference's run merging differs from shuffled ids).
+    other = None
+    if not args.no_extra:
+        o_order = "sorted" if args.order == "shuffled" else "shuffled"
+        o_src, o_dst = block_lists(wl["num_blocks"], n, rank, o_order)
+        o_saves, o_loads, _ = executor_specs(tensors, o_src, o_dst, pool.ptr)
+        scribble(torch, tensors, o_dst)
+        o_steps = max(3, min(steps, 10))
+        r = executor_rates(torch, ex, stream, o_saves, o_loads, payload, o_steps, 2, barrier)
+        o_ms = max_over_ranks(r["total_ms"])
+        other = {"block_ids": o_order, "steps": o_steps,
+                 "GBps": round(world * 2 * payload * o_steps / (o_ms / 1e3) / 1e9, 3),
+                 "save_GBps": round(min_over_ranks(r["save_GBps"]), 3),
+                 "load_GBps": round(min_over_ranks(r["load_GBps"]), 3),
+                 "p50_load_ms": round(max_over_ranks(r["p50_load_ms"]), 3),
+                 "verified": ranks.all_true(restored(torch, tensors, o_src, o_dst)
+                                            and pool_matches(torch, tensors, o_saves, pool, o_src))}
 
     # ---- e2e through the engine API (host wall clock) ------------------------
     e2e_steps = args.e2e_steps or args.steps
@@ -947,8 +1213,6 @@ def main() -> int:
                                    cache_streaming=1 if args.cache_streaming else 0,
                                    first_chunk_bytes=args.first_chunk_mib << 20))
     names = [f"model.layers.{i}.self_attn" for i in range(len(tensors))]
-    from pegaflow_b200 import Layout
-
     for nm, t in zip(names, tensors):
         lay = Layout.from_tensor(t)
         eng.register_context_layer(f"bench{rank}", "bench", local, nm, lay.data_ptr, lay.size_bytes, lay.num_blocks,
@@ -977,6 +1241,7 @@ def main() -> int:
     for k in range(args.warmup):
         e2e_step(-1 - k)
     eng.executor(local).reset_stats()  # host time of the timed calls only (no first-call allocations)
+    scribble(torch, tensors, dst)
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -987,6 +1252,7 @@ def main() -> int:
     e2e_value = world * 2 * payload * e2e_steps / e2e_wall / 1e9
     e2e_load_p50 = max_over_ranks(statistics.median([b for _, b, _ in e2e_times]) * 1e3)
     e2e_first_layer_p50 = max_over_ranks(statistics.median([f for _, _, f in e2e_times]) * 1e3)
+    verified_e2e = ranks.all_true(restored(torch, tensors, src, dst))
     eng_metrics = eng.metrics()
     eng_ex = eng.executor(local).stats()
     eng_metrics["executor_host_ms_per_call"] = eng_ex["host_ms"] / max(1, 2 * e2e_steps)
@@ -995,6 +1261,8 @@ def main() -> int:
     # ---- the reference's copy strategy on the same GPU ------------------------
     ref = None
     if not args.no_refcopy:
+        scribble(torch, tensors, dst)
+        torch.cuda.synchronize()
         t0 = time.perf_counter()
         refcopy_save(local, saves)
         t1 = time.perf_counter()
@@ -1003,31 +1271,59 @@ def main() -> int:
         ref = {"save_GBps": round(payload / (t1 - t0) / 1e9, 3), "load_GBps": round(payload / (t2 - t1) / 1e9, 3),
                "value": round(2 * payload / (t2 - t0) / 1e9, 3), "load_ms": round((t2 - t1) * 1e3, 3),
                "h2d_runs": runs, "d2h_copies": sum(len(s.block_idx) * (2 if s.layout.split else 1) for s in saves),
+               "verified": restored(torch, tensors, src, dst),
                "how": "per-segment synchronous D2H (gpu_worker.rs:343-360) + merged-run async H2D "
-                      "(transfer.rs:116-198), restated in C++, same GPU and pool"}
+                      "(transfer.rs:116-198), restated in C++, same GPU and pool; rank 0's figures"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = CpuWorkload(wl, os.cpu_count() or 1).rate(args.cpu_seconds)
+        cpu = CpuWorkload(wl, os.cpu_count() or 1, order=args.order).rate(args.cpu_seconds)
         # The same copies with the pool in page-locked memory, cacheable and
         # write-combined (shorter samples; reported beside the baseline).
         cpu["pool_variants_GBps"] = {}
         for kind in ("pinned", "pinned_wc"):
-            cw = CpuWorkload(wl, os.cpu_count() or 1, pool=kind)
+            cw = CpuWorkload(wl, os.cpu_count() or 1, pool=kind, order=args.order)
             cpu["pool_variants_GBps"][kind] = cw.rate(args.cpu_seconds / 4)["value"]
             cw.close()
 
+    pool.close()
+    cfg1 = None
+    if world == 1 and args.workload == "llama70b_tp" and not args.no_extra:
+        del tensors, saves, loads
+        torch.cuda.empty_cache()
+        cfg1 = configs1_block(torch, args, ex, local)
+
+    # P/D handoff check: rank 0 alone, GPU0 -> GPU1; the others wait on the
+    # host so no collective kernel of theirs sits on GPU1 meanwhile.
+    pd = None
+    if world >= 2 and not args.no_extra:
+        ranks.host_barrier()
+        if rank == 0:
+            pd = pd_check(torch, ex)
+        ranks.host_barrier()
+
     if rank == 0:
+        verified = bool(verified_main and verified_e2e and (other is None or other["verified"])
+                        and (cfg1 is None or all(cfg1[o]["verified"] for o in ("shuffled", "sorted")))
+                        and (pd is None or pd["verified"]) and (ref is None or ref["verified"]))
+        achieved = min(kernel_all)
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded ~N(0,1) bf16 KV)",
-            "config": config_block(args, wl),
+            "config": config_block(args, wl, world),
+            "verified": verified,
+            "verified_how": "destination blocks zeroed before each timed region, then every restored block "
+                            "compared bit for bit with its source on the GPU (torch.equal), every rank; pool "
+                            "K/V regions of the first and last layer compared with the source blocks",
             "per_gpu_GBps": round(value / world, 3),
             "save_GBps": round(save_gbps, 3), "load_GBps": round(load_gbps, 3), "p50_load_ms": round(p50_load, 3),
             "payload_bytes_per_direction": payload,
             "host_link": {"peak_h2d_GBps": link["h2d"], "peak_d2h_GBps": link["d2h"],
                           "save_frac": round(save_frac, 3), "load_frac": round(load_frac, 3),
+                          "save_frac_alone": round(save_frac_alone, 3), "load_frac_alone": round(load_frac_alone, 3),
+                          "per_rank_alone_d2h_GBps": [round(x, 2) for x in alone_d2h_all],
+                          "per_rank_alone_h2d_GBps": [round(x, 2) for x in alone_h2d_all],
                           "per_rank_peak_d2h_GBps": [round(x, 2) for x in link_d2h_all],
                           "per_rank_peak_h2d_GBps": [round(x, 2) for x in link_h2d_all],
                           "aligned": {
@@ -1037,27 +1333,35 @@ def main() -> int:
                               "load_frac_min": round(min(a / p for a, p in zip(al_load_all, link_h2d_all)), 3),
                               "how": "saves alone, then loads alone, started on every rank at once (median "
                                      "of 3); each rank against its own concurrent peak"},
-                          "how": "pinned 1 GiB cudaMemcpyAsync, best of 3, every rank copying at once; "
-                                 "peak_* are rank 0's; *_frac = min over ranks of the step's save (load) rate "
-                                 "over that rank's own peak"},
-            "roofline": {"bound": "hbm", "achieved": round(kernel_gbps, 1) if kernel_gbps else None,
-                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(kernel_gbps / peaks["hbm_gbs"], 3) if kernel_gbps else None,
+                          "how": "pinned 1 GiB cudaMemcpyAsync, best of 3; *_alone: each rank measured while "
+                                 "the others wait; peak_* / per_rank_peak_*: every rank copying at once; "
+                                 "*_frac = min over ranks of the step's save (load) rate over that rank's own "
+                                 "concurrent peak, *_frac_alone over its own single-GPU peak"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 3),
                          "traffic": traffic_per_launch(st["kernel_bytes"] / max(1, st["timed_launches"])),
-                         "traffic_how": "ncu dram__bytes_read.sum + dram__bytes_write.sum per payload byte "
-                                        "(128 MiB chunks) x this run's average launch; writes still in L2 "
-                                        "at kernel end are not counted",
+                         "traffic_how": "not measured per run: ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                                        "per payload byte from one capture (128 MiB chunks), scaled to this run's "
+                                        "average launch; writes still in L2 at kernel end are not counted",
                          "peak_source": peaks["source"],
                          "kernel": "kv_copy_kernel (pack+unpack)",
                          "bytes_per_launch": round(st["kernel_bytes"] / max(1, st["timed_launches"])),
-                         "avg_launch_us": round(st["kernel_ms"] * 1e3 / max(1, st["timed_launches"]), 2)},
-            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": payload,
-                    "d2h_bytes_per_step": payload, "p50_load_ms": round(e2e_load_p50, 3),
+                         "avg_launch_us": round(max(launch_us_all), 2),
+                         "achieved_per_rank": [round(x, 1) for x in kernel_all],
+                         "how": "algorithmic bytes (payload read + written per launch) / CUDA-event launch "
+                                "duration over the timed region; the slowest rank's figure"},
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": payload * world,
+                    "d2h_bytes_per_step": payload * world, "p50_load_ms": round(e2e_load_p50, 3),
                     "p50_first_layer_ms": round(e2e_first_layer_p50, 3), "steps": e2e_steps,
-                    "api": "PegaEngine.batch_save_kv_blocks + batch_load_kv_blocks + PyLoadState"},
+                    "verified": verified_e2e,
+                    "api": "PegaEngine.batch_save_kv_blocks + batch_load_kv_blocks + PyLoadState, one engine "
+                           "per rank"},
             "gpu_launches": st["kernel_launches"],
             "host_cpus": (f"{len(cpus)} CPUs local to the GPU (NVML affinity)" if cpus else "unbound"),
             "copy_calls": st["copy_calls"],
+            "other_order": other,
+            "configs1": cfg1,
+            "pd": pd,
             "reference_copy_path": ref,
             "cpu_baseline": cpu,
             "clocks": clocks,

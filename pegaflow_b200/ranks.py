@@ -22,6 +22,7 @@ class Ranks:
     world: int
     local: int
     backend: str | None
+    _host_group: object = None
 
     @classmethod
     def from_env(cls, backend: str | None = None, timeout_s: float = 600.0) -> "Ranks":
@@ -41,6 +42,10 @@ class Ranks:
                 kw["device_id"] = torch.device(f"cuda:{local}")
             dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s), **kw)
             r.backend = backend
+            # Host-side group for waits while another rank works on a GPU this
+            # rank also uses: a rank parked in it runs no kernel.
+            r._host_group = (dist.new_group(backend="gloo", timeout=timedelta(seconds=timeout_s))
+                             if backend != "gloo" else None)
         return r
 
     def _reduce(self, x: float, op: str) -> float:
@@ -81,6 +86,19 @@ class Ranks:
             import torch.distributed as dist
 
             dist.barrier()
+
+    def host_barrier(self) -> None:
+        """A barrier that waits on the host only (gloo), never in a GPU
+        kernel: ranks parked here while rank 0 runs kernels on their GPUs
+        (the P/D check) hold no spinning collective kernel there."""
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(group=getattr(self, "_host_group", None))
+
+    def all_true(self, flag: bool) -> bool:
+        """True when `flag` holds on every rank."""
+        return self.min(1.0 if flag else 0.0) == 1.0
 
     def close(self) -> None:
         if self.world > 1:
@@ -131,9 +149,17 @@ def pool_region(pool_bytes: int, rank: int, world: int, align: int = 1 << 21) ->
 
 
 def block_lists(num_blocks: int, n: int, rank: int, order: str) -> tuple[np.ndarray, np.ndarray]:
-    """Seeded source and destination block ids of one rank (seeds 3+rank, 4+rank)."""
+    """Source and destination block ids of one rank, disjoint whenever
+    2n <= num_blocks, so restoring into the destinations never overwrites a
+    source and the restored blocks can be compared with the sources after
+    any number of save/load steps.
+
+    sorted: sources 0..n-1, destinations n..2n-1 (sorted-contiguous runs).
+    shuffled: one seeded permutation (seed 3+rank); its first n ids are the
+    sources and the next n the destinations."""
     if order == "sorted":
         return np.arange(n), (np.arange(n) + n) % num_blocks
-    src = np.random.default_rng(3 + rank).permutation(num_blocks)[:n]
-    dst = np.random.default_rng(4 + rank).permutation(num_blocks)[:n]
-    return src, dst
+    perm = np.random.default_rng(3 + rank).permutation(num_blocks)
+    if 2 * n <= num_blocks:
+        return perm[:n], perm[n:2 * n]
+    return perm[:n], np.random.default_rng(4 + rank).permutation(num_blocks)[:n]

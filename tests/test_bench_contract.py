@@ -56,3 +56,15 @@ def test_b200_arm_fails_loudly_without_a_gpu():
     p = run("--steps", "1", "--warmup", "0", "--no-cpu", "--no-refcopy")
     assert p.returncode != 0
     assert not p.stdout.strip()  # no JSON line from a run that did not happen
+
+
+def test_reference_arm_covers_every_tp_shard_of_the_default_workload():
+    """The default workload is configs[3] at TP=N; the reference arm times the
+    whole job on the host cores (all N head shards), like the b200 arm's value."""
+    p = run("--impl", "reference", "--gpus", "2", "--steps", "2", "--warmup", "1", "--layers", "2")
+    assert p.returncode == 0, p.stderr
+    line = last_json(p.stdout)
+    assert line["config"]["workload"] == "llama70b_tp"
+    assert line["config"]["tp"] == 2 and line["config"]["heads_per_rank"] == 4
+    assert line["n_gpus"] == 2 and line["value"] > 0
+    assert line["cpu_baseline"]["sample"].startswith("2 TP shards x 2 of 2 layers x 2048 blocks")

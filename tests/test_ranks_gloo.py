@@ -22,6 +22,13 @@ def test_shard_arithmetic():
     s0, d0 = block_lists(4096, 2048, 0, "shuffled")
     s1, _ = block_lists(4096, 2048, 1, "shuffled")
     assert len(set(s0)) == 2048 and not np.array_equal(s0, s1)
+    # Sources and destinations are disjoint, in both orders, so a restore never
+    # overwrites a source block.
+    for order in ("shuffled", "sorted"):
+        for nb, n in ((4096, 2048), (8192, 640), (256, 64)):
+            s, d = block_lists(nb, n, 0, order)
+            assert len(set(s)) == n and len(set(d)) == n and not set(s) & set(d)
+            assert max(s.max(), d.max()) < nb
 
 
 def _free_port() -> int:
@@ -57,6 +64,10 @@ def _worker(rank: int, world: int, port: int, out):
         fastest = r.min(float(r.rank + 1))
         total = r.sum(float(seg))
         assert r.gather(float(10 * r.rank + 1)) == [float(10 * i + 1) for i in range(r.world)]
+        # The bench's byte check: verified only when every rank verified.
+        assert r.all_true(ok) is ok
+        assert r.all_true(r.rank == 0) is False
+        r.host_barrier()
         out.put((r.rank, ok, slowest, fastest, total, (lo, hi)))
     finally:
         r.close()
