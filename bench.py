@@ -794,6 +794,115 @@ def run_duplex(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_one_engine(args) -> None:
+    """The reference's deployment shape for BASELINE config 3: ONE engine
+    (one server process) drives N GPUs into one shared pinned pool, as
+    pegaflow-server does with its per-device workers (gpu_worker.rs:61-93).
+    Each TP rank r registers its head shard on GPU r as tp_rank r of tp_size N
+    (slot = layer * N + r, lib.rs:204-218), so a block becomes loadable only
+    when every rank has saved it (storage.rs:161-193). One thread per rank
+    calls the engine, as the server's RPC threads do; all ranks use the same
+    block ids and hashes, as vLLM's TP workers share one block table. Per
+    step: every rank saves at once, then every rank loads at once; wall clock
+    per phase. Run as one process: python bench.py --workload
+    llama70b_tp_one_engine --gpus N [--numa-pools node|device]."""
+    import torch
+
+    from pegaflow_b200 import Layout, PegaEngine, PyLoadState
+    from pegaflow_b200.ranks import block_lists
+
+    world = args.gpus
+    if torch.cuda.device_count() < world:
+        print(json.dumps({"metric": METRIC, "workload": "llama70b_tp_one_engine",
+                          "unavailable": f"needs {world} GPUs in one process"}))
+        return
+    wl = dict(WORKLOADS["llama70b_tp"])
+    if args.layers:
+        wl["layers"] = args.layers
+    src, dst = block_lists(wl["num_blocks"], wl["blocks"], 0, args.order)
+    shards = [make_workload(torch, wl, d, d, world, args.order)[0] for d in range(world)]
+    n = len(src)
+    payload = payload_bytes(shards[0], n)  # per rank, per direction
+    torch.cuda.synchronize()
+    eng = PegaEngine(2 * world * payload + (512 << 20), enable_lfu_admission=False, numa_pools=args.numa_pools)
+    names = [f"model.layers.{i}.self_attn" for i in range(wl["layers"])]
+    for d in range(world):
+        for nm, t in zip(names, shards[d]):
+            lay = Layout.from_tensor(t)
+            eng.register_context_layer("tp", "bench", d, nm, lay.data_ptr, lay.size_bytes, lay.num_blocks,
+                                       lay.bytes_per_block, lay.kv_stride_bytes, lay.segments, d, world, len(names))
+    src_l, dst_l = src.tolist(), dst.tolist()
+
+    def phase(fn) -> float:
+        errs = []
+
+        def run(r):
+            try:
+                fn(r)
+            except Exception as e:  # reported after the join
+                errs.append(e)
+
+        ths = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+        t0 = time.perf_counter()
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        el = time.perf_counter() - t0
+        if errs:
+            raise errs[0]
+        return el
+
+    def one_step(k):
+        hashes = [f"s{k}-b{i}".encode() for i in range(n)]
+        t_save = phase(lambda r: eng.batch_save_kv_blocks("tp", r, r, [(nm, src_l, hashes) for nm in names]))
+        assert eng.count_prefix_hit_blocks("tp", hashes) == n  # sealed: every rank's slots are filled
+
+        def load(r):
+            s = PyLoadState(len(names))
+            eng.batch_load_kv_blocks("tp", r, r, s.shm_name(), names, dst_l, hashes)
+            deadline = time.perf_counter() + 120.0
+            while not s.is_ready():
+                if time.perf_counter() > deadline:
+                    raise TimeoutError("engine load did not complete within 120 s")
+            ok = s.get_state() == 1
+            s.close()
+            if not ok:
+                raise RuntimeError(f"load of rank {r} failed")
+
+        return t_save, phase(load)
+
+    for k in range(args.warmup):
+        one_step(-1 - k)
+    for sh in shards:
+        scribble(torch, sh, dst)
+    torch.cuda.synchronize()
+    times = [one_step(k) for k in range(args.steps)]
+    verified = all(restored(torch, sh, src, dst) for sh in shards)
+    m = eng.metrics()
+    eng.close()
+    save_s = statistics.median(t for t, _ in times)
+    load_s = statistics.median(t for _, t in times)
+    total = sum(a + b for a, b in times)
+    value = world * 2 * payload * len(times) / total / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total / len(times) * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded ~N(0,1) bf16 KV)",
+        "config": dict(config_block(args, wl, world), workload="llama70b_tp_one_engine",
+                       parallelism=f"tp{world} in one engine process (one thread per rank), one pool"
+                                   + ("" if args.numa_pools == "off" else f" per NUMA {args.numa_pools}")),
+        "verified": verified, "per_gpu_GBps": round(value / world, 3),
+        "save_GBps": round(world * payload / save_s / 1e9, 3), "load_GBps": round(world * payload / load_s / 1e9, 3),
+        "p50_save_ms": round(save_s * 1e3, 3), "p50_load_ms": round(load_s * 1e3, 3),
+        "payload_bytes_per_direction_per_rank": payload, "numa_pools": args.numa_pools,
+        "engine": {k: m[k] for k in ("load_failures", "cache_block_evictions", "pool_alloc_failures")},
+        "how": "host wall clock per phase (all ranks save at once, then all load at once); value = all ranks' "
+               "save + load bytes / summed phase times",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def config_block(args, wl, world: int) -> dict:
     cfg = {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
            "blocks_moved": wl["blocks"], "block_ids": args.order,
@@ -1026,8 +1135,11 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["qwen3_pd", "llama8b_fp8_evict", "llama8b_duplex"],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["qwen3_pd", "llama8b_fp8_evict", "llama8b_duplex",
+                                                               "llama70b_tp_one_engine"],
                     default="llama70b_tp")
+    ap.add_argument("--numa-pools", default="off", choices=["off", "node", "device"],
+                    help="llama70b_tp_one_engine: one pool, or one per NUMA node / per GPU")
     ap.add_argument("--fp8-requests", type=int, default=64)
     ap.add_argument("--fp8-pool-gb", type=int, default=30)
     ap.add_argument("--fp8-compute-ms", type=float, default=0.5)
@@ -1072,6 +1184,13 @@ def main() -> int:
             return 0
         if int(os.environ.get("RANK", "0")) == 0:
             run_duplex(args)
+        return 0
+    if args.workload == "llama70b_tp_one_engine":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": "llama70b_tp_one_engine",
+                              "unavailable": "engine-level scenario; the reference engine cannot be built here"}))
+            return 0
+        run_one_engine(args)
         return 0
     wl = dict(WORKLOADS[args.workload])
     if args.layers:
