@@ -907,8 +907,8 @@ def config_block(args, wl, world: int) -> dict:
     cfg = {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
            "blocks_moved": wl["blocks"], "block_ids": args.order,
            "kv_dtype": "fp16" if wl.get("separate") else "bf16",
-           "save_mode": args.save_mode, "load_mode": args.load_mode,
-           "staging": {"slot_MiB": args.chunk_mib or 512, "slots": args.slots or 2, "lanes": "save, load",
+           "save_mode": args.save_mode, "load_mode": args.load_mode, "copy_kernel": args.copy_kernel,
+           "staging": {"slot_MiB": args.chunk_mib or 1024, "slots": args.slots or 2, "lanes": "save, load",
                        "first_chunk_MiB": args.first_chunk_mib or 64, "growth": "x2 per chunk",
                        "save_first_chunk": "max(first chunk, half a slot)",
                        "load_first_chunk": "a whole slot; with per-layer flags (the e2e engine loads) "
@@ -1154,6 +1154,8 @@ def main() -> int:
     ap.add_argument("--copy-streams", type=int, default=0)
     ap.add_argument("--ctas-per-sm", type=int, default=0)
     ap.add_argument("--cache-streaming", action="store_true", help="evict-first loads/stores in the kernels")
+    ap.add_argument("--copy-kernel", default="auto", choices=["auto", "registers", "bulk"],
+                    help="how staged tiles move: registers, or TMA bulk copies through shared memory")
     ap.add_argument("--e2e-steps", type=int, default=0, help="engine-API steps (default: --steps)")
     ap.add_argument("--no-refcopy", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -1235,7 +1237,8 @@ def main() -> int:
     ex = Executor(local, save_mode=args.save_mode, load_mode=args.load_mode,
                   staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
                   copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm,
-                  cache_streaming=args.cache_streaming, first_chunk_bytes=args.first_chunk_mib << 20)
+                  cache_streaming=args.cache_streaming, first_chunk_bytes=args.first_chunk_mib << 20,
+                  copy_kernel=args.copy_kernel)
     pool = PinnedBuffer(payload + wl["layers"] * 8192 + (1 << 20), write_combined=True)
     saves, loads, _ = executor_specs(tensors, src, dst, pool.ptr)
     stream = torch.cuda.Stream(local)
@@ -1330,7 +1333,7 @@ def main() -> int:
                                    staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
                                    copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm,
                                    cache_streaming=1 if args.cache_streaming else 0,
-                                   first_chunk_bytes=args.first_chunk_mib << 20))
+                                   first_chunk_bytes=args.first_chunk_mib << 20, copy_kernel=args.copy_kernel))
     names = [f"model.layers.{i}.self_attn" for i in range(len(tensors))]
     for nm, t in zip(names, tensors):
         lay = Layout.from_tensor(t)

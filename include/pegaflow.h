@@ -90,17 +90,30 @@ typedef enum pf_transfer_mode {
   PF_MODE_DIRECT = 2  /* sm_100a kernel loads/stores mapped pinned host memory (zero-copy) */
 } pf_transfer_mode;
 
+/* How the pack/unpack kernels move a staged transfer's 4 KiB tiles:
+ * REGISTERS: each warp loads a tile into registers (8 x 16 B per lane) and
+ * stores it; BULK: TMA bulk copies (cp.async.bulk) move each tile from global
+ * memory into a shared-memory ring and back out, several tiles in flight per
+ * warp, no registers in the data path. AUTO picks BULK where it applies
+ * (staged transfers whose layers are all 16-byte aligned and that raise no
+ * per-layer flags) and REGISTERS elsewhere. */
+typedef enum pf_copy_kernel {
+  PF_COPY_KERNEL_AUTO = 0,
+  PF_COPY_KERNEL_REGISTERS = 1,
+  PF_COPY_KERNEL_BULK = 2
+} pf_copy_kernel;
+
 typedef struct pf_executor_config {
   /* Saves and loads each have their own staging slots (allocated on first
    * use), so a save and a load on two streams run at the same time. */
-  uint64_t staging_chunk_bytes; /* slot size, 0 = default (512 MiB) */
+  uint64_t staging_chunk_bytes; /* slot size, 0 = default (1 GiB) */
   uint32_t staging_slots;       /* slots per direction, 0 = default (2) */
   uint32_t save_mode;           /* pf_transfer_mode */
   uint32_t load_mode;           /* pf_transfer_mode */
   uint32_t ctas_per_sm;         /* 0 = default */
   uint32_t copy_streams;        /* 0 = default (2) */
   uint32_t cache_streaming;     /* 1 = evict-first loads/stores in the kernels */
-  uint32_t reserved0;
+  uint32_t copy_kernel;         /* pf_copy_kernel: how staged tiles move through the SM */
   /* Size limit of the first staged chunk of a load; each later chunk may be
    * twice the previous one, up to staging_chunk_bytes. A small first chunk
    * raises the first per-layer flags early; large later chunks keep the

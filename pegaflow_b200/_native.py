@@ -39,6 +39,10 @@ PF_ERR_LOAD_STATE = 8
 PF_ERR_TIMEOUT = 9
 PF_ERR_NO_SPACE = 10
 
+PF_COPY_KERNEL_AUTO = 0
+PF_COPY_KERNEL_REGISTERS = 1
+PF_COPY_KERNEL_BULK = 2
+
 PF_MODE_AUTO = 0
 PF_MODE_STAGED = 1
 PF_MODE_DIRECT = 2
@@ -69,7 +73,7 @@ class ExecutorConfig(Structure):
         ("ctas_per_sm", c_uint32),
         ("copy_streams", c_uint32),
         ("cache_streaming", c_uint32),
-        ("reserved0", c_uint32),
+        ("copy_kernel", c_uint32),
         ("first_chunk_bytes", c_uint64),
     ]
 

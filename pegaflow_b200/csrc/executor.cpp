@@ -91,6 +91,35 @@ Executor::Executor(int device, const pf_executor_config& cfg) : device_(device),
   cuda_check(cudaStreamCreateWithFlags(&save_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
   init_lane(save_lane_);
   init_lane(load_lane_);
+  if (cfg_.copy_kernel != PF_COPY_KERNEL_REGISTERS) {
+    bulk_ = bulk_copy_ready();
+    if (!bulk_ && cfg_.copy_kernel == PF_COPY_KERNEL_BULK) {
+      throw cuda_init("the bulk copy kernel cannot run on device " + std::to_string(device));
+    }
+  }
+  void* st = nullptr;
+  cuda_check(cudaHostAlloc(&st, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc(status)");
+  status_host_ = static_cast<volatile int*>(st);
+  *status_host_ = 0;
+  void* dev = nullptr;
+  cuda_check(cudaHostGetDevicePointer(&dev, st, 0), "cudaHostGetDevicePointer(status)");
+  status_dev_ = static_cast<int*>(dev);
+}
+
+bool Executor::use_bulk(const Built& b) const {
+  if (!bulk_) return false;
+  for (const PlanLayer& p : b.layers) {
+    if ((p.flags & kFlagVector) == 0) return false;
+  }
+  return true;
+}
+
+void Executor::check_kernel_status() {
+  if (status_host_ && *status_host_) {
+    *status_host_ = 0;
+    throw storage_error("a bulk copy kernel gave up waiting for a tile copy (1 s); the copies of that call "
+                        "are incomplete");
+  }
 }
 
 void Executor::init_lane(Lane& l) {
@@ -157,6 +186,7 @@ Executor::~Executor() {
   destroy_lane(load_lane_);
   cudaStreamDestroy(own_stream_);
   cudaStreamDestroy(save_stream_);
+  if (status_host_) cudaFreeHost(const_cast<int*>(status_host_));
   cudaGetLastError();
 }
 
@@ -327,11 +357,12 @@ int Executor::grid_for(uint64_t tiles) const {
 }
 
 void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_begin, uint64_t tile_end,
-                      int64_t shift, cudaStream_t s) {
+                      int64_t shift, cudaStream_t s, bool bulk) {
   CopyArgs a = args0;
   a.tile_begin = tile_begin;
   a.tile_end = tile_end;
   a.side_shift = shift;
+  a.status = status_dev_;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   {
     std::lock_guard<std::mutex> g(stats_mu_);
@@ -352,8 +383,12 @@ void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_
     }
   }
   if (e0) cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
-  cuda_check(launch_copy(dir, table, a, grid_for(tile_end - tile_begin), s, cfg_.cache_streaming != 0),
-             "kernel launch");
+  if (bulk && !table && a.layer_tiles_done == nullptr) {
+    cuda_check(launch_bulk_copy(dir, a, num_sms_, s), "kernel launch");
+  } else {
+    cuda_check(launch_copy(dir, table, a, grid_for(tile_end - tile_begin), s, cfg_.cache_streaming != 0),
+               "kernel launch");
+  }
   if (e1) {
     cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
     std::lock_guard<std::mutex> g(stats_mu_);
@@ -425,6 +460,7 @@ uint64_t Executor::copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool
 void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t caller) {
   HostTimer timer{&stats_.host_ms, &stats_mu_};
   DeviceGuard on(device_);
+  check_kernel_status();
   const bool staged = cfg_.save_mode != PF_MODE_DIRECT;
   Built b;
   build_save(layers, n_layers, staged, &b);
@@ -457,13 +493,14 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
     // 0.1 ms for 256 MiB) and saves kernel launches.
     std::vector<Chunk> chunks;
     make_chunks(b, std::max(first_chunk_, slot_bytes_ / 2), &chunks);
+    const bool bulk = use_bulk(b);
     for (size_t k = 0; k < chunks.size(); ++k) {
       const uint32_t si = static_cast<uint32_t>(k % slots_);
       uint8_t* slot = staging + static_cast<uint64_t>(si) * slot_bytes_;
       if (k >= slots_) cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_drained[si], 0), "cudaStreamWaitEvent");
       const int64_t shift = static_cast<int64_t>(reinterpret_cast<uint64_t>(slot)) -
                             static_cast<int64_t>(chunks[k].dense_begin);
-      launch(kPack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, L.kstream);
+      launch(kPack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, L.kstream, bulk);
       cuda_check(cudaEventRecord(L.ev_filled[si], L.kstream), "cudaEventRecord");
       cudaStream_t cs = L.cstreams[k % L.cstreams.size()];
       cuda_check(cudaStreamWaitEvent(cs, L.ev_filled[si], 0), "cudaStreamWaitEvent");
@@ -484,6 +521,7 @@ void Executor::save(const pf_save_layer* layers, uint64_t n_layers, cudaStream_t
 void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t caller, int64_t* layer_done) {
   HostTimer timer{&stats_.host_ms, &stats_mu_};
   DeviceGuard on(device_);
+  check_kernel_status();
   const bool staged = cfg_.load_mode != PF_MODE_DIRECT;
   Built b;
   build_load(layers, n_layers, staged, &b);
@@ -548,6 +586,7 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
                                       : slot_bytes_;
     std::vector<Chunk> chunks;
     make_chunks(b, first, &chunks);
+    const bool bulk = layer_done == nullptr && use_bulk(b);
     for (size_t k = 0; k < chunks.size(); ++k) {
       const uint32_t si = static_cast<uint32_t>(k % slots_);
       uint8_t* slot = staging + static_cast<uint64_t>(si) * slot_bytes_;
@@ -558,7 +597,7 @@ void Executor::load(const pf_load_layer* layers, uint64_t n_layers, cudaStream_t
       cuda_check(cudaStreamWaitEvent(L.kstream, L.ev_filled[si], 0), "cudaStreamWaitEvent");
       const int64_t shift = static_cast<int64_t>(reinterpret_cast<uint64_t>(slot)) -
                             static_cast<int64_t>(chunks[k].dense_begin);
-      launch(kUnpack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, L.kstream);
+      launch(kUnpack, false, args, chunks[k].tile_begin, chunks[k].tile_end, shift, L.kstream, bulk);
       cuda_check(cudaEventRecord(L.ev_drained[si], L.kstream), "cudaEventRecord");
     }
     kernel_bytes = 2 * b.total_bytes;  // into the slot, then out of it
@@ -580,12 +619,14 @@ void Executor::save_sync(const pf_save_layer* layers, uint64_t n_layers) {
   DeviceGuard on(device_);
   save(layers, n_layers, save_stream_);
   cuda_check(cudaStreamSynchronize(save_stream_), "cudaStreamSynchronize(save)");
+  check_kernel_status();
 }
 
 void Executor::load_sync(const pf_load_layer* layers, uint64_t n_layers, int64_t* layer_done) {
   DeviceGuard on(device_);
   load(layers, n_layers, own_stream_, layer_done);
   cuda_check(cudaStreamSynchronize(own_stream_), "cudaStreamSynchronize(load)");
+  check_kernel_status();
 }
 
 void Executor::stats(pf_executor_stats* out) {

@@ -17,10 +17,12 @@
 namespace pf {
 
 // Staging defaults. While the copy engines stream a D2H/H2D, every kernel
-// launch on the device pays a fixed latency of tens of microseconds, so the
-// chunk schedule (first chunk, doubling to the slot size) trades 1 GiB of HBM
-// for five launches per direction on a 1.25 GiB transfer instead of twenty.
-constexpr uint64_t kDefaultSlotBytes = 512ull << 20;
+// launch on the device pays a fixed latency of 30-45 microseconds (the kernel
+// itself runs no slower), so the chunk schedule (first chunk, doubling to the
+// slot size) spends HBM on few, large launches: two 1 GiB slots per lane move
+// a 10 GiB direction in ten or eleven launches, and a 1.25 GiB direction in
+// two. On a 180 GB B200 the two lanes' 4 GiB are 2.2% of HBM.
+constexpr uint64_t kDefaultSlotBytes = 1024ull << 20;
 constexpr uint32_t kDefaultSlots = 2;
 constexpr uint64_t kDefaultFirstChunkBytes = 64ull << 20;
 // Lower bound of a layer-wise load's first chunk (which holds layer 0 and
@@ -95,7 +97,11 @@ class Executor {
   uint8_t* lane_staging(Lane& l);
   CopyArgs upload(Lane& l, const Built& b, bool with_counters);
   void launch(Dir dir, bool table, const CopyArgs& args, uint64_t tile_begin,
-              uint64_t tile_end, int64_t shift, cudaStream_t s);
+              uint64_t tile_end, int64_t shift, cudaStream_t s, bool bulk = false);
+  // The bulk kernel applies: enabled, and every layer of the plan 16-byte aligned.
+  bool use_bulk(const Built& b) const;
+  // Throws if a bulk kernel gave up on a bounded wait since the last check.
+  void check_kernel_status();
   int grid_for(uint64_t tiles) const;
   // Both return the number of copy-engine copies issued.
   uint64_t copy_runs(const Built& b, const Chunk& c, uint8_t* slot, bool d2h,
@@ -107,6 +113,9 @@ class Executor {
   int device_;
   pf_executor_config cfg_;
   int num_sms_ = 148;
+  bool bulk_ = false;                  // the bulk (TMA) kernel is enabled and ready on this device
+  volatile int* status_host_ = nullptr;  // set by a bulk kernel whose bounded wait ran out
+  int* status_dev_ = nullptr;          // device view of the same word
   cudaStream_t own_stream_ = nullptr;   // blocking loads and peer copies
   cudaStream_t save_stream_ = nullptr;  // blocking saves
   uint64_t slot_bytes_ = 0;

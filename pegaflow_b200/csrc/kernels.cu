@@ -21,6 +21,7 @@
 // the plan it is given.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "plan.h"
@@ -186,6 +187,181 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) kv_copy_kernel(const 
   flush_layer(a, l, Lp->tile_count, Lp->done_index, done_in_layer, lane);
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy variant (TMA engine, no registers in the data path)
+// ---------------------------------------------------------------------------
+// One CTA per SM, kBulkWarps warps. Each warp owns a ring of kBulkStages
+// 4 KiB stages in shared memory with one mbarrier per stage, and walks its
+// tiles (the same CTA ranges and warp interleave as kv_copy_kernel) as a
+// software pipeline run by lane 0: the bulk load of tile j is issued
+// kBulkAhead tiles before its bulk store, so kBulkAhead x 4 KiB per warp are
+// in flight on the load side while earlier stores drain. The 32 lanes decode
+// the tiles 32 at a time (layer, unit, block id -> addresses) into a
+// double-buffered descriptor table in shared memory, so the block-id loads of
+// a batch overlap instead of sitting in lane 0's issue loop.
+//
+// Every wait on an mbarrier is bounded by time; a wait that runs out sets
+// *status and the warp stops issuing, waits (bounded) for the loads it has in
+// flight and returns, so the host sees an error instead of a hung stream.
+constexpr int kBulkWarps = 6;
+constexpr int kBulkThreads = kBulkWarps * 32;
+constexpr int kBulkStages = 8;
+constexpr int kBulkAhead = 6;
+static_assert(kBulkAhead < kBulkStages, "a stage is reloaded only after its store has read it");
+constexpr unsigned long long kBulkWaitNs = 1000000000ull;  // 1 s per mbarrier wait
+
+struct BulkDesc {
+  uint64_t src;
+  uint64_t dst;
+  uint32_t bytes;
+  uint32_t pad[3];
+};
+static_assert(sizeof(BulkDesc) == 32, "BulkDesc layout");
+
+constexpr size_t kBulkStageBytes = size_t(kBulkWarps) * kBulkStages * kTileBytes;
+constexpr size_t kBulkBarBytes = size_t(kBulkWarps) * kBulkStages * sizeof(uint64_t);
+constexpr size_t kBulkDescBytes = size_t(kBulkWarps) * 64 * sizeof(BulkDesc);
+constexpr size_t kBulkSmemBytes = kBulkStageBytes + kBulkBarBytes + kBulkDescBytes;
+static_assert(kBulkSmemBytes <= 227 * 1024, "bulk kernel shared memory");
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// true once the phase with `parity` has completed; false after kBulkWaitNs.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (global_ns() - t0 > kBulkWaitNs) return false;
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int DIR>
+__global__ void __launch_bounds__(kBulkThreads, 1) kv_bulk_kernel(const CopyArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  unsigned char* stages = g_smem + size_t(warp) * kBulkStages * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(g_smem + kBulkStageBytes) + warp * kBulkStages;
+  BulkDesc* descs = reinterpret_cast<BulkDesc*>(g_smem + kBulkStageBytes + kBulkBarBytes) + warp * 64;
+
+  const uint64_t total = a.tile_end - a.tile_begin;
+  const uint64_t per_cta = (total + gridDim.x - 1) / gridDim.x;
+  const uint64_t cta_begin = a.tile_begin + (uint64_t)blockIdx.x * per_cta;
+  uint64_t cta_end = cta_begin + per_cta;
+  if (cta_end > a.tile_end) cta_end = a.tile_end;
+  const uint64_t first = cta_begin + (uint64_t)warp;
+  if (first >= cta_end) return;
+  const uint64_t n = (cta_end - first + kBulkWarps - 1) / kBulkWarps;  // this warp's tiles
+
+  if (lane == 0) {
+    for (int st = 0; st < kBulkStages; ++st) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[st])) : "memory");
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+
+  // Lane i decodes this warp's tile k0 + i into descs[buf*32 + i].
+  auto decode = [&](uint64_t k0, int buf) {
+    const uint64_t k = k0 + (uint64_t)lane;
+    BulkDesc d{};
+    if (k < n) {
+      const uint64_t tile = first + k * kBulkWarps;
+      uint32_t lo = 0, hi = a.n_layers;
+      while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (a.layers[mid].tile_start <= tile) lo = mid; else hi = mid;
+      }
+      const PlanLayer& L = a.layers[lo];
+      const uint32_t local = (uint32_t)(tile - L.tile_start);
+      const uint32_t unit_local = local / L.tiles_per_unit;
+      const uint32_t t = local - unit_local * L.tiles_per_unit;
+      const uint32_t u = unit_local / L.n;
+      const uint32_t i = unit_local - u * L.n;
+      const uint64_t b = a.ids[L.ids_off + i];
+      const uint32_t in_unit = t * kTileBytes;
+      const uint32_t rest = L.unit_bytes - in_unit;
+      const uint64_t cache = L.cache_base + b * L.block_pitch + (uint64_t)u * L.unit_stride + in_unit;
+      const uint64_t side = a.side_base[L.side_off + u] + (uint64_t)i * L.side_pitch + in_unit + a.side_shift;
+      d.src = DIR == kPack ? cache : side;
+      d.dst = DIR == kPack ? side : cache;
+      d.bytes = rest < kTileBytes ? rest : kTileBytes;
+    }
+    descs[buf * 32 + lane] = d;
+    __syncwarp();
+  };
+
+  decode(0, 0);
+  uint64_t loads_issued = 0, stores_issued = 0;
+  int bad = 0;
+  for (uint64_t j = 0; j < n + kBulkAhead && !bad; ++j) {
+    if (j < n && j > 0 && (j & 31) == 0) decode(j, (int)((j >> 5) & 1));
+    if (lane == 0) {
+      if (j < n) {
+        // Stage j % S was last read by the store of tile j - S; at most
+        // S - A - 1 newer stores may still be reading their stages.
+        const BulkDesc& d = descs[((j >> 5) & 1) * 32 + (j & 31)];
+        const uint32_t st = (uint32_t)(j % kBulkStages);
+        const uint32_t bar = smem_u32(&bars[st]);
+        bulk_wait_read<kBulkStages - kBulkAhead - 1>();
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(d.bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(smem_u32(stages + (size_t)st * kTileBytes)), "l"(d.src), "r"(d.bytes), "r"(bar)
+                     : "memory");
+        loads_issued = j + 1;
+      }
+      if (j >= kBulkAhead) {
+        const uint64_t t = j - kBulkAhead;
+        const BulkDesc& d = descs[((t >> 5) & 1) * 32 + (t & 31)];
+        const uint32_t st = (uint32_t)(t % kBulkStages);
+        if (mbar_wait(smem_u32(&bars[st]), (uint32_t)((t / kBulkStages) & 1))) {
+          asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                       ::"l"(d.dst), "r"(smem_u32(stages + (size_t)st * kTileBytes)), "r"(d.bytes)
+                       : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          stores_issued = t + 1;
+        } else {
+          bad = 1;
+        }
+      }
+    }
+    bad = __shfl_sync(0xffffffffu, bad, 0);
+  }
+  if (lane == 0) {
+    if (bad) {
+      if (a.status) {
+        *reinterpret_cast<volatile int*>(a.status) = 1;
+        __threadfence_system();
+      }
+      // Loads still in flight land in this warp's stages: wait for them
+      // (bounded) before the CTA's shared memory can be reused.
+      for (uint64_t t = stores_issued; t < loads_issued; ++t) {
+        mbar_wait(smem_u32(&bars[t % kBulkStages]), (uint32_t)((t / kBulkStages) & 1));
+      }
+    }
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  }
+  __syncwarp();
+}
+
 // Runtime flags -> template instance.
 template <int DIR, bool TABLE, bool SMEM>
 void launch_cs(bool cs, const CopyArgs& a, int grid, size_t shm, cudaStream_t s) {
@@ -225,6 +401,37 @@ int copy_kernel_resident_ctas() {
   take(reinterpret_cast<const void*>(&kv_copy_kernel<kPack, true, true, true>), kMaxSmemTableBytes);
   take(reinterpret_cast<const void*>(&kv_copy_kernel<kPack, false, false, false>), 0);
   return lowest;
+}
+
+bool bulk_copy_ready() {
+  for (const void* fn : {reinterpret_cast<const void*>(&kv_bulk_kernel<kPack>),
+                         reinterpret_cast<const void*>(&kv_bulk_kernel<kUnpack>)}) {
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemBytes) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kBulkThreads, kBulkSmemBytes) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      return false;
+    }
+  }
+  return true;
+}
+
+uint64_t bulk_tiles_per_cta() { return uint64_t(kBulkWarps) * 2 * kBulkStages; }
+
+cudaError_t launch_bulk_copy(Dir dir, const CopyArgs& args, int num_sms, cudaStream_t stream) {
+  if (args.tile_end <= args.tile_begin) return cudaSuccess;
+  const uint64_t tiles = args.tile_end - args.tile_begin;
+  const uint64_t need = (tiles + bulk_tiles_per_cta() - 1) / bulk_tiles_per_cta();
+  const int grid = static_cast<int>(std::max<uint64_t>(1, std::min<uint64_t>(need, (uint64_t)num_sms)));
+  if (dir == kPack) {
+    kv_bulk_kernel<kPack><<<grid, kBulkThreads, kBulkSmemBytes, stream>>>(args);
+  } else {
+    kv_bulk_kernel<kUnpack><<<grid, kBulkThreads, kBulkSmemBytes, stream>>>(args);
+  }
+  return cudaGetLastError();
 }
 
 cudaError_t launch_copy(Dir dir, bool table, const CopyArgs& args, int grid,

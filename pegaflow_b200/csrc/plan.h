@@ -65,6 +65,7 @@ struct CopyArgs {
   int64_t side_shift;           // added to affine side addresses (staging slot)
   uint32_t n_layers;
   uint32_t pad;
+  int* status;                  // bulk kernel: set to 1 when a bounded wait gave up, or null
 };
 
 // Directions.
@@ -75,6 +76,17 @@ enum Dir : int { kPack = 0, kUnpack = 1 };
 // evict-first (.cs) loads and stores.
 cudaError_t launch_copy(Dir dir, bool table, const CopyArgs& args, int grid,
                         cudaStream_t stream, bool streaming = false);
+
+// The bulk-copy variant: tiles move through shared memory with TMA bulk
+// copies (cp.async.bulk global -> shared -> global) instead of registers.
+// Only for affine launches (no table) whose layers are all 16-byte aligned
+// and that raise no per-layer flags; one CTA per SM.
+cudaError_t launch_bulk_copy(Dir dir, const CopyArgs& args, int num_sms, cudaStream_t stream);
+// Prepares the bulk kernels on the current device (their shared-memory
+// size); false when the device cannot run them.
+bool bulk_copy_ready();
+// Tiles the bulk kernel keeps per CTA before it uses fewer CTAs.
+uint64_t bulk_tiles_per_cta();
 
 // CTAs of kv_copy_kernel resident per SM on the current device (the lowest
 // over its instances); grids beyond SMs x this run as a partial second wave.

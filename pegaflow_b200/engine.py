@@ -70,8 +70,14 @@ class PegaEngine:
             cfg.pre_evict_threshold_bytes, cfg.pre_evict_target_bytes, cfg.pre_evict_interval_ms = pre_evict
         if executor:
             modes = {"auto": N.PF_MODE_AUTO, "staged": N.PF_MODE_STAGED, "direct": N.PF_MODE_DIRECT}
+            kernels = {"auto": N.PF_COPY_KERNEL_AUTO, "registers": N.PF_COPY_KERNEL_REGISTERS,
+                       "bulk": N.PF_COPY_KERNEL_BULK}
             for k, v in executor.items():
-                setattr(cfg.executor, k, modes[v] if k.endswith("_mode") else v)
+                if k.endswith("_mode"):
+                    v = modes[v]
+                elif k == "copy_kernel" and isinstance(v, str):
+                    v = kernels[v]
+                setattr(cfg.executor, k, v)
         root = dfs_root.encode() if dfs_root else None  # kept alive across the create call
         cfg.dfs_root = root
         cfg.dfs_quota_bytes = dfs_quota

@@ -18,6 +18,8 @@ import numpy as np
 from . import _native as N
 
 _MODES = {"auto": N.PF_MODE_AUTO, "staged": N.PF_MODE_STAGED, "direct": N.PF_MODE_DIRECT}
+_COPY_KERNELS = {"auto": N.PF_COPY_KERNEL_AUTO, "registers": N.PF_COPY_KERNEL_REGISTERS,
+                 "bulk": N.PF_COPY_KERNEL_BULK}
 
 
 @dataclass(frozen=True)
@@ -176,6 +178,7 @@ class Executor:
         copy_streams: int = 0,
         cache_streaming: bool = False,
         first_chunk_bytes: int = 0,
+        copy_kernel: str = "auto",
         _handle: Optional[int] = None,
     ):
         self.device_id = device_id
@@ -198,6 +201,7 @@ class Executor:
         cfg.cache_streaming = 1 if cache_streaming else 0
         if first_chunk_bytes:
             cfg.first_chunk_bytes = first_chunk_bytes
+        cfg.copy_kernel = _COPY_KERNELS[copy_kernel]
         h = c_void_p()
         N.check(N.lib.pf_executor_create(device_id, byref(cfg), byref(h)))
         self._h = h

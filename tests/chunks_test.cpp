@@ -114,25 +114,39 @@ int main() {
     ++cases;
   }
 
-  // The benchmark's schedules for one 1.25 GiB direction: 32 layers of 640
-  // blocks x (K, V) x 32 KiB, 512 MiB slots.
+  // The benchmark's schedules. configs[1]: one 1.25 GiB direction of 32
+  // layers of 640 blocks x (K, V) x 32 KiB; configs[3] at TP1: 10 GiB of 80
+  // layers of 2048 blocks x (K, V) x 32 KiB. Default 1 GiB slots, and the
+  // earlier 512 MiB slots.
   const Case llama = make_case(std::vector<std::pair<uint32_t, uint32_t>>(32, {32768, 2}), 640);
-  const uint64_t slot = 512ull << 20;
+  const Case llama70 = make_case(std::vector<std::pair<uint32_t, uint32_t>>(80, {32768, 2}), 2048);
+  const uint64_t m512 = 512ull << 20, g1 = 1024ull << 20;
   struct Want {
+    const Case* c;
+    uint64_t slot;
     uint64_t first;
     std::vector<uint64_t> mib;
   };
+  std::vector<uint64_t> tp1_loads(10, 1024), tp1_saves(9, 1024);
+  tp1_saves.insert(tp1_saves.begin(), 512);
+  tp1_saves.push_back(512);
   const Want wants[] = {
-      {64ull << 20, {64, 128, 256, 512, 320}},     // growth from 64 MiB
-      {slot, {512, 512, 256}},                      // loads without per-layer flags: whole slots
-      {slot / 2, {256, 512, 512}},                  // saves: half a slot first
-      {40ull << 20, {40, 80, 160, 320, 512, 168}},  // a layer-wise load: first chunk = one 40 MiB layer
+      {&llama, m512, 64ull << 20, {64, 128, 256, 512, 320}},     // growth from 64 MiB
+      {&llama, m512, m512, {512, 512, 256}},                      // loads without per-layer flags: whole slots
+      {&llama, m512, m512 / 2, {256, 512, 512}},                  // saves: half a slot first
+      {&llama, m512, 40ull << 20, {40, 80, 160, 320, 512, 168}},  // layer-wise load: first chunk = one layer
+      {&llama, g1, g1, {1024, 256}},                              // default slots: loads without flags
+      {&llama, g1, g1 / 2, {512, 768}},                           // default slots: saves
+      {&llama, g1, 40ull << 20, {40, 80, 160, 320, 640, 40}},     // default slots: layer-wise load
+      {&llama70, g1, g1, tp1_loads},                              // configs[3] TP1 loads: ten whole slots
+      {&llama70, g1, g1 / 2, tp1_saves},                          // configs[3] TP1 saves
   };
   for (const Want& w : wants) {
     std::vector<Chunk> ch;
-    cut_chunks(llama.layers, llama.total_tiles, slot, w.first, &ch);
-    if (*check(llama, slot, w.first, ch) || spans_mib(ch) != w.mib) {
-      std::printf("FAIL schedule with first chunk %llu MiB:", static_cast<unsigned long long>(w.first >> 20));
+    cut_chunks(w.c->layers, w.c->total_tiles, w.slot, w.first, &ch);
+    if (*check(*w.c, w.slot, w.first, ch) || spans_mib(ch) != w.mib) {
+      std::printf("FAIL schedule with slot %llu MiB, first chunk %llu MiB:",
+                  static_cast<unsigned long long>(w.slot >> 20), static_cast<unsigned long long>(w.first >> 20));
       for (uint64_t m : spans_mib(ch)) std::printf(" %llu", static_cast<unsigned long long>(m));
       std::printf("\n");
       return 1;
@@ -152,8 +166,8 @@ int main() {
     const Case fp8 = make_case(spec, 265);
     const uint64_t first = layerwise_first_limit(fp8.layers, kFirst, kMin);
     std::vector<Chunk> ch;
-    cut_chunks(fp8.layers, fp8.total_tiles, slot, first, &ch);
-    if (*check(fp8, slot, first, ch) || ch[0].tile_end != fp8.layers[2].tile_start) {
+    cut_chunks(fp8.layers, fp8.total_tiles, g1, first, &ch);
+    if (*check(fp8, g1, first, ch) || ch[0].tile_end != fp8.layers[2].tile_start) {
       std::printf("FAIL fp8 first chunk: limit %llu, ends at tile %llu, layer 1 of KV starts at %llu\n",
                   static_cast<unsigned long long>(first), static_cast<unsigned long long>(ch[0].tile_end),
                   static_cast<unsigned long long>(fp8.layers[2].tile_start));
@@ -163,7 +177,7 @@ int main() {
   {
     const uint64_t first = layerwise_first_limit(llama.layers, kFirst, kMin);  // one 40 MiB layer
     std::vector<Chunk> ch;
-    cut_chunks(llama.layers, llama.total_tiles, slot, first, &ch);
+    cut_chunks(llama.layers, llama.total_tiles, g1, first, &ch);
     if (first != (40ull << 20) || ch[0].tile_end != llama.layers[1].tile_start) {
       std::printf("FAIL llama first chunk %llu\n", static_cast<unsigned long long>(first));
       return 1;

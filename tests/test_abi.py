@@ -33,7 +33,8 @@ def test_abi_version(native):
 def test_config_defaults(native):
     """Library defaults: the reference's 30 GiB write-combined pool with TinyLFU
     admission (lib.rs:56, pinned_mem.rs:159, storage.rs:91), one pool (no NUMA
-    split), 2 x 512 MiB staging slots per lane."""
+    split), 2 x 1 GiB staging slots per lane, the copy kernel chosen per
+    transfer (bulk copies where they apply)."""
     from ctypes import byref
 
     e = native.EngineConfig()
@@ -42,7 +43,8 @@ def test_config_defaults(native):
     assert (e.pre_evict_enabled, e.pre_evict_threshold_bytes, e.pre_evict_target_bytes) == (0, 5 << 30, 8 << 30)
     x = native.ExecutorConfig()
     native.lib.pf_executor_config_default(byref(x))
-    assert (x.staging_chunk_bytes, x.staging_slots, x.first_chunk_bytes) == (512 << 20, 2, 64 << 20)
+    assert (x.staging_chunk_bytes, x.staging_slots, x.first_chunk_bytes) == (1 << 30, 2, 64 << 20)
+    assert x.copy_kernel == native.PF_COPY_KERNEL_AUTO
 
 
 def test_library_is_sm100a_build(native):
