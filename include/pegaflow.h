@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define PF_ABI_VERSION 3
+#define PF_ABI_VERSION 4
 
 /* ------------------------------------------------------------------------ */
 /* Status codes: one per EngineError variant (pegaflow-core/src/lib.rs:58-67) */
@@ -245,6 +245,12 @@ typedef struct pf_executor_stats {
   uint64_t timed_launches;
   uint64_t bytes_p2p;       /* payload moved by pf_p2p_transfer */
   double host_ms;           /* calling-thread time inside save/load/p2p: checks, plan, enqueue */
+  /* While timing is on, each kernel also stamps %globaltimer when its first
+   * CTA starts and its last CTA ends: kernel_body_ms sums those spans over
+   * body_launches launches. The CUDA-event duration (kernel_ms) adds the
+   * launch's own latency, which grows while the copy engines stream. */
+  double kernel_body_ms;
+  uint64_t body_launches;
 } pf_executor_stats;
 int pf_executor_stats_get(pf_executor* exec, pf_executor_stats* out);
 int pf_executor_stats_reset(pf_executor* exec);

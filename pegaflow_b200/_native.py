@@ -25,7 +25,7 @@ from ctypes import (
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpegaflow_b200.so"
-ABI_VERSION = 3  # PF_ABI_VERSION the structs below follow
+ABI_VERSION = 4  # PF_ABI_VERSION the structs below follow
 
 PF_OK = 0
 PF_ERR_INSTANCE_MISSING = 1
@@ -109,6 +109,8 @@ class ExecutorStats(Structure):
         ("timed_launches", c_uint64),
         ("bytes_p2p", c_uint64),
         ("host_ms", c_double),
+        ("kernel_body_ms", c_double),
+        ("body_launches", c_uint64),
     ]
 
 

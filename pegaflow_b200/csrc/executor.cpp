@@ -187,7 +187,20 @@ Executor::~Executor() {
   cudaStreamDestroy(own_stream_);
   cudaStreamDestroy(save_stream_);
   if (status_host_) cudaFreeHost(const_cast<int*>(status_host_));
+  cudaFree(spans_);
   cudaGetLastError();
+}
+
+void Executor::reset_spans() {
+  // {max, 0} so the kernels' atomicMin / atomicMax start from an empty span.
+  std::vector<unsigned long long> init(2 * kSpanCap);
+  for (uint64_t i = 0; i < kSpanCap; ++i) {
+    init[2 * i] = ~0ull;
+    init[2 * i + 1] = 0;
+  }
+  cuda_check(cudaMemcpy(spans_, init.data(), init.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice),
+             "cudaMemcpy(spans)");
+  spans_used_ = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -367,6 +380,7 @@ void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_
   {
     std::lock_guard<std::mutex> g(stats_mu_);
     stats_.kernel_launches += 1;
+    if (timing_ && spans_ && spans_used_ < kSpanCap) a.span = spans_ + 2 * spans_used_++;
     if (timing_) {
       auto take = [this]() {
         if (!event_pool_.empty()) {
@@ -652,6 +666,21 @@ void Executor::stats(pf_executor_stats* out) {
     event_pool_.push_back(p.first);
     event_pool_.push_back(p.second);
   }
+  if (spans_used_ > 0 && timed_.empty()) {
+    // Every span handed out so far belongs to a launch whose end event was
+    // waited on above: spans are given out with a launch's events, and no
+    // timed launch was added since (else the spans wait for a later call).
+    std::vector<unsigned long long> sp(2 * spans_used_);
+    cuda_check(cudaMemcpy(sp.data(), spans_, sp.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost),
+               "cudaMemcpy(spans)");
+    for (uint64_t i = 0; i < spans_used_; ++i) {
+      if (sp[2 * i + 1] > sp[2 * i]) {
+        stats_.kernel_body_ms += static_cast<double>(sp[2 * i + 1] - sp[2 * i]) * 1e-6;
+        stats_.body_launches += 1;
+      }
+    }
+    reset_spans();
+  }
   *out = stats_;
 }
 
@@ -663,7 +692,13 @@ void Executor::reset_stats() {
 }
 
 void Executor::set_timing(bool on) {
+  DeviceGuard dev(device_);
   std::lock_guard<std::mutex> g(stats_mu_);
+  if (on && !spans_) {
+    cuda_check(cudaMalloc(reinterpret_cast<void**>(&spans_), 2 * kSpanCap * sizeof(unsigned long long)),
+               "cudaMalloc(spans)");
+    reset_spans();
+  }
   timing_ = on;
 }
 

@@ -133,6 +133,13 @@ class Executor {
   void fold_finished_timings();
   std::vector<cudaEvent_t> event_pool_;
   pf_executor_stats stats_{};
+  // Kernel-body spans ({start, end} %globaltimer ns per timed launch): a
+  // device array of kSpanCap entries, handed out in launch order while
+  // timing is on and read back by stats().
+  static constexpr uint64_t kSpanCap = 8192;
+  unsigned long long* spans_ = nullptr;
+  uint64_t spans_used_ = 0;
+  void reset_spans();  // stats_mu_ held; no timed launch in flight
 };
 
 }  // namespace pf

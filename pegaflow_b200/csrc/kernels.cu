@@ -35,6 +35,8 @@ constexpr int kMinCtasPerSm = 4;
 constexpr int kVecPerLane = kTileBytes / (32 * 16);  // 8
 static_assert(kVecPerLane == 8, "tile = 32 lanes x 8 x 16 B");
 static_assert(sizeof(PlanLayer) % 16 == 0, "layer table is copied in 16-byte words");
+// Unaligned units below this size (one tile each) are copied one per lane.
+constexpr uint32_t kTinyUnitBytes = 16;
 // Layer tables up to 48 KiB (512 layers) go to shared memory without opt-in.
 constexpr size_t kMaxSmemTableBytes = 48 * 1024;
 
@@ -108,6 +110,32 @@ __device__ __forceinline__ void flush_layer(const CopyArgs& a, uint32_t l,
 
 extern __shared__ __align__(16) unsigned char g_smem[];
 
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Kernel-body timing (only while the executor times launches, a.span set):
+// the CTA's first thread stamps its start into span[0] (min over CTAs); the
+// last of the CTA's warps to finish, after a fence that waits for its writes,
+// stamps span[1] (max over CTAs).
+__device__ __forceinline__ void span_start(const CopyArgs& a, unsigned int* warps_done) {
+  if (threadIdx.x == 0) {
+    *warps_done = 0;
+    atomicMin(&a.span[0], global_ns());
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void span_warp_done(const CopyArgs& a, unsigned int* warps_done, int lane,
+                                               unsigned int warps) {
+  if (a.span == nullptr) return;
+  __threadfence();
+  __syncwarp();
+  if (lane == 0 && atomicAdd(warps_done, 1u) == warps - 1) atomicMax(&a.span[1], global_ns());
+}
+
 // SMEM: the CTA first copies the plan's layer table into shared memory with
 // coalesced 16-byte loads (one round trip), so the per-warp layer lookups
 // below hit shared memory instead of chaining dependent global loads.
@@ -117,6 +145,8 @@ template <int DIR, bool TABLE, bool SMEM, bool CS>
 __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) kv_copy_kernel(const CopyArgs a) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  __shared__ unsigned int warps_done;
+  if (a.span) span_start(a, &warps_done);
 
   const PlanLayer* layers = a.layers;
   if (SMEM) {
@@ -135,7 +165,10 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) kv_copy_kernel(const 
   if (cta_end > a.tile_end) cta_end = a.tile_end;
 
   uint64_t tile = cta_begin + (uint64_t)warp;
-  if (tile >= cta_end) return;
+  if (tile >= cta_end) {
+    span_warp_done(a, &warps_done, lane, kWarpsPerCta);
+    return;
+  }
 
   // Layer of the first tile: last l with tile_start <= tile.
   uint32_t lo = 0, hi = a.n_layers;
@@ -158,6 +191,31 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) kv_copy_kernel(const 
       Lp = &layers[l];
     }
     const PlanLayer& L = *Lp;
+    if ((L.flags & kFlagVector) == 0 && L.unit_bytes < kTinyUnitBytes) {
+      // Tiny unaligned units (4-byte per-block scales): one unit per tile,
+      // so the warp's next tiles of this layer (up to 32) go one to a lane
+      // instead of one tile per warp iteration.
+      uint64_t lim = L.tile_start + L.tile_count;
+      if (lim > cta_end) lim = cta_end;
+      uint64_t cnt = (lim - tile + kWarpsPerCta - 1) / kWarpsPerCta;
+      const uint32_t count = cnt < 32 ? (uint32_t)cnt : 32u;
+      if ((uint32_t)lane < count) {
+        const uint32_t unit_local = (uint32_t)(tile + (uint64_t)lane * kWarpsPerCta - L.tile_start);
+        const uint32_t u = unit_local / L.n;
+        const uint32_t i = unit_local - u * L.n;
+        const uint64_t b = a.ids[L.ids_off + i];
+        char* cache = reinterpret_cast<char*>(L.cache_base + b * L.block_pitch + (uint64_t)u * L.unit_stride);
+        char* side = TABLE ? reinterpret_cast<char*>(a.side_ptrs[L.unit_off + unit_local])
+                           : reinterpret_cast<char*>(a.side_base[L.side_off + u] + (uint64_t)i * L.side_pitch +
+                                                     a.side_shift);
+        for (uint32_t k = 0; k < L.unit_bytes; ++k) {
+          if (DIR == kPack) side[k] = cache[k]; else cache[k] = side[k];
+        }
+      }
+      done_in_layer += count;
+      tile += (uint64_t)(count - 1) * kWarpsPerCta;  // the loop adds the last step
+      continue;
+    }
     const uint32_t local = (uint32_t)(tile - L.tile_start);
     const uint32_t unit_local = local / L.tiles_per_unit;
     const uint32_t t = local - unit_local * L.tiles_per_unit;
@@ -185,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) kv_copy_kernel(const 
     ++done_in_layer;
   }
   flush_layer(a, l, Lp->tile_count, Lp->done_index, done_in_layer, lane);
+  span_warp_done(a, &warps_done, lane, kWarpsPerCta);
 }
 
 // ---------------------------------------------------------------------------
@@ -228,12 +287,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 // true once the phase with `parity` has completed; false after kBulkWaitNs.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = global_ns();
@@ -258,6 +311,8 @@ template <int DIR>
 __global__ void __launch_bounds__(kBulkThreads, 1) kv_bulk_kernel(const CopyArgs a) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  __shared__ unsigned int warps_done;
+  if (a.span) span_start(a, &warps_done);
   unsigned char* stages = g_smem + size_t(warp) * kBulkStages * kTileBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(g_smem + kBulkStageBytes) + warp * kBulkStages;
   BulkDesc* descs = reinterpret_cast<BulkDesc*>(g_smem + kBulkStageBytes + kBulkBarBytes) + warp * 64;
@@ -268,7 +323,10 @@ __global__ void __launch_bounds__(kBulkThreads, 1) kv_bulk_kernel(const CopyArgs
   uint64_t cta_end = cta_begin + per_cta;
   if (cta_end > a.tile_end) cta_end = a.tile_end;
   const uint64_t first = cta_begin + (uint64_t)warp;
-  if (first >= cta_end) return;
+  if (first >= cta_end) {
+    span_warp_done(a, &warps_done, lane, kBulkWarps);
+    return;
+  }
   const uint64_t n = (cta_end - first + kBulkWarps - 1) / kBulkWarps;  // this warp's tiles
 
   if (lane == 0) {
@@ -360,6 +418,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) kv_bulk_kernel(const CopyArgs
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   __syncwarp();
+  span_warp_done(a, &warps_done, lane, kBulkWarps);
 }
 
 // Runtime flags -> template instance.

@@ -66,6 +66,7 @@ struct CopyArgs {
   uint32_t n_layers;
   uint32_t pad;
   int* status;                  // bulk kernel: set to 1 when a bounded wait gave up, or null
+  unsigned long long* span;     // {first CTA start, last CTA end} in %globaltimer ns, or null
 };
 
 // Directions.

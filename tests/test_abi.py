@@ -27,7 +27,7 @@ def test_binding_covers_header(native):
 
 
 def test_abi_version(native):
-    assert native.lib.pf_abi_version() == 3 == native.ABI_VERSION
+    assert native.lib.pf_abi_version() == 4 == native.ABI_VERSION
 
 
 def test_config_defaults(native):
