@@ -909,7 +909,7 @@ def config_block(args, wl, world: int) -> dict:
            "kv_dtype": "fp16" if wl.get("separate") else "bf16",
            "save_mode": args.save_mode, "load_mode": args.load_mode, "copy_kernel": args.copy_kernel,
            "staging": {"slot_MiB": args.chunk_mib or 1024, "slots": args.slots or 2, "lanes": "save, load",
-                       "first_chunk_MiB": args.first_chunk_mib or 64, "growth": "x2 per chunk",
+                       "first_chunk_MiB": args.first_chunk_mib or 256, "growth": "x2 per chunk",
                        "save_first_chunk": "max(first chunk, half a slot)",
                        "load_first_chunk": "a whole slot; with per-layer flags (the e2e engine loads) "
                                            "the first layer, at most the first chunk"},

@@ -120,8 +120,10 @@ typedef struct pf_executor_config {
    * kernel launch count low. Saves start at the larger of this and half a
    * slot; loads without per-layer flags use whole slots. A load given
    * per-layer flags starts at the smaller of this and its first layer plus
-   * the small layers listed right after it (at least 4 MiB).
-   * 0 = default (64 MiB). */
+   * the small layers listed right after it (at least 4 MiB), so its first
+   * flag rises after that layer's DMA alone when the layer fits.
+   * 0 = default (256 MiB: a whole first layer of the benchmark shapes,
+   * 40 MiB for Llama-3.1-8B and 128 MiB for Llama-3-70B at TP1). */
   uint64_t first_chunk_bytes;
 } pf_executor_config;
 

@@ -24,7 +24,10 @@ namespace pf {
 // two. On a 180 GB B200 the two lanes' 4 GiB are 2.2% of HBM.
 constexpr uint64_t kDefaultSlotBytes = 1024ull << 20;
 constexpr uint32_t kDefaultSlots = 2;
-constexpr uint64_t kDefaultFirstChunkBytes = 64ull << 20;
+// A layer-wise load's first chunk holds its first layer whole up to this
+// size, so layer 0's flag waits for that layer's DMA only (a 128 MiB layer
+// split at 64 MiB waited for 192 MiB).
+constexpr uint64_t kDefaultFirstChunkBytes = 256ull << 20;
 // Lower bound of a layer-wise load's first chunk (which holds layer 0 and
 // the small layers listed right after it).
 constexpr uint64_t kLayerwiseMinFirstChunk = 4ull << 20;

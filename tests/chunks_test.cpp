@@ -184,6 +184,21 @@ int main() {
     }
   }
   {
+    // configs[3] at TP1 with the default 256 MiB first-chunk limit: the first
+    // chunk is the whole 128 MiB layer 0 (a 64 MiB limit split it, and layer
+    // 0's flag then waited for the second chunk too).
+    const uint64_t first = layerwise_first_limit(llama70.layers, 256ull << 20, kMin);
+    std::vector<Chunk> ch;
+    cut_chunks(llama70.layers, llama70.total_tiles, g1, first, &ch);
+    std::vector<uint64_t> want = {128, 256, 512};
+    for (int k = 0; k < 9; ++k) want.push_back(1024);
+    want.push_back(128);
+    if (first != (128ull << 20) || ch[0].tile_end != llama70.layers[1].tile_start || spans_mib(ch) != want) {
+      std::printf("FAIL llama70 layer-wise first chunk %llu\n", static_cast<unsigned long long>(first));
+      return 1;
+    }
+  }
+  {
     // Layers of 1.5 MiB: the 4 MiB floor applies; a cap below the layer wins.
     const Case small = make_case(std::vector<std::pair<uint32_t, uint32_t>>(24, {24576, 1}), 64);
     if (layerwise_first_limit(small.layers, kFirst, kMin) != kMin ||

@@ -43,7 +43,7 @@ def test_config_defaults(native):
     assert (e.pre_evict_enabled, e.pre_evict_threshold_bytes, e.pre_evict_target_bytes) == (0, 5 << 30, 8 << 30)
     x = native.ExecutorConfig()
     native.lib.pf_executor_config_default(byref(x))
-    assert (x.staging_chunk_bytes, x.staging_slots, x.first_chunk_bytes) == (1 << 30, 2, 64 << 20)
+    assert (x.staging_chunk_bytes, x.staging_slots, x.first_chunk_bytes) == (1 << 30, 2, 256 << 20)
     assert x.copy_kernel == native.PF_COPY_KERNEL_AUTO
 
 
