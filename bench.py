@@ -132,20 +132,22 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-# DRAM bytes per payload byte of one pack or unpack launch, from one ncu
-# capture of dram__bytes_read.sum / dram__bytes_write.sum on 128 MiB staging
-# chunks (larger than L2), not a per-run measurement.
-# Reads equal the payload (no re-reads); writes still in the 126 MB L2 when
-# the kernel ends reach DRAM after it, so the write figure is below 1.
-TRAFFIC_READ_PER_BYTE = 134_251_584 / 134_217_728
-TRAFFIC_WRITE_PER_BYTE = 76_006_592 / 134_217_728
+# DRAM traffic of one pack or unpack launch, from one ncu capture of
+# dram__bytes_read.sum / dram__bytes_write.sum of the bulk kernel on 128 MiB
+# (pack) and 160 MiB (unpack) chunks, larger than L2; not a per-run
+# measurement. Reads equal the payload (no re-reads). Writes still in the
+# 126 MB L2 when a launch ends (about 50 MB, whatever the chunk size) reach
+# DRAM after it, so a launch's write traffic is its payload less that.
+TRAFFIC_READ_PER_BYTE = (134_253_056 + 167_813_120) / (134_217_728 + 167_772_160)
+TRAFFIC_WRITE_RESIDUE = ((134_217_728 - 81_046_272) + (167_772_160 - 118_041_088)) / 2
 
 
 def traffic_per_launch(kernel_bytes_per_launch: float) -> int:
-    """ncu-measured DRAM traffic scaled to the average launch (payload = half
-    the algorithmic bytes: each payload byte is read once and written once)."""
+    """ncu-measured DRAM traffic model applied to the average launch
+    (payload = half the algorithmic bytes: each payload byte is read once and
+    written once)."""
     payload = kernel_bytes_per_launch / 2
-    return round(payload * (TRAFFIC_READ_PER_BYTE + TRAFFIC_WRITE_PER_BYTE))
+    return round(payload * TRAFFIC_READ_PER_BYTE + max(0.0, payload - TRAFFIC_WRITE_RESIDUE))
 
 
 def link_peaks(torch, device: int, barrier=None) -> dict:
@@ -1468,9 +1470,10 @@ def main() -> int:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 3),
                          "traffic": traffic_per_launch(st["kernel_bytes"] / max(1, st["timed_launches"])),
-                         "traffic_how": "not measured per run: ncu dram__bytes_read.sum + dram__bytes_write.sum "
-                                        "per payload byte from one capture (128 MiB chunks), scaled to this run's "
-                                        "average launch; writes still in L2 at kernel end are not counted",
+                         "traffic_how": "not measured per run: from one ncu capture of dram__bytes_read.sum + "
+                                        "dram__bytes_write.sum (128 and 160 MiB chunks): reads = payload, writes = "
+                                        "payload less the ~50 MB still in L2 at kernel end; applied to this run's "
+                                        "average launch",
                          "peak_source": peaks["source"],
                          "kernel": "kv_copy_kernel (pack+unpack)",
                          "bytes_per_launch": round(st["kernel_bytes"] / max(1, st["timed_launches"])),
