@@ -259,6 +259,15 @@ int pf_executor_stats_reset(pf_executor* exec);
 /* Record CUDA events around each kernel launch (on the kernel's stream). */
 int pf_executor_set_timing(pf_executor* exec, int enabled);
 
+/* Test hook for the bulk kernel's bounded waits (no counterpart in the
+ * reference). The next bulk-kernel launch of this executor arms the mbarrier
+ * of the launch's tile `tile` (counted from the launch's first tile) but
+ * issues no copy into it, so the wait for that tile runs out after 1 s; the
+ * warp then stops, the kernel returns, and the executor fails the call with
+ * PF_ERR_STORAGE. No fault and no hang: the barrier is simply never
+ * completed. UINT64_MAX (the default) disarms it. */
+int pf_executor_debug_stall_tile(pf_executor* exec, uint64_t tile);
+
 /* ------------------------------------------------------------------------ */
 /* Reference copy strategy, restated for side-by-side timing on one box      */
 /* ------------------------------------------------------------------------ */

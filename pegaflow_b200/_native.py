@@ -219,6 +219,7 @@ _SIGNATURES = {
     "pf_executor_stats_get": (c_int, [c_void_p, POINTER(ExecutorStats)]),
     "pf_executor_stats_reset": (c_int, [c_void_p]),
     "pf_executor_set_timing": (c_int, [c_void_p, c_int]),
+    "pf_executor_debug_stall_tile": (c_int, [c_void_p, c_uint64]),
     "pf_refcopy_save": (c_int, [c_int32, POINTER(SaveLayer), c_uint64]),
     "pf_refcopy_load": (c_int, [c_int32, POINTER(LoadLayer), c_uint64, POINTER(c_uint64)]),
     "pf_pinned_alloc": (c_int, [c_uint64, c_int, POINTER(c_void_p)]),

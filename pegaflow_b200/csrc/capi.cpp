@@ -158,6 +158,11 @@ int pf_executor_set_timing(pf_executor* exec, int enabled) {
   return guarded([&] { exec->get().set_timing(enabled != 0); });
 }
 
+int pf_executor_debug_stall_tile(pf_executor* exec, uint64_t tile) {
+  if (!exec) return null_arg("executor");
+  return guarded([&] { exec->get().debug_stall_tile(tile); });
+}
+
 int pf_refcopy_save(int32_t device_id, const pf_save_layer* layers, uint64_t n_layers) {
   if (!layers && n_layers) return null_arg("layers");
   return guarded([&] { pf::refcopy_save(device_id, layers, n_layers); });

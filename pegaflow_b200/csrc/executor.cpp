@@ -376,11 +376,17 @@ void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_
   a.tile_end = tile_end;
   a.side_shift = shift;
   a.status = status_dev_;
+  a.stall_tile = ~0ull;
+  const bool use_bulk = bulk && !table && a.layer_tiles_done == nullptr;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   {
     std::lock_guard<std::mutex> g(stats_mu_);
     stats_.kernel_launches += 1;
     if (timing_ && spans_ && spans_used_ < kSpanCap) a.span = spans_ + 2 * spans_used_++;
+    if (use_bulk && stall_tile_ != ~0ull) {
+      a.stall_tile = stall_tile_;
+      stall_tile_ = ~0ull;
+    }
     if (timing_) {
       auto take = [this]() {
         if (!event_pool_.empty()) {
@@ -397,7 +403,7 @@ void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_
     }
   }
   if (e0) cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
-  if (bulk && !table && a.layer_tiles_done == nullptr) {
+  if (use_bulk) {
     cuda_check(launch_bulk_copy(dir, a, num_sms_, s), "kernel launch");
   } else {
     cuda_check(launch_copy(dir, table, a, grid_for(tile_end - tile_begin), s, cfg_.cache_streaming != 0),
@@ -689,6 +695,11 @@ void Executor::reset_stats() {
   stats(&tmp);
   std::lock_guard<std::mutex> g(stats_mu_);
   stats_ = pf_executor_stats{};
+}
+
+void Executor::debug_stall_tile(uint64_t tile) {
+  std::lock_guard<std::mutex> g(stats_mu_);
+  stall_tile_ = tile;
 }
 
 void Executor::set_timing(bool on) {

@@ -65,6 +65,8 @@ class Executor {
   void stats(pf_executor_stats* out);
   void reset_stats();
   void set_timing(bool on);
+  // Test hook: the next bulk launch leaves `tile` uncopied (its wait runs out).
+  void debug_stall_tile(uint64_t tile);
 
  private:
   // Plans (plan_build.h) with this executor's device check.
@@ -117,6 +119,7 @@ class Executor {
   pf_executor_config cfg_;
   int num_sms_ = 148;
   bool bulk_ = false;                  // the bulk (TMA) kernel is enabled and ready on this device
+  uint64_t stall_tile_ = ~0ull;        // test hook, consumed by the next bulk launch (stats_mu_)
   volatile int* status_host_ = nullptr;  // set by a bulk kernel whose bounded wait ran out
   int* status_dev_ = nullptr;          // device view of the same word
   cudaStream_t own_stream_ = nullptr;   // blocking loads and peer copies

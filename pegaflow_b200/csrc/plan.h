@@ -67,6 +67,7 @@ struct CopyArgs {
   uint32_t pad;
   int* status;                  // bulk kernel: set to 1 when a bounded wait gave up, or null
   unsigned long long* span;     // {first CTA start, last CTA end} in %globaltimer ns, or null
+  uint64_t stall_tile;          // bulk kernel test hook: tile (from tile_begin) whose copy is not issued
 };
 
 // Directions.
