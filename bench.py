@@ -910,6 +910,7 @@ def config_block(args, wl, world: int) -> dict:
            "blocks_moved": wl["blocks"], "block_ids": args.order,
            "kv_dtype": "fp16" if wl.get("separate") else "bf16",
            "save_mode": args.save_mode, "load_mode": args.load_mode, "copy_kernel": args.copy_kernel,
+           "pool": "pinned, write-combined" if args.pool_wc else "pinned, cacheable",
            "staging": {"slot_MiB": args.chunk_mib or 1024, "slots": args.slots or 2, "lanes": "save, load",
                        "first_chunk_MiB": args.first_chunk_mib or 256, "growth": "x2 per chunk",
                        "save_first_chunk": "max(first chunk, half a slot)",
@@ -1156,6 +1157,8 @@ def main() -> int:
     ap.add_argument("--copy-streams", type=int, default=0)
     ap.add_argument("--ctas-per-sm", type=int, default=0)
     ap.add_argument("--cache-streaming", action="store_true", help="evict-first loads/stores in the kernels")
+    ap.add_argument("--pool-wc", type=int, default=1, choices=[0, 1],
+                    help="pinned pool memory write-combined (1, the reference's pool kind) or cacheable (0)")
     ap.add_argument("--copy-kernel", default="auto", choices=["auto", "registers", "bulk"],
                     help="how staged tiles move: registers, or TMA bulk copies through shared memory")
     ap.add_argument("--e2e-steps", type=int, default=0, help="engine-API steps (default: --steps)")
@@ -1241,7 +1244,7 @@ def main() -> int:
                   copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm,
                   cache_streaming=args.cache_streaming, first_chunk_bytes=args.first_chunk_mib << 20,
                   copy_kernel=args.copy_kernel)
-    pool = PinnedBuffer(payload + wl["layers"] * 8192 + (1 << 20), write_combined=True)
+    pool = PinnedBuffer(payload + wl["layers"] * 8192 + (1 << 20), write_combined=args.pool_wc == 1)
     saves, loads, _ = executor_specs(tensors, src, dst, pool.ptr)
     stream = torch.cuda.Stream(local)
     sp = stream.cuda_stream
@@ -1336,7 +1339,7 @@ def main() -> int:
 
     # ---- e2e through the engine API (host wall clock) ------------------------
     e2e_steps = args.e2e_steps or args.steps
-    eng = PegaEngine(2 * payload + (256 << 20), enable_lfu_admission=False,
+    eng = PegaEngine(2 * payload + (256 << 20), enable_lfu_admission=False, write_combined=args.pool_wc == 1,
                      executor=dict(save_mode=args.save_mode, load_mode=args.load_mode,
                                    staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
                                    copy_streams=args.copy_streams, ctas_per_sm=args.ctas_per_sm,

@@ -31,8 +31,8 @@ def test_bulk_wait_that_runs_out_fails_the_call_and_the_gpu_stays_usable(cuda, n
     t = kv(torch, (2, 256, 16, 8, 128), 61)
     lay = Layout.from_tensor(t)
     n, seg = 64, lay.bytes_per_block
-    src = np.random.default_rng(62).permutation(256)[:n]
-    dst = np.random.default_rng(63).permutation(256)[:n]
+    perm = np.random.default_rng(62).permutation(256)
+    src, dst = perm[:n], perm[n:2 * n]  # disjoint: a restore never overwrites a source
     pool = PinnedBuffer(2 * n * seg)
     save = SaveSpec(lay, src, pool.ptr, pool.ptr + n * seg)
     ks = np.arange(n, dtype=np.uint64) * seg + pool.ptr
