@@ -9,10 +9,17 @@
 // across the host link) or mapped pinned host memory (zero-copy).
 //
 // Work is split into 4 KiB tiles (plan.h). Each CTA owns a contiguous range
-// of tiles and its 8 warps walk it interleaved, so neighbouring warps touch
-// neighbouring bytes. Per tile, one warp decodes (layer, unit, block) with
-// integer math, reads the block index once (a broadcast load), and moves the
-// tile with 8 x 16-byte loads per lane in flight before the 8 stores.
+// of tiles and its warps walk it interleaved, so neighbouring warps touch
+// neighbouring bytes. Two kernels move the tiles:
+//   kv_copy_kernel: per tile, one warp decodes (layer, unit, block) with
+//     integer math, reads the block index once (a broadcast load), and moves
+//     the tile with 8 x 16-byte loads per lane in flight before the 8 stores.
+//     Handles every layout: unaligned units, zero-copy and peer tables,
+//     per-layer completion flags.
+//   kv_bulk_kernel: TMA bulk copies (cp.async.bulk) move each tile from
+//     global memory into a per-warp ring of shared-memory stages and back
+//     out, several tiles in flight per warp; for staged, 16-byte aligned
+//     transfers without per-layer flags.
 // Sorted and shuffled block lists cost the same: the block index only picks
 // the tile's base address.
 //
