@@ -400,19 +400,33 @@ void Executor::launch(Dir dir, bool table, const CopyArgs& args0, uint64_t tile_
       };
       e0 = take();
       e1 = take();
+      // Until its events are in timed_, stats() must not read or reset the
+      // spans: this launch may hold one and write it.
+      ++unregistered_launches_;
     }
   }
-  if (e0) cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
-  if (use_bulk) {
-    cuda_check(launch_bulk_copy(dir, a, num_sms_, s), "kernel launch");
-  } else {
-    cuda_check(launch_copy(dir, table, a, grid_for(tile_end - tile_begin), s, cfg_.cache_streaming != 0),
-               "kernel launch");
+  try {
+    if (e0) cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
+    if (use_bulk) {
+      cuda_check(launch_bulk_copy(dir, a, num_sms_, s), "kernel launch");
+    } else {
+      cuda_check(launch_copy(dir, table, a, grid_for(tile_end - tile_begin), s, cfg_.cache_streaming != 0),
+                 "kernel launch");
+    }
+    if (e1) cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
+  } catch (...) {
+    if (e1) {
+      std::lock_guard<std::mutex> g(stats_mu_);
+      --unregistered_launches_;
+      event_pool_.push_back(e0);
+      event_pool_.push_back(e1);
+    }
+    throw;
   }
   if (e1) {
-    cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
     std::lock_guard<std::mutex> g(stats_mu_);
     timed_.emplace_back(e0, e1);
+    --unregistered_launches_;
     // A caller that times without reading stats must not grow this list
     // without bound: spans that have finished are folded in as we go.
     if (timed_.size() >= 1024) fold_finished_timings();
@@ -672,10 +686,11 @@ void Executor::stats(pf_executor_stats* out) {
     event_pool_.push_back(p.first);
     event_pool_.push_back(p.second);
   }
-  if (spans_used_ > 0 && timed_.empty()) {
+  if (spans_used_ > 0 && timed_.empty() && unregistered_launches_ == 0) {
     // Every span handed out so far belongs to a launch whose end event was
     // waited on above: spans are given out with a launch's events, and no
-    // timed launch was added since (else the spans wait for a later call).
+    // timed launch was added or is being added since (else the spans wait
+    // for a later call).
     std::vector<unsigned long long> sp(2 * spans_used_);
     cuda_check(cudaMemcpy(sp.data(), spans_, sp.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost),
                "cudaMemcpy(spans)");

@@ -145,6 +145,7 @@ class Executor {
   static constexpr uint64_t kSpanCap = 8192;
   unsigned long long* spans_ = nullptr;
   uint64_t spans_used_ = 0;
+  uint64_t unregistered_launches_ = 0;  // timed launches whose events are not yet in timed_
   void reset_spans();  // stats_mu_ held; no timed launch in flight
 };
 
