@@ -486,6 +486,24 @@ int pf_engine_batch_load_kv_blocks(pf_engine* e, const char* instance_id,
                                    const pf_bytes* block_hashes,
                                    uint64_t n_blocks);
 
+/* The gRPC server's Save and Load RPCs (pegaflow-server/src/service.rs,
+ * Save and Load handlers), taking the request's protobuf wire bytes
+ * (engine.proto SaveRequest / LoadRequest) instead of decoded arguments. The
+ * library decodes them (fields in any order, packed or unpacked ids, unknown
+ * fields skipped) and runs batch_save_kv_blocks / batch_load_kv_blocks with
+ * the same results and errors; a malformed request is
+ * PF_ERR_INVALID_ARGUMENT. Layers of a Save whose hash lists are identical
+ * share one list. A Load's block ids and hashes are paired up to the shorter
+ * of the two lists (the reference zips them, lib.rs:1032-1033). */
+int pf_engine_save_request(pf_engine* e, const uint8_t* request, uint64_t len);
+int pf_engine_load_request(pf_engine* e, const uint8_t* request, uint64_t len);
+/* Field 1 (instance_id) of a Save or Load request's wire bytes, copied into
+ * out (NUL-terminated, at most cap bytes with the NUL); *out_len is its
+ * length. PF_ERR_INVALID_ARGUMENT when it does not fit or the bytes are
+ * malformed. */
+int pf_request_instance_id(const uint8_t* request, uint64_t len, char* out, uint64_t cap,
+                           uint64_t* out_len);
+
 /* Block until every queued load on device_id has finished (bounded by
  * timeout_s; PF_ERR_TIMEOUT otherwise). No reference counterpart. */
 int pf_engine_wait_loads(pf_engine* e, int32_t device_id, double timeout_s);

@@ -278,6 +278,9 @@ _SIGNATURES = {
         ],
     ),
     "pf_engine_wait_loads": (c_int, [c_void_p, c_int32, c_double]),
+    "pf_engine_save_request": (c_int, [c_void_p, c_char_p, c_uint64]),
+    "pf_engine_load_request": (c_int, [c_void_p, c_char_p, c_uint64]),
+    "pf_request_instance_id": (c_int, [c_char_p, c_uint64, c_char_p, c_uint64, POINTER(c_uint64)]),
     "pf_engine_pool_usage": (c_int, [c_void_p, POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint64)]),
     "pf_engine_slot_info": (
         c_int,

@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "common.h"
+#include "wire.h"
 #include "engine.h"
 #include "executor.h"
 #include "offset_allocator.h"
@@ -438,6 +439,36 @@ int pf_engine_batch_load_kv_blocks(pf_engine* e, const char* instance_id, uint64
     hashes.reserve(n_blocks);
     for (uint64_t k = 0; k < n_blocks; ++k) hashes.push_back(bytes_str(block_hashes[k]));
     e->impl->batch_load(str(instance_id), tp_rank, device_id, str(load_state_shm), names, ids, hashes);
+  });
+}
+
+int pf_engine_save_request(pf_engine* e, const uint8_t* request, uint64_t len) {
+  if (!e || (!request && len)) return null_arg("engine or request");
+  return guarded([&] {
+    pf::SaveRequestWire req;
+    pf::decode_save_request(request, len, &req);
+    e->impl->batch_save(req.instance_id, req.tp_rank, req.device_id, req.saves);
+  });
+}
+
+int pf_engine_load_request(pf_engine* e, const uint8_t* request, uint64_t len) {
+  if (!e || (!request && len)) return null_arg("engine or request");
+  return guarded([&] {
+    pf::LoadRequestWire req;
+    pf::decode_load_request(request, len, &req);
+    e->impl->batch_load(req.instance_id, req.tp_rank, req.device_id, req.load_state_shm, req.layer_names,
+                        req.block_ids, req.block_hashes);
+  });
+}
+
+int pf_request_instance_id(const uint8_t* request, uint64_t len, char* out, uint64_t cap, uint64_t* out_len) {
+  if ((!request && len) || !out || !out_len) return null_arg("argument");
+  return guarded([&] {
+    const std::string id = pf::decode_request_instance_id(request, len);
+    *out_len = id.size();
+    if (id.size() + 1 > cap) throw pf::invalid_argument("instance_id longer than the output buffer");
+    std::memcpy(out, id.data(), id.size());
+    out[id.size()] = '\0';
   });
 }
 

@@ -181,6 +181,10 @@ class PegaEngine:
         block_hashes: Sequence[bytes],
     ) -> None:
         names = (c_char_p * max(1, len(layer_names)))(*[n.encode() for n in layer_names])
+        # The reference pairs ids with hashes up to the shorter list
+        # (lib.rs:1032-1033); the C call takes one count for both arrays.
+        n = min(len(block_ids), len(block_hashes))
+        block_ids, block_hashes = list(block_ids)[:n], list(block_hashes)[:n]
         ids, ids_keep = N.int32_array(block_ids)
         arr, keep = N.bytes_array(block_hashes)
         N.check(
@@ -198,6 +202,17 @@ class PegaEngine:
             )
         )
         del keep, ids_keep
+
+    def save_request(self, request: bytes) -> None:
+        """The server's Save RPC on a request's wire bytes (engine.proto
+        SaveRequest), decoded by the library: batch_save_kv_blocks without
+        per-layer Python lists."""
+        N.check(N.lib.pf_engine_save_request(self._h, request, len(request)))
+
+    def load_request(self, request: bytes) -> None:
+        """The server's Load RPC on a request's wire bytes (engine.proto
+        LoadRequest), decoded by the library."""
+        N.check(N.lib.pf_engine_load_request(self._h, request, len(request)))
 
     # -- core engine calls the reference exposes through its server ------------
 
@@ -348,3 +363,12 @@ class PyLoadState:
             self.close()
         except Exception:
             pass
+
+
+def request_instance_id(request: bytes) -> str:
+    """Field 1 (instance_id) of a Save or Load request's wire bytes."""
+    cap = 4096
+    out = ctypes.create_string_buffer(cap)
+    n = c_uint64()
+    N.check(N.lib.pf_request_instance_id(request, len(request), out, cap, byref(n)))
+    return out.raw[: n.value].decode("utf-8", "replace")

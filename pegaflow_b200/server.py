@@ -173,16 +173,24 @@ class EngineService:
                           req.kv_stride_bytes, req.segments, req.tp_rank, req.tp_size, req.num_layers)
         return P.RegisterContextResponse(status=self._ok())
 
-    def Save(self, req, context):
-        saves = [(s.layer_name, list(s.block_ids), list(s.block_hashes)) for s in req.saves]
-        self._tracked(req.instance_id, context, self.engine.batch_save_kv_blocks, req.instance_id, req.tp_rank,
-                      req.device_id, saves)
+    # Save and Load carry the data path's block lists: a Save for 80 layers x
+    # 2,048 blocks is about 6 MB of ids and hashes. Their wire bytes go to the
+    # library, which decodes them natively (csrc/wire.cpp) with the GIL
+    # released, instead of building per-layer Python lists.
+    RAW_REQUESTS = ("Save", "Load")
+
+    def Save(self, raw: bytes, context):
+        from .engine import request_instance_id
+
+        instance_id = self._engine_call(context, request_instance_id, raw)
+        self._tracked(instance_id, context, self.engine.save_request, raw)
         return P.SaveResponse(status=self._ok())
 
-    def Load(self, req, context):
-        self._tracked(req.instance_id, context, self.engine.batch_load_kv_blocks, req.instance_id, req.tp_rank,
-                      req.device_id, req.load_state_shm, list(req.layer_names), list(req.block_ids),
-                      list(req.block_hashes))
+    def Load(self, raw: bytes, context):
+        from .engine import request_instance_id
+
+        instance_id = self._engine_call(context, request_instance_id, raw)
+        self._tracked(instance_id, context, self.engine.load_request, raw)
         return P.LoadResponse(status=self._ok())
 
     def Query(self, req, context):
@@ -230,7 +238,8 @@ class EngineService:
         methods = {}
         for rpc, (req_name, resp_name) in P.METHODS.items():
             methods[rpc] = grpc.unary_unary_rpc_method_handler(
-                getattr(self, rpc), request_deserializer=P.M[req_name].FromString,
+                getattr(self, rpc),
+                request_deserializer=None if rpc in self.RAW_REQUESTS else P.M[req_name].FromString,
                 response_serializer=P.M[resp_name].SerializeToString)
         return grpc.method_handlers_generic_handler(P.SERVICE, methods)
 

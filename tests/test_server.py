@@ -126,11 +126,13 @@ def test_query_reports_packed_file_tier_states(native, tmp_path):
         engine.close()
 
 
-def test_unregister_unmaps_tensors_only_after_copies_that_use_them():
+def test_unregister_unmaps_tensors_only_after_copies_that_use_them(native):
     """A Save RPC still copying from an instance's KV tensors, and loads
     queued on its devices, finish before UnregisterContext unmaps them."""
     import threading
     import time
+
+    from pegaflow_b200 import proto as P
 
     from pegaflow_b200.server import EngineService, TensorRegistry
 
@@ -140,7 +142,8 @@ def test_unregister_unmaps_tensors_only_after_copies_that_use_them():
         def register_context_layer(self, *a):
             events.append("register")
 
-        def batch_save_kv_blocks(self, *a):
+        def save_request(self, raw):
+            assert P.SaveRequest.FromString(raw).instance_id == "i"
             in_save.set()
             release.wait(10)
             events.append("save done")
@@ -167,7 +170,7 @@ def test_unregister_unmaps_tensors_only_after_copies_that_use_them():
                                               bytes_per_block=4096, kv_stride_bytes=0, segments=1, tp_size=1,
                                               num_layers=1), ctx)
     save = threading.Thread(target=svc.Save,
-                            args=(types.SimpleNamespace(instance_id="i", tp_rank=0, device_id=3, saves=[]), ctx))
+                            args=(P.SaveRequest(instance_id="i", tp_rank=0, device_id=3).SerializeToString(), ctx))
     save.start()
     assert in_save.wait(5)
     unreg = threading.Thread(target=svc.UnregisterContext, args=(types.SimpleNamespace(instance_id="i"), ctx))
