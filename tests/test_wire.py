@@ -167,3 +167,29 @@ def test_only_equal_hash_lists_are_shared(wire_test, tmp_path):
     assert rc == 0
     assert [line.rsplit("shared=", 1)[1] for line in out.splitlines() if line.startswith("layer ")] == \
         ["0", "1", "0", "1"]
+
+
+def test_client_encoder_matches_the_protobuf_library():
+    """The client builds Save requests without a message per layer
+    (encode_save_request); its bytes must be exactly the protobuf library's
+    serialisation of the same request, defaults omitted, negative ids and
+    device ids as ten-byte varints, layers sharing or not sharing lists."""
+    from pegaflow_b200.client import encode_save_request
+
+    rng = random.Random(3)
+    for case in range(300):
+        n = rng.choice([0, 1, 3, 50])
+        ids = [rng.randint(-2**31, 2**31 - 1) for _ in range(n)]
+        hs = [bytes(rng.getrandbits(8) for _ in range(rng.choice([0, 1, 32]))) for _ in range(n)]
+        saves = []
+        for li in range(rng.choice([0, 1, 2, 10])):
+            if rng.random() < 0.6:
+                saves.append((rng.choice(["", f"L{li}", "é" * 3]), list(ids), list(hs)))
+            else:
+                m = rng.choice([0, 2])
+                saves.append((f"x{li}", [rng.randint(-3, 9) for _ in range(m)],
+                              [bytes([li] * 4) for _ in range(m)]))
+        iid, tp, dev = rng.choice(["", "inst", "ü"]), rng.choice([0, 1, 2**32 - 1]), rng.choice([-1, 0, 5, -2**31])
+        want = P.SaveRequest(instance_id=iid, tp_rank=tp, device_id=dev,
+                             saves=[P.SaveLayer(layer_name=a, block_ids=b, block_hashes=c) for a, b, c in saves])
+        assert encode_save_request(iid, tp, dev, saves) == want.SerializeToString(), case
