@@ -905,6 +905,119 @@ def run_one_engine(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_server_e2e(args) -> None:
+    """The deployment path end to end: this process holds the KV cache (as a
+    vLLM worker does), `python -m pegaflow_b200.server` runs as its own
+    process and maps the cache over CUDA IPC, and every step is a Save RPC
+    (all layers, one hash list) followed by a Load RPC and its LoadState
+    completion, through EngineRpcClient over gRPC. BASELINE config 3 at TP1
+    (80 layers x 2,048 blocks, 10 GiB per direction) by default, or config 1
+    with --server-shape llama8b. Host wall clock; bytes checked after the
+    timed steps."""
+    import pickle
+    import socket
+
+    import torch
+
+    from pegaflow_b200 import CudaIPCWrapper, EngineRpcClient, Layout, PyLoadState
+    from pegaflow_b200.ranks import block_lists
+
+    torch.cuda.set_device(0)
+    wl = dict(WORKLOADS[args.server_shape])
+    if args.layers:
+        wl["layers"] = args.layers
+    tensors, _, _ = make_workload(torch, wl, 0, 0, 1, args.order)
+    src, dst = block_lists(wl["num_blocks"], wl["blocks"], 0, args.order)
+    n = len(src)
+    payload = payload_bytes(tensors, n)
+    torch.cuda.synchronize()
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    pool_mib = (2 * payload + (512 << 20)) >> 20
+    proc = subprocess.Popen([sys.executable, "-m", "pegaflow_b200.server", "--addr", f"127.0.0.1:{port}",
+                             "--pool-size", f"{pool_mib}mb", "--disable-lfu-admission", "--log-level", "warning"],
+                            cwd=str(ROOT), stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
+    client, deadline = None, time.time() + 300
+    while client is None:
+        try:
+            client = EngineRpcClient(f"http://127.0.0.1:{port}", connect_timeout_s=1.0)
+        except RuntimeError:
+            if proc.poll() is not None or time.time() > deadline:
+                out = proc.stdout.read().decode(errors="replace") if proc.stdout else ""
+                proc.kill()
+                raise RuntimeError(f"server did not start: {out[-2000:]}")
+    names = [f"model.layers.{i}.self_attn" for i in range(len(tensors))]
+    try:
+        for nm, t in zip(names, tensors):
+            lay = Layout.from_tensor(t)
+            ok, msg = client.register_context("srv", "bench", 0, 1, 0, len(names), nm, pickle.dumps(CudaIPCWrapper(t)),
+                                              lay.num_blocks, lay.bytes_per_block, lay.kv_stride_bytes, lay.segments)
+            if not ok:
+                raise RuntimeError(msg)
+        src_l, dst_l = src.tolist(), dst.tolist()
+
+        def step(k):
+            hashes = [f"s{k}-b{i}".encode() for i in range(n)]
+            t0 = time.perf_counter()
+            ok, msg = client.save("srv", 0, 0, [(nm, src_l, hashes) for nm in names])
+            if not ok:
+                raise RuntimeError(msg)
+            t1 = time.perf_counter()
+            st = PyLoadState(len(names))
+            ok, msg = client.load("srv", 0, 0, st.shm_name(), names, dst_l, hashes)
+            if not ok:
+                raise RuntimeError(msg)
+            limit = time.perf_counter() + 120.0
+            while not st.is_ready():
+                if time.perf_counter() > limit:
+                    raise TimeoutError("load did not complete within 120 s")
+            t2 = time.perf_counter()
+            good = st.get_state() == 1
+            st.close()
+            if not good:
+                raise RuntimeError("load failed")
+            return t1 - t0, t2 - t1
+
+        for k in range(args.warmup):
+            step(-1 - k)
+        scribble(torch, tensors, dst)
+        torch.cuda.synchronize()
+        times = [step(k) for k in range(args.steps)]
+        torch.cuda.synchronize()
+        verified = restored(torch, tensors, src, dst)
+    finally:
+        try:
+            client.shutdown()
+        except RuntimeError:
+            pass
+        try:
+            proc.wait(timeout=60)
+        except subprocess.TimeoutExpired:
+            proc.kill()
+    total = sum(a + b for a, b in times)
+    value = 2 * payload * len(times) / total / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total / len(times) * 1e3, 3), "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded ~N(0,1) bf16 KV)",
+        "config": dict(config_block(args, wl, 1), workload="server_e2e", shape=args.server_shape,
+                       parallelism="one vLLM-like client process and the engine server process on one GPU"),
+        "verified": verified,
+        "save_GBps": round(payload / statistics.median(a for a, _ in times) / 1e9, 3),
+        "load_GBps": round(payload / statistics.median(b for _, b in times) / 1e9, 3),
+        "p50_save_ms": round(statistics.median(a for a, _ in times) * 1e3, 3),
+        "p50_load_ms": round(statistics.median(b for _, b in times) * 1e3, 3),
+        "payload_bytes_per_direction": payload,
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": payload, "d2h_bytes_per_step": payload,
+                "api": "EngineRpcClient.save / load over gRPC to python -m pegaflow_b200.server (CUDA IPC), "
+                       "PyLoadState completion"},
+        "how": "host wall clock per RPC: Save returns once the bytes are in the pool; Load is timed from the RPC "
+               "to the LoadState's success",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def config_block(args, wl, world: int) -> dict:
     cfg = {"workload": args.workload, "desc": wl["desc"], "layers": wl["layers"], "num_blocks": wl["num_blocks"],
            "blocks_moved": wl["blocks"], "block_ids": args.order,
@@ -1139,8 +1252,10 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["qwen3_pd", "llama8b_fp8_evict", "llama8b_duplex",
-                                                               "llama70b_tp_one_engine"],
+                                                               "llama70b_tp_one_engine", "server_e2e"],
                     default="llama70b_tp")
+    ap.add_argument("--server-shape", default="llama70b_tp", choices=["llama70b_tp", "llama8b"],
+                    help="server_e2e: the KV shape moved through the gRPC server")
     ap.add_argument("--numa-pools", default="off", choices=["off", "node", "device"],
                     help="llama70b_tp_one_engine: one pool, or one per NUMA node / per GPU")
     ap.add_argument("--fp8-requests", type=int, default=64)
@@ -1191,6 +1306,14 @@ def main() -> int:
             return 0
         if int(os.environ.get("RANK", "0")) == 0:
             run_duplex(args)
+        return 0
+    if args.workload == "server_e2e":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": "server_e2e",
+                              "unavailable": "the reference server is Rust and cannot be built here"}))
+            return 0
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_server_e2e(args)
         return 0
     if args.workload == "llama70b_tp_one_engine":
         if args.impl == "reference":

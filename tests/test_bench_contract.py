@@ -40,7 +40,8 @@ def test_reference_arm_line_has_the_contract_keys():
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
 
 
-@pytest.mark.parametrize("workload", ["qwen3_pd", "llama8b_fp8_evict", "llama8b_duplex", "llama70b_tp_one_engine"])
+@pytest.mark.parametrize("workload", ["qwen3_pd", "llama8b_fp8_evict", "llama8b_duplex", "llama70b_tp_one_engine",
+                                      "server_e2e"])
 def test_engine_scenarios_report_the_reference_arm_unavailable(workload):
     p = run("--impl", "reference", "--workload", workload)
     assert p.returncode == 0, p.stderr
