@@ -898,9 +898,11 @@ def run_one_engine(args) -> None:
         "save_GBps": round(world * payload / save_s / 1e9, 3), "load_GBps": round(world * payload / load_s / 1e9, 3),
         "p50_save_ms": round(save_s * 1e3, 3), "p50_load_ms": round(load_s * 1e3, 3),
         "payload_bytes_per_direction_per_rank": payload, "numa_pools": args.numa_pools,
-        "engine": {k: m[k] for k in ("load_failures", "cache_block_evictions", "pool_alloc_failures")},
+        "engine": {k: (round(m[k], 2) if isinstance(m[k], float) else m[k])
+                   for k in ("load_failures", "cache_block_evictions", "pool_alloc_failures", "save_calls",
+                             "save_plan_ms", "save_transfer_ms", "save_insert_ms", "save_ms", "load_ms")},
         "how": "host wall clock per phase (all ranks save at once, then all load at once); value = all ranks' "
-               "save + load bytes / summed phase times",
+               "save + load bytes / summed phase times; engine *_ms are summed over every call of every rank",
     }
     print(json.dumps(line), flush=True)
 
