@@ -925,6 +925,12 @@ def run_server_e2e(args) -> None:
     from pegaflow_b200.ranks import block_lists
 
     torch.cuda.set_device(0)
+    if args.server_bind:
+        # The server inherits this process's CPU affinity, so its pool pages
+        # are first touched on the NUMA node next to GPU 0.
+        from pegaflow_b200.ranks import bind_to_gpu_cpus
+
+        bind_to_gpu_cpus(0)
     wl = dict(WORKLOADS[args.server_shape])
     if args.layers:
         wl["layers"] = args.layers
@@ -983,6 +989,14 @@ def run_server_e2e(args) -> None:
 
         for k in range(args.warmup):
             step(-1 - k)
+        from pegaflow_b200.client import encode_save_request
+
+        enc = []
+        for k in range(5):
+            hs = [f"e{k}-b{i}".encode() for i in range(n)]
+            t0 = time.perf_counter()
+            encode_save_request("srv", 0, 0, [(nm, src_l, hs) for nm in names])
+            enc.append(time.perf_counter() - t0)
         scribble(torch, tensors, dst)
         torch.cuda.synchronize()
         times = [step(k) for k in range(args.steps)]
@@ -1011,6 +1025,8 @@ def run_server_e2e(args) -> None:
         "p50_save_ms": round(statistics.median(a for a, _ in times) * 1e3, 3),
         "p50_load_ms": round(statistics.median(b for _, b in times) * 1e3, 3),
         "payload_bytes_per_direction": payload,
+        "client_encode_ms_p50": round(statistics.median(enc) * 1e3, 3),
+        "server_bound_to_gpu_cpus": bool(args.server_bind),
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": payload, "d2h_bytes_per_step": payload,
                 "api": "EngineRpcClient.save / load over gRPC to python -m pegaflow_b200.server (CUDA IPC), "
                        "PyLoadState completion"},
@@ -1258,6 +1274,8 @@ def main() -> int:
                     default="llama70b_tp")
     ap.add_argument("--server-shape", default="llama70b_tp", choices=["llama70b_tp", "llama8b"],
                     help="server_e2e: the KV shape moved through the gRPC server")
+    ap.add_argument("--server-bind", action="store_true",
+                    help="server_e2e: start the server on the CPUs local to GPU 0")
     ap.add_argument("--numa-pools", default="off", choices=["off", "node", "device"],
                     help="llama70b_tp_one_engine: one pool, or one per NUMA node / per GPU")
     ap.add_argument("--fp8-requests", type=int, default=64)
