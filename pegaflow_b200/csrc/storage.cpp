@@ -43,6 +43,12 @@ constexpr uint32_t kPoolMaxAllocs = 4000000;  // pinned_pool.rs:61
 
 size_t BlockKeyHash::operator()(const BlockKey& k) const { return static_cast<size_t>(fnv1a(k.ns, k.hash)); }
 
+size_t Storage::shard_of(const BlockKey& k) {
+  // The top bits of a multiplicative mix of the key's hash, so a shard's own
+  // map (which buckets by the same hash) still spreads its keys.
+  return static_cast<size_t>((static_cast<uint64_t>(BlockKeyHash{}(k)) * 0x9E3779B97F4A7C15ull) >> 58);
+}
+
 // ---------------------------------------------------------------------------
 // Pool
 // ---------------------------------------------------------------------------
@@ -295,40 +301,45 @@ void Storage::pre_evict_loop() {
 }
 
 bool Storage::inflight_has_slot(const std::string& ns, const std::string& hash, uint64_t slot) {
-  std::lock_guard<std::mutex> g(inflight_mu_);
-  auto it = inflight_.find(BlockKey{ns, hash});
-  if (it == inflight_.end()) return false;
+  const BlockKey key{ns, hash};
+  InflightShard& sh = shard(key);
+  std::lock_guard<std::mutex> g(sh.mu);
+  auto it = sh.map.find(key);
+  if (it == sh.map.end()) return false;
   return slot < it->second.slots.size() && it->second.slots[slot] != nullptr;
 }
 
 void Storage::insert_slots(const std::string& ns, const std::vector<std::string>& hashes, uint64_t slot,
                            std::vector<LayerBlockPtr>& blocks, uint64_t total_slots) {
-  // Same per-block steps as insert_slot (storage.rs:457-514), with the locks
-  // taken once for the whole list instead of once per block.
+  // Same per-block steps as insert_slot (storage.rs:457-514), with the cache
+  // lock taken once for the whole list; each block takes its shard's lock.
   maybe_drop_stale_inflight();
   std::vector<std::pair<BlockKey, SealedBlockPtr>> sealed;
   {
-    std::unique_lock<std::mutex> gc(cache_mu_);
     std::vector<char> cached(hashes.size(), 0);
-    BlockKey probe{ns, std::string()};
-    for (size_t i = 0; i < hashes.size(); ++i) {
-      probe.hash = hashes[i];
-      cached[i] = index_.count(probe) ? 1 : 0;
+    {
+      std::lock_guard<std::mutex> gc(cache_mu_);
+      BlockKey probe{ns, std::string()};
+      for (size_t i = 0; i < hashes.size(); ++i) {
+        probe.hash = hashes[i];
+        cached[i] = index_.count(probe) ? 1 : 0;
+      }
     }
-    gc.unlock();
-    std::lock_guard<std::mutex> gi(inflight_mu_);
     std::unordered_map<std::string, bool> sealed_here;  // a repeated hash finds its block sealed
     for (size_t i = 0; i < hashes.size(); ++i) {
       if (cached[i]) continue;
       if (!sealed.empty() && sealed_here.count(hashes[i])) continue;
       BlockKey key{ns, hashes[i]};
-      auto it = inflight_.find(key);
-      if (it == inflight_.end()) {
+      InflightShard& sh = shard(key);
+      std::lock_guard<std::mutex> gi(sh.mu);
+      auto it = sh.map.find(key);
+      if (it == sh.map.end()) {
         Inflight fresh;
         fresh.slots.assign(total_slots, nullptr);
         fresh.remaining = total_slots;
         fresh.total_slots = total_slots;
-        it = inflight_.emplace(key, std::move(fresh)).first;
+        it = sh.map.emplace(key, std::move(fresh)).first;
+        inflight_blocks_.fetch_add(1, std::memory_order_relaxed);
       }
       Inflight& ib = it->second;
       if (slot < ib.slots.size() && ib.slots[slot]) continue;
@@ -347,7 +358,8 @@ void Storage::insert_slots(const std::string& ns, const std::vector<std::string>
         auto sb = std::make_shared<SealedBlock>();
         sb->slots = std::move(ib.slots);
         sb->footprint = ib.footprint;
-        inflight_.erase(it);
+        sh.map.erase(it);
+        inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
         sealed_here[key.hash] = true;
         sealed.emplace_back(std::move(key), std::move(sb));
       }
@@ -378,13 +390,14 @@ void Storage::probe_save(const std::string& ns, const std::vector<std::string>& 
       if (index_.count(key)) out->cached[i] = 1;
     }
   }
-  std::lock_guard<std::mutex> g(inflight_mu_);
-  if (inflight_.empty()) return;
+  if (inflight_blocks_.load(std::memory_order_relaxed) == 0) return;
   for (size_t i = 0; i < n; ++i) {
     if (out->cached[i]) continue;
     key.hash = hashes[i];
-    auto it = inflight_.find(key);
-    if (it == inflight_.end()) continue;
+    InflightShard& sh = shard(key);
+    std::lock_guard<std::mutex> g(sh.mu);
+    auto it = sh.map.find(key);
+    if (it == sh.map.end()) continue;
     const std::vector<LayerBlockPtr>& slots = it->second.slots;
     std::vector<char>& f = out->filled[i];
     f.resize(slots.size());
@@ -402,6 +415,11 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
   // so fill-major would start a new inflight block from the later fills: the
   // second pass below does that. That new block cannot seal in this call: it
   // gets at most fills-1 < total_slots slots.
+  //
+  // The hashes are visited shard by shard, one shard lock at a time. The
+  // saves of a block's TP ranks start at different shards (rank r of t at
+  // shard r*64/t), so they sweep the shards side by side instead of queueing
+  // on one lock.
   const size_t n = hashes.size();
   if (fills.empty() || n == 0) return;
   maybe_drop_stale_inflight();
@@ -420,13 +438,35 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
     }
   }
   std::vector<char> cached(n, 0);
-  BlockKey key{ns, std::string()};
+  std::vector<BlockKey> keys;
+  keys.reserve(n);
+  for (size_t i = 0; i < n; ++i) keys.push_back(BlockKey{ns, hashes[i]});
   {
     std::lock_guard<std::mutex> g(cache_mu_);
-    for (size_t i = 0; i < n; ++i) {
-      key.hash = hashes[i];
-      cached[i] = index_.count(key) ? 1 : 0;
+    for (size_t i = 0; i < n; ++i) cached[i] = index_.count(keys[i]) ? 1 : 0;
+  }
+  std::vector<std::vector<uint32_t>> by_shard(kInflightShards);  // positions, in list order
+  for (size_t i = 0; i < n; ++i) {
+    if (!cached[i]) by_shard[shard_of(keys[i])].push_back(static_cast<uint32_t>(i));
+  }
+  // An inflight block with another slot count makes fill-major throw part
+  // way through its first fill; let it do exactly that.
+  if (inflight_blocks_.load(std::memory_order_relaxed) != 0) {
+    bool mismatch = false;
+    for (size_t sh_i = 0; sh_i < kInflightShards && !mismatch; ++sh_i) {
+      if (by_shard[sh_i].empty()) continue;
+      InflightShard& sh = inflight_[sh_i];
+      std::lock_guard<std::mutex> g(sh.mu);
+      if (sh.map.empty()) continue;
+      for (uint32_t i : by_shard[sh_i]) {
+        auto it = sh.map.find(keys[i]);
+        if (it != sh.map.end() && it->second.total_slots != total_slots) {
+          mismatch = true;
+          break;
+        }
+      }
     }
+    if (mismatch) return per_fill();
   }
   struct Seal {
     size_t fill;
@@ -435,34 +475,28 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
     SealedBlockPtr block;
   };
   std::vector<Seal> seals;
-  {
-    std::unique_lock<std::mutex> gi(inflight_mu_);
-    // An inflight block with another slot count makes fill-major throw part
-    // way through its first fill; let it do exactly that.
-    if (!inflight_.empty()) {
-      for (size_t i = 0; i < n; ++i) {
-        if (cached[i]) continue;
-        key.hash = hashes[i];
-        auto it = inflight_.find(key);
-        if (it != inflight_.end() && it->second.total_slots != total_slots) {
-          gi.unlock();
-          return per_fill();
-        }
-      }
-    }
-    std::unordered_set<std::string_view> sealed_here;  // a repeated hash finds its block sealed
-    sealed_here.reserve(n);
-    seals.reserve(n);
-    // Every slot filled by this call: a hash with no inflight block seals at
-    // the last fill, so its block is built directly, without an inflight
-    // entry that would be created and erased at once.
-    const bool all_slots = fills.size() == total_slots;
-    for (size_t i = 0; i < n; ++i) {
-      if (cached[i]) continue;
+  seals.reserve(n);
+  std::unordered_set<std::string_view> sealed_here;  // a repeated hash finds its block sealed
+  sealed_here.reserve(n);
+  // Every slot filled by this call: a hash with no inflight block seals at
+  // the last fill, so its block is built directly, without an inflight
+  // entry that would be created and erased at once.
+  const bool all_slots = fills.size() == total_slots;
+  size_t start = 0;
+  if (total_slots % fills.size() == 0) {
+    const uint64_t tp = total_slots / fills.size();
+    start = static_cast<size_t>((fills.front().slot % tp) * kInflightShards / tp);
+  }
+  for (size_t step = 0; step < kInflightShards; ++step) {
+    const size_t sh_i = (start + step) % kInflightShards;
+    if (by_shard[sh_i].empty()) continue;
+    InflightShard& sh = inflight_[sh_i];
+    std::lock_guard<std::mutex> g(sh.mu);
+    for (uint32_t i : by_shard[sh_i]) {
       if (!sealed_here.empty() && sealed_here.count(hashes[i])) continue;
-      key.hash = hashes[i];
-      auto it = inflight_.find(key);
-      if (it == inflight_.end() && all_slots) {
+      const BlockKey& key = keys[i];
+      auto it = sh.map.find(key);
+      if (it == sh.map.end() && all_slots) {
         auto sb = std::make_shared<SealedBlock>();
         sb->slots.resize(total_slots);
         for (const SlotFill& f : fills) {
@@ -473,14 +507,20 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
         seals.push_back({fills.size() - 1, i, key, std::move(sb)});
         continue;
       }
-      if (it == inflight_.end()) {
+      if (it == sh.map.end()) {
         Inflight fresh;
         fresh.slots.assign(total_slots, nullptr);
         fresh.remaining = total_slots;
         fresh.total_slots = total_slots;
-        it = inflight_.emplace(key, std::move(fresh)).first;
+        it = sh.map.emplace(key, std::move(fresh)).first;
+        inflight_blocks_.fetch_add(1, std::memory_order_relaxed);
       }
       Inflight& ib = it->second;
+      if (ib.total_slots != total_slots) {
+        // Created by a call with another slot count after the check above.
+        throw storage_error("slot count mismatch: expected " + std::to_string(ib.total_slots) + ", got " +
+                            std::to_string(total_slots));
+      }
       for (size_t f = 0; f < fills.size(); ++f) {
         const uint64_t slot = fills[f].slot;
         if (ib.slots[slot]) continue;
@@ -490,7 +530,8 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
           auto sb = std::make_shared<SealedBlock>();
           sb->slots = std::move(ib.slots);
           sb->footprint = ib.footprint;
-          inflight_.erase(it);
+          sh.map.erase(it);
+          inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
           sealed_here.insert(hashes[i]);
           seals.push_back({f, i, key, std::move(sb)});
           break;
@@ -499,8 +540,8 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
     }
   }
   if (seals.empty()) return;
-  auto by_fill = [](const Seal& a, const Seal& b) { return a.fill < b.fill; };
-  if (!std::is_sorted(seals.begin(), seals.end(), by_fill)) std::stable_sort(seals.begin(), seals.end(), by_fill);
+  auto fill_major = [](const Seal& a, const Seal& b) { return a.fill != b.fill ? a.fill < b.fill : a.index < b.index; };
+  if (!std::is_sorted(seals.begin(), seals.end(), fill_major)) std::sort(seals.begin(), seals.end(), fill_major);
   SealListener listener;
   {
     std::lock_guard<std::mutex> g(listener_mu_);
@@ -525,18 +566,20 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
   }
   counters_.insertions.fetch_add(inserted);
   counters_.admission_rejections.fetch_add(rejected);
-  if (refused.empty()) return;
-  std::lock_guard<std::mutex> gi(inflight_mu_);
   for (const Seal* s : refused) {
-    auto it = inflight_.find(s->key);
-    if (it == inflight_.end()) {
+    InflightShard& sh = shard(s->key);
+    std::lock_guard<std::mutex> g(sh.mu);
+    auto it = sh.map.find(s->key);
+    if (it == sh.map.end()) {
       Inflight fresh;
       fresh.slots.assign(total_slots, nullptr);
       fresh.remaining = total_slots;
       fresh.total_slots = total_slots;
-      it = inflight_.emplace(s->key, std::move(fresh)).first;
+      it = sh.map.emplace(s->key, std::move(fresh)).first;
+      inflight_blocks_.fetch_add(1, std::memory_order_relaxed);
     }
     Inflight& ib = it->second;
+    if (ib.total_slots != total_slots) continue;  // another call's block: fill-major would have thrown
     for (size_t f = s->fill + 1; f < fills.size(); ++f) {
       const uint64_t slot = fills[f].slot;
       if (ib.slots[slot]) continue;
@@ -574,14 +617,16 @@ bool Storage::insert_slot(const std::string& ns, const std::string& hash, uint64
   }
   SealedBlockPtr sealed;
   {
-    std::lock_guard<std::mutex> g(inflight_mu_);
-    auto it = inflight_.find(key);
-    if (it == inflight_.end()) {
+    InflightShard& sh = shard(key);
+    std::lock_guard<std::mutex> g(sh.mu);
+    auto it = sh.map.find(key);
+    if (it == sh.map.end()) {
       Inflight fresh;
       fresh.slots.assign(total_slots, nullptr);
       fresh.remaining = total_slots;
       fresh.total_slots = total_slots;
-      it = inflight_.emplace(key, std::move(fresh)).first;
+      it = sh.map.emplace(key, std::move(fresh)).first;
+      inflight_blocks_.fetch_add(1, std::memory_order_relaxed);
     }
     Inflight& ib = it->second;
     if (slot < ib.slots.size() && ib.slots[slot]) return false;
@@ -601,7 +646,8 @@ bool Storage::insert_slot(const std::string& ns, const std::string& hash, uint64
       sealed = std::make_shared<SealedBlock>();
       sealed->slots = std::move(ib.slots);
       sealed->footprint = ib.footprint;
-      inflight_.erase(it);
+      sh.map.erase(it);
+      inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
     }
   }
   if (sealed) {
@@ -670,22 +716,20 @@ SealedBlockPtr Storage::cache_peek(const std::string& ns, const std::string& has
   return it == index_.end() ? nullptr : it->second->second;
 }
 
-uint64_t Storage::inflight_count() {
-  std::lock_guard<std::mutex> g(inflight_mu_);
-  return inflight_.size();
-}
+uint64_t Storage::inflight_count() { return inflight_blocks_.load(std::memory_order_relaxed); }
 
 uint64_t Storage::drop_stale_inflight() {
   if (cfg_.inflight_max_age_ms == 0) return 0;
   const auto now = std::chrono::steady_clock::now();
   const auto max_age = std::chrono::milliseconds(cfg_.inflight_max_age_ms);
   std::vector<Inflight> dropped;  // their pool memory is released after the lock
-  {
-    std::lock_guard<std::mutex> g(inflight_mu_);
-    for (auto it = inflight_.begin(); it != inflight_.end();) {
+  for (InflightShard& sh : inflight_) {
+    std::lock_guard<std::mutex> g(sh.mu);
+    for (auto it = sh.map.begin(); it != sh.map.end();) {
       if (now - it->second.created > max_age) {
         dropped.push_back(std::move(it->second));
-        it = inflight_.erase(it);
+        it = sh.map.erase(it);
+        inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
       } else {
         ++it;
       }
@@ -729,10 +773,13 @@ Storage::BlockView Storage::cache_view() {
 }
 
 Storage::BlockView Storage::inflight_view() {
-  std::lock_guard<std::mutex> g(inflight_mu_);
   BlockView out;
-  out.reserve(inflight_.size());
-  for (const auto& kv : inflight_) out.emplace_back(kv.first.ns + '\0' + kv.first.hash, slot_addresses(kv.second.slots));
+  for (InflightShard& sh : inflight_) {
+    std::lock_guard<std::mutex> g(sh.mu);
+    for (const auto& kv : sh.map) {
+      out.emplace_back(kv.first.ns + '\0' + kv.first.hash, slot_addresses(kv.second.slots));
+    }
+  }
   std::sort(out.begin(), out.end());
   return out;
 }

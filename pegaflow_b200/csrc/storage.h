@@ -9,6 +9,7 @@
 #pragma once
 
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <chrono>
 #include <condition_variable>
@@ -244,8 +245,20 @@ class Storage {
 
   std::vector<std::shared_ptr<PinnedPool>> pools_;
   StorageConfig cfg_;
-  std::mutex inflight_mu_;
-  std::unordered_map<BlockKey, Inflight, BlockKeyHash> inflight_;
+  // Inflight blocks, split into shards by key, each with its own lock: the
+  // saves of different TP ranks fill different slots of the same hashes at
+  // the same time, and under one lock for all blocks they ran one after
+  // another (the reference keeps inflight blocks in a sharded concurrent
+  // map). A call takes one shard's lock at a time.
+  static constexpr size_t kInflightShards = 64;
+  struct InflightShard {
+    std::mutex mu;
+    std::unordered_map<BlockKey, Inflight, BlockKeyHash> map;
+  };
+  std::array<InflightShard, kInflightShards> inflight_;
+  std::atomic<uint64_t> inflight_blocks_{0};  // entries over all shards
+  static size_t shard_of(const BlockKey& k);
+  InflightShard& shard(const BlockKey& k) { return inflight_[shard_of(k)]; }
   std::mutex cache_mu_;
   LruList lru_;  // front = least recently used
   std::unordered_map<BlockKey, LruList::iterator, BlockKeyHash> index_;
