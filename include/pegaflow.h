@@ -221,8 +221,7 @@ int pf_p2p_transfer(pf_executor* exec, int32_t peer_device, int push,
  * an 8 MiB staging slot. A save whose plan (layer table + block ids + offsets)
  * exceeds 1 MiB, or with a copy unit above 4 MiB, fails with
  * PF_ERR_INVALID_ARGUMENT. The first call on a device resolves the arrays'
- * addresses (cudaGetSymbolAddress) and should come before any stream capture.
- * The arrays are reserved in device memory when that first call loads the
+ * addresses (cudaGetSymbolAddress). The arrays are reserved in device memory when that first call loads the
  * library's device code on the device (CUDA loads modules lazily), so make
  * the first call before the caller's allocator claims HBM: the warm-up call
  * pf_save_blocks_noalloc(device, NULL, 0, stream) loads the code, reserves

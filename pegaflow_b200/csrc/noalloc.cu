@@ -19,8 +19,7 @@
 // than the staging slot, is rejected with PF_ERR_INVALID_ARGUMENT.
 //
 // Set-up: the first call on a device (with that device current) resolves the
-// arrays' device addresses with cudaGetSymbolAddress; make that first call
-// before any stream capture. Every call on a device shares the same arrays
+// arrays' device addresses with cudaGetSymbolAddress. Every call on a device shares the same arrays
 // and leaves its contents behind: nothing in them needs to start at zero (the
 // plan is written whole by each call and each staging range is written by the
 // kernel before it is copied out). Calls that overlap on the GPU (on
