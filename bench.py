@@ -1524,6 +1524,7 @@ def main() -> int:
     for k in range(args.warmup):
         e2e_step(-1 - k)
     eng.executor(local).reset_stats()  # host time of the timed calls only (no first-call allocations)
+    eng_before = eng.metrics()
     scribble(torch, tensors, dst)
     barrier()
     torch.cuda.synchronize()
@@ -1539,6 +1540,11 @@ def main() -> int:
     eng_metrics = eng.metrics()
     eng_ex = eng.executor(local).stats()
     eng_metrics["executor_host_ms_per_call"] = eng_ex["host_ms"] / max(1, 2 * e2e_steps)
+    # Per timed step (the warm-up's first-call costs left out).
+    eng_metrics["phases_ms_per_step"] = {
+        k: round((eng_metrics[k] - eng_before[k]) / e2e_steps, 3)
+        for k in ("save_plan_ms", "save_transfer_ms", "save_insert_ms", "load_lookup_ms", "load_queue_ms",
+                  "load_setup_ms", "load_transfer_ms", "load_first_layer_ms")}
     eng.close()
 
     # ---- the reference's copy strategy on the same GPU ------------------------
@@ -1674,7 +1680,7 @@ def main() -> int:
             "engine_metrics": {k: (round(eng_metrics[k], 2) if isinstance(eng_metrics[k], float) else eng_metrics[k])
                                for k in ("save_bytes", "load_bytes", "load_failures", "cache_block_evictions",
                                          "save_plan_ms", "save_transfer_ms", "save_insert_ms", "save_ms",
-                                         "load_ms", "executor_host_ms_per_call")},
+                                         "load_ms", "executor_host_ms_per_call", "phases_ms_per_step")},
         }
         print(json.dumps(line), flush=True)
     ranks.close()

@@ -541,6 +541,12 @@ typedef struct pf_engine_metrics {
   double save_transfer_ms;  /* pack kernels + D2H, waited on */
   double save_insert_ms;    /* slot bookkeeping after the copy (host) */
   uint64_t inflight_dropped; /* inflight blocks released after the age limit (ABI 3) */
+  /* Load phases (ABI 4), summed over load calls: */
+  double load_lookup_ms;      /* cache lookup + task build on the caller's thread */
+  double load_queue_ms;       /* task queued until the device's load thread takes it */
+  double load_setup_ms;       /* LoadState attach + pool pointer tables (load thread) */
+  double load_transfer_ms;    /* executor load: plan, H2D + unpack, waited on */
+  double load_first_layer_ms; /* task queued until its first layer is marked ready */
 } pf_engine_metrics;
 int pf_engine_metrics_get(pf_engine* e, pf_engine_metrics* out);
 

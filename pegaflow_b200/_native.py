@@ -197,6 +197,11 @@ class EngineMetrics(Structure):
         ("save_transfer_ms", c_double),
         ("save_insert_ms", c_double),
         ("inflight_dropped", c_uint64),
+        ("load_lookup_ms", c_double),
+        ("load_queue_ms", c_double),
+        ("load_setup_ms", c_double),
+        ("load_transfer_ms", c_double),
+        ("load_first_layer_ms", c_double),
     ]
 
 

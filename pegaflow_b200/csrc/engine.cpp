@@ -114,6 +114,7 @@ void DeviceWorker::process(LoadTask& task) {
   const auto t0 = Clock::now();
   bool ok = true;
   uint64_t bytes = 0;
+  Clock::time_point t_setup = t0, t_first = t0, t_done = t0;
   // A LoadState with a per-layer extension covering every requested layer
   // gets its words raised as layers land (load_with_layer_words).
   pf_load_state* ls = nullptr;
@@ -147,11 +148,14 @@ void DeviceWorker::process(LoadTask& task) {
       layers.push_back(pl);
       bytes += load_geometry(L.reg).unit_bytes * load_geometry(L.reg).units * L.ids.size();
     }
+    t_setup = Clock::now();
     if (words) {
-      load_with_layer_words(layers.data(), layers.size(), words);
+      t_first = load_with_layer_words(layers.data(), layers.size(), words);
     } else {
       exec_->load_sync(layers.data(), layers.size(), nullptr);
+      t_first = Clock::now();
     }
+    t_done = Clock::now();
   } catch (const std::exception& e) {
     ok = false;
     fprintf(stderr, "pegaflow_b200: load task failed: %s\n", e.what());
@@ -170,12 +174,19 @@ void DeviceWorker::process(LoadTask& task) {
   if (ok && bytes > 0) {
     counters_->load_bytes.fetch_add(bytes);
     counters_->load_calls.fetch_add(1);
+    auto ms = [](Clock::time_point a, Clock::time_point b) {
+      return std::chrono::duration<double, std::milli>(b - a).count();
+    };
     std::lock_guard<std::mutex> g(counters_->ms_mu);
     counters_->load_ms += ms_since(t0);
+    counters_->load_queue_ms += ms(task.queued, t0);
+    counters_->load_setup_ms += ms(t0, t_setup);
+    counters_->load_transfer_ms += ms(t_setup, t_done);
+    counters_->load_first_layer_ms += ms(task.queued, t_first);
   }
 }
 
-void DeviceWorker::load_with_layer_words(const pf_load_layer* layers, size_t n, int64_t* words) {
+Clock::time_point DeviceWorker::load_with_layer_words(const pf_load_layer* layers, size_t n, int64_t* words) {
   // Registering the LoadState page with CUDA for every task would cost a
   // driver round trip on each side of every load (and unregistering can stall
   // other work), so the kernels raise flags in one mapped pinned array this
@@ -193,6 +204,8 @@ void DeviceWorker::load_with_layer_words(const pf_load_layer* layers, size_t n, 
   exec_->load(layers, n, s, const_cast<int64_t*>(flags));
   std::vector<char> copied(n, 0);
   size_t left = n;
+  Clock::time_point first{};
+  bool any = false;
   for (;;) {
     const cudaError_t q = cudaStreamQuery(s);
     for (size_t l = 0; l < n && left; ++l) {
@@ -202,6 +215,10 @@ void DeviceWorker::load_with_layer_words(const pf_load_layer* layers, size_t n, 
         __atomic_store_n(&words[l], int64_t{1}, __ATOMIC_RELEASE);
         copied[l] = 1;
         --left;
+        if (!any) {
+          first = Clock::now();
+          any = true;
+        }
       }
     }
     if (q == cudaSuccess) break;
@@ -215,6 +232,7 @@ void DeviceWorker::load_with_layer_words(const pf_load_layer* layers, size_t n, 
   for (size_t l = 0; l < n; ++l) {
     if (!copied[l]) __atomic_store_n(&words[l], int64_t{1}, __ATOMIC_RELEASE);
   }
+  return any ? first : Clock::now();
 }
 
 // ---------------------------------------------------------------------------
@@ -711,6 +729,7 @@ void Engine::batch_load_inner(const std::string& instance_id, uint64_t tp_rank, 
                               const std::string& shm, const std::vector<std::string>& layer_names,
                               const std::vector<int32_t>& block_ids, const std::vector<std::string>& hashes) {
   // lib.rs:990-1069
+  const auto t0 = Clock::now();
   auto inst = get_instance(instance_id);
   auto gpu = get_gpu(*inst, device_id);
   if (!gpu) throw worker_missing(instance_id, device_id);
@@ -758,6 +777,11 @@ void Engine::batch_load_inner(const std::string& instance_id, uint64_t tp_rank, 
   }
   if (!gpu->worker) throw cuda_init("engine pool is plain host memory; transfers need a pinned pool");
   task.hold = std::move(cache);
+  task.queued = Clock::now();
+  {
+    std::lock_guard<std::mutex> g(counters_.ms_mu);
+    counters_.load_lookup_ms += std::chrono::duration<double, std::milli>(task.queued - t0).count();
+  }
   gpu->worker->submit_load(std::move(task));
 }
 
@@ -788,6 +812,11 @@ void Engine::metrics(pf_engine_metrics* out) {
     out->save_plan_ms = counters_.save_plan_ms;
     out->save_transfer_ms = counters_.save_transfer_ms;
     out->save_insert_ms = counters_.save_insert_ms;
+    out->load_lookup_ms = counters_.load_lookup_ms;
+    out->load_queue_ms = counters_.load_queue_ms;
+    out->load_setup_ms = counters_.load_setup_ms;
+    out->load_transfer_ms = counters_.load_transfer_ms;
+    out->load_first_layer_ms = counters_.load_first_layer_ms;
   }
   auto& sc = storage_->counters();
   out->cache_block_insertions = sc.insertions.load();

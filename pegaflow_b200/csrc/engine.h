@@ -1,6 +1,7 @@
 // PegaEngine (pegaflow-core/src/lib.rs:93-1069) over the B200 executor.
 #pragma once
 
+#include <chrono>
 #include <condition_variable>
 #include <cstdint>
 #include <deque>
@@ -37,6 +38,7 @@ struct EngineCounters {
   std::mutex ms_mu;
   double save_ms = 0, load_ms = 0;
   double save_plan_ms = 0, save_transfer_ms = 0, save_insert_ms = 0;
+  double load_lookup_ms = 0, load_queue_ms = 0, load_setup_ms = 0, load_transfer_ms = 0, load_first_layer_ms = 0;
 };
 
 // One load task (gpu_worker.rs:12-28): layers with the LayerBlocks they read,
@@ -51,6 +53,7 @@ struct LoadTask {
   std::vector<LoadLayer> layers;
   std::string shm;
   std::vector<SealedBlockPtr> hold;  // the sealed blocks read by the task
+  std::chrono::steady_clock::time_point queued;  // when the task was handed to the load thread
 };
 
 // Per-device worker: the executor plus the load thread of GpuWorkerPool
@@ -78,7 +81,8 @@ class DeviceWorker {
   // layer l lands: the kernels raise flags in this worker's own mapped
   // pinned array, and this thread copies each new one into `words` while the
   // load runs. The LoadState page itself is never registered with CUDA.
-  void load_with_layer_words(const pf_load_layer* layers, size_t n, int64_t* words);
+  // Returns when the first layer was marked ready.
+  std::chrono::steady_clock::time_point load_with_layer_words(const pf_load_layer* layers, size_t n, int64_t* words);
   std::unique_ptr<Executor> exec_;
   std::unique_ptr<PinnedMemory> flags_mem_;  // per-layer flags the kernels raise (grown on demand)
   EngineCounters* counters_;
