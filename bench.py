@@ -867,10 +867,10 @@ def run_one_engine(args) -> None:
         def load(r):
             s = PyLoadState(len(names))
             eng.batch_load_kv_blocks("tp", r, r, s.shm_name(), names, dst_l, hashes)
-            deadline = time.perf_counter() + 120.0
-            while not s.is_ready():
-                if time.perf_counter() > deadline:
-                    raise TimeoutError("engine load did not complete within 120 s")
+            # Each rank's vLLM worker polls its LoadState in its own process;
+            # here the ranks share one interpreter, so the wait blocks in the
+            # library (GIL released) instead of spinning against the others.
+            eng.wait_loads(r, 120.0)
             ok = s.get_state() == 1
             s.close()
             if not ok:
@@ -883,9 +883,14 @@ def run_one_engine(args) -> None:
     for sh in shards:
         scribble(torch, sh, dst)
     torch.cuda.synchronize()
+    m0 = eng.metrics()
     times = [one_step(k) for k in range(args.steps)]
     verified = all(restored(torch, sh, src, dst) for sh in shards)
     m = eng.metrics()
+    # Per timed step, summed over the ranks' calls.
+    phases = {k: round((m[k] - m0[k]) / len(times), 3)
+              for k in ("save_plan_ms", "save_transfer_ms", "save_insert_ms", "load_lookup_ms", "load_queue_ms",
+                        "load_setup_ms", "load_transfer_ms", "load_first_layer_ms")}
     eng.close()
     save_s = statistics.median(t for t, _ in times)
     load_s = statistics.median(t for _, t in times)
@@ -905,8 +910,10 @@ def run_one_engine(args) -> None:
         "engine": {k: (round(m[k], 2) if isinstance(m[k], float) else m[k])
                    for k in ("load_failures", "cache_block_evictions", "pool_alloc_failures", "save_calls",
                              "save_plan_ms", "save_transfer_ms", "save_insert_ms", "save_ms", "load_ms")},
+        "engine_phases_ms_per_step": phases,
         "how": "host wall clock per phase (all ranks save at once, then all load at once); value = all ranks' "
-               "save + load bytes / summed phase times; engine *_ms are summed over every call of every rank",
+               "save + load bytes / summed phase times; engine *_ms are summed over every call of every rank "
+               "(engine_phases_ms_per_step: over the timed steps, divided by the steps)",
     }
     print(json.dumps(line), flush=True)
 
