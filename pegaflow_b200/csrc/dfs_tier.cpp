@@ -432,7 +432,7 @@ void DfsTier::write_and_register(const std::string& ns,
     m.file = file_name;
     m.offset = offset;
     m.total_slots = total_slots;
-    for (const LayerBlockPtr& s : kb.second->slots) m.slots.push_back(SlotMeta{s && s->v_ptr != nullptr, s ? s->size : 0});
+    for (const LayerBlock* s : kb.second->slots) m.slots.push_back(SlotMeta{s && s->v_ptr != nullptr, s ? s->size : 0});
     offset += m.total_size();
     total_size += kb.second->footprint;
     metas.push_back(std::move(m));
@@ -442,7 +442,7 @@ void DfsTier::write_and_register(const std::string& ns,
   const int fd = ::open(path.c_str(), O_WRONLY | O_CREAT | O_TRUNC | O_CLOEXEC, 0644);
   if (fd < 0) ok = false;
   for (size_t b = 0; ok && b < blocks.size(); ++b) {
-    for (const LayerBlockPtr& s : blocks[b].second->slots) {
+    for (const LayerBlock* s : blocks[b].second->slots) {
       if (!s) continue;
       if (s->v_ptr) {
         const uint64_t half = s->size / 2;
@@ -671,7 +671,8 @@ void DfsTier::run_prefetch(PrefetchTask& task) {
       }
       auto sealed = std::make_shared<SealedBlock>();
       sealed->slots.resize(m.slots.size());
-      for (size_t s = 0; s < m.slots.size(); ++s) sealed->slots[s] = layer_block_at(batch, s);
+      for (size_t s = 0; s < m.slots.size(); ++s) sealed->slots[s] = &batch->blocks[s];
+      sealed->owners.push_back(batch);
       sealed->footprint = size;
       rebuilt.emplace_back(hash, std::move(sealed));
     }

@@ -757,7 +757,7 @@ void Engine::batch_load_inner(const std::string& instance_id, uint64_t tp_rank, 
       if (block_ids[k] < 0) continue;
       if (slot >= cache[k]->slots.size()) continue;
       L.ids.push_back(block_ids[k]);
-      L.blocks.push_back(cache[k]->slots[slot].get());
+      L.blocks.push_back(cache[k]->slots[slot]);
     }
     // Layers without blocks stay in the task (as empty entries) so per-layer
     // completion words line up with layer_names; the executor raises them at once.

@@ -36,6 +36,7 @@ uint64_t splitmix64(uint64_t x) {
 
 constexpr uint64_t kDefaultBytesPerValue = 128ull << 20;  // cache.rs:14
 constexpr uint64_t kReclaimBatch = 64;                      // storage.rs:41
+constexpr int kMaxDropWaits = 64;  // allocate: waits for other threads' drops before failing
 constexpr uint64_t kPoolMinUnit = 64;
 constexpr uint32_t kPoolMaxAllocs = 4000000;  // pinned_pool.rs:61
 
@@ -195,10 +196,14 @@ std::shared_ptr<PoolAllocation> Storage::allocate(uint64_t size, size_t pool) {
   // The allocator succeeds exactly when its largest-free report covers the
   // request, so the retry below is taken at most once per reclaim that freed
   // something; a retry that frees nothing ends the loop (the reference would
-  // spin if the allocator ran out of nodes).
+  // spin if the allocator ran out of nodes). One exception: when concurrent
+  // saves reclaim at once, another thread may hold the last evicted blocks
+  // (taken from the LRU list, not yet dropped), so this thread finds nothing
+  // to evict although their memory is about to come back. It waits for those
+  // drops and tries again, a bounded number of times.
   pool = std::min(pool, pools_.size() - 1);
   PinnedPool& p = *pools_[pool];
-  for (;;) {
+  for (int waits = 0;;) {
     if (auto a = p.allocate(size)) return a;
     uint64_t freed = 0;
     reclaim_until_fits(size, pool, &freed);
@@ -206,15 +211,36 @@ std::shared_ptr<PoolAllocation> Storage::allocate(uint64_t size, size_t pool) {
     if (p.largest_free() >= size) {
       if (auto a = p.allocate(size)) return a;
     }
+    if (waits < kMaxDropWaits && wait_for_drops(p, size)) {
+      ++waits;
+      continue;
+    }
     counters_.pool_alloc_failures.fetch_add(1);
     return nullptr;
   }
 }
 
+bool Storage::wait_for_drops(PinnedPool& p, uint64_t size) {
+  // Drops take microseconds to milliseconds; give up after one second.
+  if (dropping_.load(std::memory_order_acquire) == 0) return false;
+  const auto limit = std::chrono::steady_clock::now() + std::chrono::seconds(1);
+  while (dropping_.load(std::memory_order_acquire) != 0 && p.largest_free() < size) {
+    if (std::chrono::steady_clock::now() > limit) return false;
+    std::this_thread::yield();
+  }
+  return true;
+}
+
+void Storage::drop_evicted(std::vector<SealedBlockPtr>& evicted) {
+  if (evicted.empty()) return;
+  evicted.clear();  // frees pool memory whose last holder this was
+  dropping_.fetch_sub(1, std::memory_order_acq_rel);
+}
+
 bool Storage::holds_memory_in(const SealedBlock& b, size_t pool) const {
   // A slot's K and V come from one save call on one device, so one pool.
   const PinnedPool& p = *pools_[pool];
-  for (const LayerBlockPtr& s : b.slots) {
+  for (const LayerBlock* s : b.slots) {
     if (s && p.contains(s->k_ptr)) return true;
   }
   return false;
@@ -235,7 +261,10 @@ std::vector<SealedBlockPtr> Storage::evict_lru(uint64_t max_blocks, uint64_t byt
     index_.erase(it->first);
     it = lru_.erase(it);
   }
-  return out;  // dropped by the caller outside the cache lock: frees pool memory
+  // Dropped by the caller outside the cache lock, with drop_evicted; until
+  // then dropping_ tells other reclaiming threads that memory is on its way.
+  if (!out.empty()) dropping_.fetch_add(1, std::memory_order_acq_rel);
+  return out;
 }
 
 void Storage::reclaim_until_fits(uint64_t required, size_t pool, uint64_t* freed_blocks) {
@@ -247,7 +276,7 @@ void Storage::reclaim_until_fits(uint64_t required, size_t pool, uint64_t* freed
     if (evicted.empty()) break;
     *freed_blocks += evicted.size();
     counters_.evictions.fetch_add(evicted.size());
-    evicted.clear();
+    drop_evicted(evicted);
   }
 }
 
@@ -293,7 +322,7 @@ void Storage::pre_evict_loop() {
         const uint64_t need = target > free_bytes ? target - free_bytes : 0;
         std::vector<SealedBlockPtr> evicted = evict_lru(UINT64_MAX, need, i);
         counters_.evictions.fetch_add(evicted.size());
-        evicted.clear();
+        drop_evicted(evicted);
       }
     }
     lk.lock();
@@ -352,11 +381,13 @@ void Storage::insert_slots(const std::string& ns, const std::vector<std::string>
                             std::to_string(ib.total_slots) + " slots)");
       }
       ib.footprint += blocks[i]->size;
-      ib.slots[slot] = std::move(blocks[i]);
+      ib.slots[slot] = blocks[i].get();
+      ib.owners.push_back(std::move(blocks[i]));
       ib.remaining -= 1;
       if (ib.remaining == 0) {
         auto sb = std::make_shared<SealedBlock>();
         sb->slots = std::move(ib.slots);
+        sb->owners = std::move(ib.owners);
         sb->footprint = ib.footprint;
         sh.map.erase(it);
         inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
@@ -398,7 +429,7 @@ void Storage::probe_save(const std::string& ns, const std::vector<std::string>& 
     std::lock_guard<std::mutex> g(sh.mu);
     auto it = sh.map.find(key);
     if (it == sh.map.end()) continue;
-    const std::vector<LayerBlockPtr>& slots = it->second.slots;
+    const std::vector<const LayerBlock*>& slots = it->second.slots;
     std::vector<char>& f = out->filled[i];
     f.resize(slots.size());
     for (size_t s = 0; s < slots.size(); ++s) f[s] = slots[s] ? 1 : 0;
@@ -478,6 +509,15 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
   seals.reserve(n);
   std::unordered_set<std::string_view> sealed_here;  // a repeated hash finds its block sealed
   sealed_here.reserve(n);
+  // One owner for the batches of every fill: each block this call touches
+  // holds it once (instead of one reference per slot).
+  SlotOwner owner;
+  {
+    auto group = std::make_shared<std::vector<std::shared_ptr<LayerBlockBatch>>>();
+    group->reserve(fills.size());
+    for (const SlotFill& f : fills) group->push_back(f.batch);
+    owner = std::move(group);
+  }
   // Every slot filled by this call: a hash with no inflight block seals at
   // the last fill, so its block is built directly, without an inflight
   // entry that would be created and erased at once.
@@ -501,8 +541,9 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
         sb->slots.resize(total_slots);
         for (const SlotFill& f : fills) {
           sb->footprint += f.batch->blocks[i].size;
-          sb->slots[f.slot] = layer_block_at(f.batch, i);
+          sb->slots[f.slot] = &f.batch->blocks[i];
         }
+        sb->owners.push_back(owner);
         sealed_here.insert(hashes[i]);
         seals.push_back({fills.size() - 1, i, key, std::move(sb)});
         continue;
@@ -521,14 +562,20 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
         throw storage_error("slot count mismatch: expected " + std::to_string(ib.total_slots) + ", got " +
                             std::to_string(total_slots));
       }
+      bool owned = false;
       for (size_t f = 0; f < fills.size(); ++f) {
         const uint64_t slot = fills[f].slot;
         if (ib.slots[slot]) continue;
+        if (!owned) {
+          ib.owners.push_back(owner);
+          owned = true;
+        }
         ib.footprint += fills[f].batch->blocks[i].size;
-        ib.slots[slot] = layer_block_at(fills[f].batch, i);
+        ib.slots[slot] = &fills[f].batch->blocks[i];
         if (--ib.remaining == 0) {
           auto sb = std::make_shared<SealedBlock>();
           sb->slots = std::move(ib.slots);
+          sb->owners = std::move(ib.owners);
           sb->footprint = ib.footprint;
           sh.map.erase(it);
           inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
@@ -580,11 +627,16 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
     }
     Inflight& ib = it->second;
     if (ib.total_slots != total_slots) continue;  // another call's block: fill-major would have thrown
+    bool owned = false;
     for (size_t f = s->fill + 1; f < fills.size(); ++f) {
       const uint64_t slot = fills[f].slot;
       if (ib.slots[slot]) continue;
+      if (!owned) {
+        ib.owners.push_back(owner);
+        owned = true;
+      }
       ib.footprint += fills[f].batch->blocks[s->index].size;
-      ib.slots[slot] = layer_block_at(fills[f].batch, s->index);
+      ib.slots[slot] = &fills[f].batch->blocks[s->index];
       --ib.remaining;
     }
   }
@@ -640,11 +692,13 @@ bool Storage::insert_slot(const std::string& ns, const std::string& hash, uint64
                           " slots)");
     }
     ib.footprint += block->size;
-    ib.slots[slot] = std::move(block);
+    ib.slots[slot] = block.get();
+    ib.owners.push_back(std::move(block));
     ib.remaining -= 1;
     if (ib.remaining == 0) {
       sealed = std::make_shared<SealedBlock>();
       sealed->slots = std::move(ib.slots);
+      sealed->owners = std::move(ib.owners);
       sealed->footprint = ib.footprint;
       sh.map.erase(it);
       inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
@@ -756,19 +810,11 @@ uint64_t Storage::cached_count() {
   return lru_.size();
 }
 
-namespace {
-std::vector<const LayerBlock*> slot_addresses(const std::vector<LayerBlockPtr>& slots) {
-  std::vector<const LayerBlock*> out(slots.size());
-  for (size_t s = 0; s < slots.size(); ++s) out[s] = slots[s].get();
-  return out;
-}
-}  // namespace
-
 Storage::BlockView Storage::cache_view() {
   std::lock_guard<std::mutex> g(cache_mu_);
   BlockView out;
   out.reserve(lru_.size());
-  for (const auto& kv : lru_) out.emplace_back(kv.first.ns + '\0' + kv.first.hash, slot_addresses(kv.second->slots));
+  for (const auto& kv : lru_) out.emplace_back(kv.first.ns + '\0' + kv.first.hash, kv.second->slots);
   return out;
 }
 
@@ -777,7 +823,7 @@ Storage::BlockView Storage::inflight_view() {
   for (InflightShard& sh : inflight_) {
     std::lock_guard<std::mutex> g(sh.mu);
     for (const auto& kv : sh.map) {
-      out.emplace_back(kv.first.ns + '\0' + kv.first.hash, slot_addresses(kv.second.slots));
+      out.emplace_back(kv.first.ns + '\0' + kv.first.hash, kv.second.slots);
     }
   }
   std::sort(out.begin(), out.end());

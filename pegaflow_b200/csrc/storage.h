@@ -86,6 +86,12 @@ using LayerBlockPtr = std::shared_ptr<LayerBlock>;
 inline LayerBlockPtr layer_block_at(const std::shared_ptr<LayerBlockBatch>& batch, size_t i) {
   return LayerBlockPtr(batch, &batch->blocks[i]);
 }
+// Keeps the batches that a block's slots point into alive: a LayerBlockPtr
+// (its batch), or the group of every batch one multi-slot insert call wrote.
+// A block holds one owner per call that filled any of its slots, so a TP
+// block of L layers saved by T ranks holds T owners, not L x T batch
+// references; dropping an evicted block is T reference-count decrements.
+using SlotOwner = std::shared_ptr<const void>;
 
 // One layer's share of a multi-slot insert: block i of `batch` goes into
 // `slot` of hash i.
@@ -105,7 +111,9 @@ struct SaveProbe {
 };
 
 struct SealedBlock {
-  std::vector<LayerBlockPtr> slots;
+  // Per slot, its host bytes (all set once sealed); valid while `owners` lives.
+  std::vector<const LayerBlock*> slots;
+  std::vector<SlotOwner> owners;
   uint64_t footprint = 0;
 };
 using SealedBlockPtr = std::shared_ptr<SealedBlock>;
@@ -227,11 +235,19 @@ class Storage {
   // Evicts cached blocks in LRU order until `bytes` of footprint are gone,
   // taking only blocks that hold memory in `pool` when there are several.
   std::vector<SealedBlockPtr> evict_lru(uint64_t max_blocks, uint64_t bytes, size_t pool);
+  // Drops what evict_lru returned (releasing pool memory) and ends its
+  // dropping_ count. wait_for_drops waits (at most 1 s) until no thread holds
+  // evicted blocks or `p` has room for `size`; false when no thread held any
+  // or the wait ran out.
+  void drop_evicted(std::vector<SealedBlockPtr>& evicted);
+  bool wait_for_drops(PinnedPool& p, uint64_t size);
+  std::atomic<int> dropping_{0};  // evict_lru results not yet dropped
   bool holds_memory_in(const SealedBlock& b, size_t pool) const;
   void pre_evict_loop();
 
   struct Inflight {
-    std::vector<LayerBlockPtr> slots;
+    std::vector<const LayerBlock*> slots;  // null = not filled yet
+    std::vector<SlotOwner> owners;
     uint64_t remaining;
     uint64_t total_slots;
     uint64_t footprint = 0;
