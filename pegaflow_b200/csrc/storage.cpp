@@ -329,6 +329,27 @@ void Storage::pre_evict_loop() {
   }
 }
 
+Storage::InflightIt Storage::inflight_add(InflightShard& sh, const BlockKey& key, uint64_t total_slots) {
+  Inflight fresh;
+  fresh.slots.assign(total_slots, nullptr);
+  fresh.remaining = total_slots;
+  fresh.total_slots = total_slots;
+  auto it = sh.map.emplace(key, std::move(fresh)).first;
+  if (++sh.totals[total_slots] == 1) sh.summarize();
+  inflight_blocks_.fetch_add(1, std::memory_order_relaxed);
+  return it;
+}
+
+Storage::InflightIt Storage::inflight_remove(InflightShard& sh, InflightIt it) {
+  auto t = sh.totals.find(it->second.total_slots);
+  if (t != sh.totals.end() && --t->second == 0) {
+    sh.totals.erase(t);
+    sh.summarize();
+  }
+  inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
+  return sh.map.erase(it);
+}
+
 bool Storage::inflight_has_slot(const std::string& ns, const std::string& hash, uint64_t slot) {
   const BlockKey key{ns, hash};
   InflightShard& sh = shard(key);
@@ -363,12 +384,7 @@ void Storage::insert_slots(const std::string& ns, const std::vector<std::string>
       std::lock_guard<std::mutex> gi(sh.mu);
       auto it = sh.map.find(key);
       if (it == sh.map.end()) {
-        Inflight fresh;
-        fresh.slots.assign(total_slots, nullptr);
-        fresh.remaining = total_slots;
-        fresh.total_slots = total_slots;
-        it = sh.map.emplace(key, std::move(fresh)).first;
-        inflight_blocks_.fetch_add(1, std::memory_order_relaxed);
+        it = inflight_add(sh, key, total_slots);
       }
       Inflight& ib = it->second;
       if (slot < ib.slots.size() && ib.slots[slot]) continue;
@@ -389,8 +405,7 @@ void Storage::insert_slots(const std::string& ns, const std::vector<std::string>
         sb->slots = std::move(ib.slots);
         sb->owners = std::move(ib.owners);
         sb->footprint = ib.footprint;
-        sh.map.erase(it);
-        inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
+        inflight_remove(sh, it);
         sealed_here[key.hash] = true;
         sealed.emplace_back(std::move(key), std::move(sb));
       }
@@ -481,14 +496,16 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
     if (!cached[i]) by_shard[shard_of(keys[i])].push_back(static_cast<uint32_t>(i));
   }
   // An inflight block with another slot count makes fill-major throw part
-  // way through its first fill; let it do exactly that.
+  // way through its first fill; let it do exactly that. (A snapshot: such a
+  // block created after this check meets the throw in the main pass.)
   if (inflight_blocks_.load(std::memory_order_relaxed) != 0) {
     bool mismatch = false;
     for (size_t sh_i = 0; sh_i < kInflightShards && !mismatch; ++sh_i) {
       if (by_shard[sh_i].empty()) continue;
       InflightShard& sh = inflight_[sh_i];
+      const uint64_t sole = sh.sole_total.load(std::memory_order_acquire);
+      if (sole == 0 || sole == total_slots) continue;  // every entry here has this call's slot count
       std::lock_guard<std::mutex> g(sh.mu);
-      if (sh.map.empty()) continue;
       for (uint32_t i : by_shard[sh_i]) {
         auto it = sh.map.find(keys[i]);
         if (it != sh.map.end() && it->second.total_slots != total_slots) {
@@ -549,12 +566,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
         continue;
       }
       if (it == sh.map.end()) {
-        Inflight fresh;
-        fresh.slots.assign(total_slots, nullptr);
-        fresh.remaining = total_slots;
-        fresh.total_slots = total_slots;
-        it = sh.map.emplace(key, std::move(fresh)).first;
-        inflight_blocks_.fetch_add(1, std::memory_order_relaxed);
+        it = inflight_add(sh, key, total_slots);
       }
       Inflight& ib = it->second;
       if (ib.total_slots != total_slots) {
@@ -577,8 +589,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
           sb->slots = std::move(ib.slots);
           sb->owners = std::move(ib.owners);
           sb->footprint = ib.footprint;
-          sh.map.erase(it);
-          inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
+          inflight_remove(sh, it);
           sealed_here.insert(hashes[i]);
           seals.push_back({f, i, key, std::move(sb)});
           break;
@@ -618,12 +629,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
     std::lock_guard<std::mutex> g(sh.mu);
     auto it = sh.map.find(s->key);
     if (it == sh.map.end()) {
-      Inflight fresh;
-      fresh.slots.assign(total_slots, nullptr);
-      fresh.remaining = total_slots;
-      fresh.total_slots = total_slots;
-      it = sh.map.emplace(s->key, std::move(fresh)).first;
-      inflight_blocks_.fetch_add(1, std::memory_order_relaxed);
+      it = inflight_add(sh, s->key, total_slots);
     }
     Inflight& ib = it->second;
     if (ib.total_slots != total_slots) continue;  // another call's block: fill-major would have thrown
@@ -673,12 +679,7 @@ bool Storage::insert_slot(const std::string& ns, const std::string& hash, uint64
     std::lock_guard<std::mutex> g(sh.mu);
     auto it = sh.map.find(key);
     if (it == sh.map.end()) {
-      Inflight fresh;
-      fresh.slots.assign(total_slots, nullptr);
-      fresh.remaining = total_slots;
-      fresh.total_slots = total_slots;
-      it = sh.map.emplace(key, std::move(fresh)).first;
-      inflight_blocks_.fetch_add(1, std::memory_order_relaxed);
+      it = inflight_add(sh, key, total_slots);
     }
     Inflight& ib = it->second;
     if (slot < ib.slots.size() && ib.slots[slot]) return false;
@@ -700,8 +701,7 @@ bool Storage::insert_slot(const std::string& ns, const std::string& hash, uint64
       sealed->slots = std::move(ib.slots);
       sealed->owners = std::move(ib.owners);
       sealed->footprint = ib.footprint;
-      sh.map.erase(it);
-      inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
+      inflight_remove(sh, it);
     }
   }
   if (sealed) {
@@ -782,8 +782,7 @@ uint64_t Storage::drop_stale_inflight() {
     for (auto it = sh.map.begin(); it != sh.map.end();) {
       if (now - it->second.created > max_age) {
         dropped.push_back(std::move(it->second));
-        it = sh.map.erase(it);
-        inflight_blocks_.fetch_sub(1, std::memory_order_relaxed);
+        it = inflight_remove(sh, it);
       } else {
         ++it;
       }

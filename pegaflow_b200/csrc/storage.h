@@ -270,7 +270,22 @@ class Storage {
   struct InflightShard {
     std::mutex mu;
     std::unordered_map<BlockKey, Inflight, BlockKeyHash> map;
+    // Entries per slot count, and a summary readable without the lock (0:
+    // no entries, the slot count all entries share, or ~0 when they differ),
+    // so that a call can tell that no entry here has a slot count other than
+    // its own without a lookup per hash or waiting for the lock.
+    std::unordered_map<uint64_t, uint32_t> totals;
+    std::atomic<uint64_t> sole_total{0};
+    void summarize() {
+      sole_total.store(totals.empty() ? 0 : totals.size() == 1 ? totals.begin()->first : ~0ull,
+                       std::memory_order_release);
+    }
   };
+  using InflightIt = std::unordered_map<BlockKey, Inflight, BlockKeyHash>::iterator;
+  // Add an empty entry for `key` / remove one, with the shard's lock held;
+  // both keep inflight_blocks_ and the shard's slot-count tally.
+  InflightIt inflight_add(InflightShard& sh, const BlockKey& key, uint64_t total_slots);
+  InflightIt inflight_remove(InflightShard& sh, InflightIt it);
   std::array<InflightShard, kInflightShards> inflight_;
   std::atomic<uint64_t> inflight_blocks_{0};  // entries over all shards
   static size_t shard_of(const BlockKey& k);
