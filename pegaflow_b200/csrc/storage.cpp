@@ -44,10 +44,12 @@ constexpr uint32_t kPoolMaxAllocs = 4000000;  // pinned_pool.rs:61
 
 size_t BlockKeyHash::operator()(const BlockKey& k) const { return static_cast<size_t>(fnv1a(k.ns, k.hash)); }
 
-size_t Storage::shard_of(const BlockKey& k) {
+size_t Storage::shard_of(const BlockKey& k) { return shard_of_hash(BlockKeyHash{}(k)); }
+
+size_t Storage::shard_of_hash(uint64_t h) {
   // The top bits of a multiplicative mix of the key's hash, so a shard's own
   // map (which buckets by the same hash) still spreads its keys.
-  return static_cast<size_t>((static_cast<uint64_t>(BlockKeyHash{}(k)) * 0x9E3779B97F4A7C15ull) >> 58);
+  return static_cast<size_t>((h * 0x9E3779B97F4A7C15ull) >> 58);
 }
 
 // ---------------------------------------------------------------------------
@@ -485,15 +487,29 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
   }
   std::vector<char> cached(n, 0);
   std::vector<BlockKey> keys;
+  std::vector<uint64_t> key_hash(n);
   keys.reserve(n);
-  for (size_t i = 0; i < n; ++i) keys.push_back(BlockKey{ns, hashes[i]});
+  for (size_t i = 0; i < n; ++i) {
+    keys.push_back(BlockKey{ns, hashes[i]});
+    key_hash[i] = BlockKeyHash{}(keys.back());
+  }
+  // A hash listed twice finds its block sealed by the first occurrence; only
+  // a list with a repeat needs the set of hashes sealed so far. Equal keys
+  // hash equally, so comparing the 64-bit hashes misses no repeat (a
+  // collision only turns the set on).
+  bool repeats = false;
+  {
+    std::vector<uint64_t> sorted(key_hash);
+    std::sort(sorted.begin(), sorted.end());
+    repeats = std::adjacent_find(sorted.begin(), sorted.end()) != sorted.end();
+  }
   {
     std::lock_guard<std::mutex> g(cache_mu_);
     for (size_t i = 0; i < n; ++i) cached[i] = index_.count(keys[i]) ? 1 : 0;
   }
   std::vector<std::vector<uint32_t>> by_shard(kInflightShards);  // positions, in list order
   for (size_t i = 0; i < n; ++i) {
-    if (!cached[i]) by_shard[shard_of(keys[i])].push_back(static_cast<uint32_t>(i));
+    if (!cached[i]) by_shard[shard_of_hash(key_hash[i])].push_back(static_cast<uint32_t>(i));
   }
   // An inflight block with another slot count makes fill-major throw part
   // way through its first fill; let it do exactly that. (A snapshot: such a
@@ -525,7 +541,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
   std::vector<Seal> seals;
   seals.reserve(n);
   std::unordered_set<std::string_view> sealed_here;  // a repeated hash finds its block sealed
-  sealed_here.reserve(n);
+  if (repeats) sealed_here.reserve(n);
   // One owner for the batches of every fill: each block this call touches
   // holds it once (instead of one reference per slot).
   SlotOwner owner;
@@ -550,7 +566,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
     InflightShard& sh = inflight_[sh_i];
     std::lock_guard<std::mutex> g(sh.mu);
     for (uint32_t i : by_shard[sh_i]) {
-      if (!sealed_here.empty() && sealed_here.count(hashes[i])) continue;
+      if (repeats && !sealed_here.empty() && sealed_here.count(hashes[i])) continue;
       const BlockKey& key = keys[i];
       auto it = sh.map.find(key);
       if (it == sh.map.end() && all_slots) {
@@ -561,7 +577,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
           sb->slots[f.slot] = &f.batch->blocks[i];
         }
         sb->owners.push_back(owner);
-        sealed_here.insert(hashes[i]);
+        if (repeats) sealed_here.insert(hashes[i]);
         seals.push_back({fills.size() - 1, i, key, std::move(sb)});
         continue;
       }
@@ -590,7 +606,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
           sb->owners = std::move(ib.owners);
           sb->footprint = ib.footprint;
           inflight_remove(sh, it);
-          sealed_here.insert(hashes[i]);
+          if (repeats) sealed_here.insert(hashes[i]);
           seals.push_back({f, i, key, std::move(sb)});
           break;
         }

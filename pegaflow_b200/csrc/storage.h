@@ -289,6 +289,7 @@ class Storage {
   std::array<InflightShard, kInflightShards> inflight_;
   std::atomic<uint64_t> inflight_blocks_{0};  // entries over all shards
   static size_t shard_of(const BlockKey& k);
+  static size_t shard_of_hash(uint64_t key_hash);  // shard_of from BlockKeyHash's value
   InflightShard& shard(const BlockKey& k) { return inflight_[shard_of(k)]; }
   std::mutex cache_mu_;
   LruList lru_;  // front = least recently used

@@ -187,6 +187,13 @@ def test_layer_wise_completion_words(cuda, oracle):
         assert s.wait_layer(li, timeout_s=60), li
     assert wait_state(s) == 1
     assert all(s.layer_ready(i) for i in range(len(names)))
+    # The load's phase timings: the first layer is ready within the task's
+    # time from queueing to completion.
+    p.e.wait_loads(0, 30.0)
+    m = p.e.metrics()
+    assert m["load_calls"] == 1 and m["load_transfer_ms"] > 0
+    assert 0 < m["load_first_layer_ms"] <= m["load_queue_ms"] + m["load_setup_ms"] + m["load_transfer_ms"] + 1e-3
+    assert m["load_lookup_ms"] >= 0 and m["load_ms"] >= m["load_transfer_ms"]
     p.m.batch_load("inst", 0, 0, names, dst, hs)
     p.check_caches()
 
