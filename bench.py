@@ -271,6 +271,57 @@ def executor_specs(tensors, src, dst, pool_ptr):
     return saves, loads, off
 
 
+def duplex_block(torch, ex, tensors, src, dst, payload: int, steps: int, device: int, serial_gbps: float) -> dict:
+    """Save and load at once on one GPU, same tensors and executor as the
+    serial step: the source blocks are saved into pool region A on one stream
+    (the executor's save lane) while blocks saved earlier are restored from
+    region B on another (its load lane), as when a prefill's offload overlaps
+    another request's restore. Source and destination ids are disjoint. The
+    destination blocks are zeroed and region A cleared after the warm-up, so
+    the checks see only what the timed steps moved."""
+    from pegaflow_b200 import PinnedBuffer
+
+    peak = duplex_peak(torch, device)
+    half = (payload + len(tensors) * 8192 + (1 << 20) + 4095) // 4096 * 4096
+    pool2 = PinnedBuffer(2 * half, write_combined=True)
+    saves_a, _, _ = executor_specs(tensors, src, dst, pool2.ptr)
+    saves_b, loads_b, _ = executor_specs(tensors, src, dst, pool2.ptr + half)
+    a, b = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ex.save(saves_b, stream=a.cuda_stream)  # region B now holds the source blocks
+    a.synchronize()
+
+    def one():
+        e0, e1, eb = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(a)
+        b.wait_event(e0)
+        ex.save(saves_a, stream=a.cuda_stream)
+        ex.load(loads_b, stream=b.cuda_stream)
+        eb.record(b)
+        a.wait_event(eb)
+        e1.record(a)
+        return e0, e1
+
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize(device)
+    scribble(torch, tensors, dst)
+    pool2.numpy()[:half] = 0
+    torch.cuda.synchronize(device)
+    evs = [one() for _ in range(steps)]
+    torch.cuda.synchronize(device)
+    ms = statistics.median(x.elapsed_time(y) for x, y in evs)
+    gbps = 2 * payload / (ms / 1e3) / 1e9
+    verified = restored(torch, tensors, src, dst) and pool_matches(torch, tensors, saves_a, pool2, src)
+    pool2.close()
+    return {"GBps": round(gbps, 3), "ms_per_step": round(ms, 3), "steps": steps,
+            "vs_serial": round(gbps / serial_gbps, 3) if serial_gbps else None,
+            "peak_duplex_GBps": peak, "frac_of_duplex_peak": round(gbps / peak, 3) if peak else None,
+            "verified": verified,
+            "how": "the same save and load as the serial step, on two streams at once (save lane: source "
+                   "blocks into pool region A; load lane: region B into the destination blocks); median "
+                   "device time per step; peak_duplex: a 1 GiB pinned D2H and a 1 GiB H2D at once"}
+
+
 def payload_bytes(tensors, n) -> int:
     from pegaflow_b200 import Layout
 
@@ -1554,6 +1605,11 @@ def main() -> int:
                   "load_setup_ms", "load_transfer_ms", "load_first_layer_ms")}
     eng.close()
 
+    # ---- save and load at once (one GPU) --------------------------------------
+    duplex = None
+    if world == 1 and not args.no_extra:
+        duplex = duplex_block(torch, ex, tensors, src, dst, payload, max(3, min(steps, 8)), local, value)
+
     # ---- the reference's copy strategy on the same GPU ------------------------
     ref = None
     if not args.no_refcopy:
@@ -1677,6 +1733,7 @@ def main() -> int:
             "host_cpus": (f"{len(cpus)} CPUs local to the GPU (NVML affinity)" if cpus else "unbound"),
             "copy_calls": st["copy_calls"],
             "other_order": other,
+            "duplex": duplex,
             "configs1": cfg1,
             "configs0": cfg0,
             "configs4": cfg4,
