@@ -560,7 +560,11 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
     const uint64_t tp = total_slots / fills.size();
     start = static_cast<size_t>((fills.front().slot % tp) * kInflightShards / tp);
   }
-  for (size_t step = 0; step < kInflightShards; ++step) {
+  // A block created with another slot count after the check above stops the
+  // pass (fill-major would throw there); what sealed before it is still
+  // published below, then the call throws.
+  std::string mismatch;
+  for (size_t step = 0; step < kInflightShards && mismatch.empty(); ++step) {
     const size_t sh_i = (start + step) % kInflightShards;
     if (by_shard[sh_i].empty()) continue;
     InflightShard& sh = inflight_[sh_i];
@@ -586,9 +590,9 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
       }
       Inflight& ib = it->second;
       if (ib.total_slots != total_slots) {
-        // Created by a call with another slot count after the check above.
-        throw storage_error("slot count mismatch: expected " + std::to_string(ib.total_slots) + ", got " +
-                            std::to_string(total_slots));
+        mismatch = "slot count mismatch: expected " + std::to_string(ib.total_slots) + ", got " +
+                   std::to_string(total_slots);
+        break;
       }
       bool owned = false;
       for (size_t f = 0; f < fills.size(); ++f) {
@@ -613,7 +617,10 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
       }
     }
   }
-  if (seals.empty()) return;
+  if (seals.empty()) {
+    if (!mismatch.empty()) throw storage_error(mismatch);
+    return;
+  }
   auto fill_major = [](const Seal& a, const Seal& b) { return a.fill != b.fill ? a.fill < b.fill : a.index < b.index; };
   if (!std::is_sorted(seals.begin(), seals.end(), fill_major)) std::sort(seals.begin(), seals.end(), fill_major);
   SealListener listener;
@@ -662,6 +669,7 @@ void Storage::insert_slots_multi(const std::string& ns, const std::vector<std::s
       --ib.remaining;
     }
   }
+  if (!mismatch.empty()) throw storage_error(mismatch);
 }
 
 bool Storage::cache_insert_locked(const BlockKey& key, SealedBlockPtr block) {
