@@ -202,9 +202,10 @@ std::shared_ptr<PoolAllocation> Storage::allocate(uint64_t size, size_t pool) {
   // saves reclaim at once, another thread may hold the last evicted blocks
   // (taken from the LRU list, not yet dropped), so this thread finds nothing
   // to evict although their memory is about to come back. It waits for those
-  // drops and tries again, a bounded number of times.
+  // drops and tries again, at most kMaxDropWaits times within one second.
   pool = std::min(pool, pools_.size() - 1);
   PinnedPool& p = *pools_[pool];
+  std::chrono::steady_clock::time_point deadline{};
   for (int waits = 0;;) {
     if (auto a = p.allocate(size)) return a;
     uint64_t freed = 0;
@@ -213,7 +214,8 @@ std::shared_ptr<PoolAllocation> Storage::allocate(uint64_t size, size_t pool) {
     if (p.largest_free() >= size) {
       if (auto a = p.allocate(size)) return a;
     }
-    if (waits < kMaxDropWaits && wait_for_drops(p, size)) {
+    if (waits == 0) deadline = std::chrono::steady_clock::now() + std::chrono::seconds(1);
+    if (waits < kMaxDropWaits && wait_for_drops(p, size, deadline)) {
       ++waits;
       continue;
     }
@@ -222,12 +224,11 @@ std::shared_ptr<PoolAllocation> Storage::allocate(uint64_t size, size_t pool) {
   }
 }
 
-bool Storage::wait_for_drops(PinnedPool& p, uint64_t size) {
-  // Drops take microseconds to milliseconds; give up after one second.
+bool Storage::wait_for_drops(PinnedPool& p, uint64_t size, std::chrono::steady_clock::time_point deadline) {
+  // Drops take microseconds to milliseconds.
   if (dropping_.load(std::memory_order_acquire) == 0) return false;
-  const auto limit = std::chrono::steady_clock::now() + std::chrono::seconds(1);
   while (dropping_.load(std::memory_order_acquire) != 0 && p.largest_free() < size) {
-    if (std::chrono::steady_clock::now() > limit) return false;
+    if (std::chrono::steady_clock::now() > deadline) return false;
     std::this_thread::yield();
   }
   return true;

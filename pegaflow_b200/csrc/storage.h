@@ -236,11 +236,11 @@ class Storage {
   // taking only blocks that hold memory in `pool` when there are several.
   std::vector<SealedBlockPtr> evict_lru(uint64_t max_blocks, uint64_t bytes, size_t pool);
   // Drops what evict_lru returned (releasing pool memory) and ends its
-  // dropping_ count. wait_for_drops waits (at most 1 s) until no thread holds
-  // evicted blocks or `p` has room for `size`; false when no thread held any
-  // or the wait ran out.
+  // dropping_ count. wait_for_drops waits (until `deadline`) until no thread
+  // holds evicted blocks or `p` has room for `size`; false when no thread
+  // held any or the deadline passed.
   void drop_evicted(std::vector<SealedBlockPtr>& evicted);
-  bool wait_for_drops(PinnedPool& p, uint64_t size);
+  bool wait_for_drops(PinnedPool& p, uint64_t size, std::chrono::steady_clock::time_point deadline);
   std::atomic<int> dropping_{0};  // evict_lru results not yet dropped
   bool holds_memory_in(const SealedBlock& b, size_t pool) const;
   void pre_evict_loop();
