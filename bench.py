@@ -739,7 +739,8 @@ def run_duplex(args) -> None:
     saves, _, off = executor_specs(tensors, save_ids, save_ids, pool.ptr)
     _, loads, _ = executor_specs(tensors, load_ids, load_ids, pool.ptr + off)
     ex = Executor(0, save_mode=args.save_mode, load_mode=args.load_mode, staging_chunk_bytes=args.chunk_mib << 20,
-                  staging_slots=args.slots, copy_streams=args.copy_streams, first_chunk_bytes=args.first_chunk_mib << 20)
+                  staging_slots=args.slots, copy_streams=args.copy_streams, first_chunk_bytes=args.first_chunk_mib << 20,
+                  copy_kernel=args.copy_kernel)
     a, b = torch.cuda.Stream(), torch.cuda.Stream()
 
     def timed(duplex):
@@ -776,7 +777,8 @@ def run_duplex(args) -> None:
     eng = PegaEngine(3 * payload + (512 << 20), enable_lfu_admission=False,
                      executor=dict(save_mode=args.save_mode, load_mode=args.load_mode,
                                    staging_chunk_bytes=args.chunk_mib << 20, staging_slots=args.slots,
-                                   copy_streams=args.copy_streams, first_chunk_bytes=args.first_chunk_mib << 20))
+                                   copy_streams=args.copy_streams, first_chunk_bytes=args.first_chunk_mib << 20,
+                                   copy_kernel=args.copy_kernel))
     names = [f"model.layers.{i}.self_attn" for i in range(len(tensors))]
     for nm, t in zip(names, tensors):
         lay = Layout.from_tensor(t)
