@@ -744,19 +744,22 @@ def run_duplex(args) -> None:
     a, b = torch.cuda.Stream(), torch.cuda.Stream()
 
     def timed(duplex):
-        e0, e1, eb = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0, e1, ea, eb = (torch.cuda.Event(enable_timing=True) for _ in range(4))
         e0.record(a)
         if duplex:
             b.wait_event(e0)
             ex.save(saves, stream=a.cuda_stream)
+            ea.record(a)
             ex.load(loads, stream=b.cuda_stream)
             eb.record(b)
             a.wait_event(eb)
         else:
             ex.save(saves, stream=a.cuda_stream)
+            ea.record(a)
             ex.load(loads, stream=a.cuda_stream)
+            eb.record(a)
         e1.record(a)
-        return e0, e1
+        return e0, e1, ea, eb
 
     for _ in range(args.warmup):
         timed(True)
@@ -768,9 +771,14 @@ def run_duplex(args) -> None:
     for mode in ("serial", "duplex"):
         evs = [timed(mode == "duplex") for _ in range(args.steps)]
         torch.cuda.synchronize()
-        ms = [x.elapsed_time(y) for x, y in evs]
+        ms = [x.elapsed_time(y) for x, y, _, _ in evs]
+        # Each lane's end from the step's start (serial: the load ends after the save).
+        save_end = [x.elapsed_time(s) for x, _, s, _ in evs]
+        load_end = [x.elapsed_time(l) for x, _, _, l in evs]
         res[mode] = {"ms_per_step": round(statistics.median(ms), 3),
-                     "GBps": round(2 * payload / (statistics.median(ms) / 1e3) / 1e9, 2)}
+                     "GBps": round(2 * payload / (statistics.median(ms) / 1e3) / 1e9, 2),
+                     "save_end_ms": round(statistics.median(save_end), 3),
+                     "load_end_ms": round(statistics.median(load_end), 3)}
     clocks = sampler.stop()
 
     # Engine: this step's save runs while the previous step's blocks load.
