@@ -72,10 +72,11 @@ struct LayerBlock {
   uint64_t size;   // block_size_bytes (memory_footprint)
 };
 // The blocks one save call wrote for one layer. They share the call's K (and
-// V) pool allocations, which go back to the pool when the last block of the
-// batch is dropped: the lifetime the reference gets from one
-// Arc<PinnedAllocation> per block (storage.rs:249-261), with one heap object
-// per (call, layer) instead of one per block.
+// V) pool allocations, which go back to the pool when no sealed or inflight
+// block holds the batch any more (directly, or through the owner group of
+// the call that wrote it; see SlotOwner): the lifetime the reference gets
+// from one Arc<PinnedAllocation> per block (storage.rs:249-261), with one
+// heap object per (call, layer) instead of one per block.
 struct LayerBlockBatch {
   std::vector<LayerBlock> blocks;
   std::shared_ptr<PoolAllocation> k_alloc;
